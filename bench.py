@@ -1,0 +1,384 @@
+#!/usr/bin/env python
+"""Benchmark of the nested GDN-2 forward hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config config1] [--path auto|simt|tc]
+
+One "step" is one forward of the op over one batch of synthetic input of the
+named configuration (default ``config1``: B=8, T=8192, H=16, K=V=128, L=3
+firing every 1/4/16 chunks, m=64, bf16 inputs, fp32 state). Under torchrun
+(N > 1) every rank runs the same per-GPU workload on its own seeded batch
+(weak scaling; the path shards by (batch, head) and needs no collective);
+times are CUDA-event times, max over ranks.
+
+Rank 0 prints one JSON line. ``value`` is whole-job tokens/s with inputs
+resident in HBM; ``e2e`` is the same metric through the public API with
+host (pinned) inputs copied in and o / final state copied out every step.
+``roofline`` relates the forward to HBM bandwidth (the bound of this path),
+``cpu_baseline`` is the CPU oracle (numpy restatement of the reference's
+naive.py) timed on a bounded sample on this host.
+
+``--impl reference`` times the reference's CPU algorithm (the oracle port;
+the reference itself is Python and cannot travel to the GPU host) on rank 0
+only and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "nested-GDN layer fwd tokens/s/GPU at 1/2/4/8 B200; % tensor-pipe peak"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", default="config1")
+    ap.add_argument("--path", choices=("auto", "simt", "tc"), default="auto")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def workload(cfg_name):
+    from nested_recurrent_memory_b200.synthetic import CONFIGS
+    B, T, H, K, V, L, m, firing, dtype = CONFIGS[cfg_name]
+    return dict(B=B, T=T, H=H, K=K, V=V, L=L, m=m, firing=tuple(firing), dtype=dtype)
+
+
+def alg_counts(w):
+    """Algorithmic flops and bytes per token per head (counting rules: tile
+    triangles dense, triangular inverse excluded, intermediate states not
+    counted)."""
+    C, K, V, L, m = 64, w["K"], w["V"], w["L"], w["m"]
+    s = 2 if str(w["dtype"]).endswith(("bfloat16", "float16")) else 4
+    flop = (4 * C * C * K + 2 * C * C * (K + V) + 2 * C * C * V + 6 * C * K * V) / C
+    for lvl in range(1, L):
+        f = w["firing"][lvl]
+        flop += 2 * K * V + (8 * m * K * V + 2 * m * V * (2 * K + V)) / (f * C)
+    nbytes = s * (L * K + K + V + K + K + V + L + V)
+    nbytes += L * K * V * 4 / w["T"]
+    nbytes += (L - 1) * (m * K + 3 * K * V + V * V) * s / w["T"]
+    return flop, nbytes
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(self.REASONS, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle on a bounded sample
+# ---------------------------------------------------------------------------
+
+def cpu_sample_run(w, heads, seed=0):
+    """One bounded sample: one batch row, ``heads`` heads, the full T, in
+    fp32 through the oracle. Returns (seconds, token-heads processed)."""
+    import numpy as np
+    import torch
+
+    import oracle  # CPU baseline leg only
+    from nested_recurrent_memory_b200.synthetic import config_inputs
+
+    inp = config_inputs(1, w["T"], heads, w["K"], w["V"], w["L"], w["m"], w["firing"],
+                        dtype=torch.float32, seed=seed)
+    L = inp.pop("L")
+    a = {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in inp.items()}
+    t0 = time.perf_counter()
+    oracle.chunk_forward(**a, L=L, output_final_state=True, dtype=np.float32)
+    return time.perf_counter() - t0, w["T"] * heads
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference(args, w):
+    """--impl reference: the CPU algorithm on rank 0; other ranks exit."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    heads = 4
+    for _ in range(args.warmup):
+        cpu_sample_run(w, heads)
+    secs = []
+    for i in range(args.steps):
+        s, th = cpu_sample_run(w, heads, seed=i)
+        secs.append(s)
+    total = sum(secs)
+    # token-heads/s divided by H: tokens of the configuration per second
+    value = args.steps * w["T"] * heads / w["H"] / total
+    sample = (f"per step: 1 of {w['B']} batch rows, {heads} of {w['H']} heads, T={w['T']}, "
+              "fp32 numpy oracle (restated reference naive_chunk_nested_gdn2)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args, w),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, w):
+    return {
+        "workload": (f"{args.config}: B={w['B']} per GPU, T={w['T']}, H={w['H']}, "
+                     f"K=V={w['K']}, L={w['L']} firing {'/'.join(map(str, w['firing']))} chunks, "
+                     f"m={w['m']}, C=64, {str(w['dtype']).replace('torch.', '')} inputs, fp32 state"),
+        "global_batch": w["B"] * args.gpus, "seq_len": w["T"], "heads": w["H"],
+        "parallelism": f"(batch, head) sharding, {args.gpus} GPU(s), no collective",
+        "l2": "inputs larger than L2 (no flush needed)",
+    }
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, w):
+    import torch
+    import torch.distributed as dist
+
+    from nested_recurrent_memory_b200 import FwdCall, chunk_nested_gdn2
+    from nested_recurrent_memory_b200.synthetic import config_inputs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    inp = config_inputs(w["B"], w["T"], w["H"], w["K"], w["V"], w["L"], w["m"], w["firing"],
+                        dtype=w["dtype"], seed=1000 + rank, device=dev, gen_device=dev)
+    L = inp.pop("L")
+    call = FwdCall(**inp, L=L, path=args.path)
+    launches_per_step = call.num_launches
+
+    for _ in range(args.warmup):
+        call.launch()
+    barrier()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = vis.split(",")[local] if vis else str(local)
+    clocks = ClockSampler(gpu_index)
+    clocks.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    for _ in range(args.steps):
+        call.launch()
+    end.record()
+    barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    tokens_per_step = w["B"] * w["T"] * world
+    value = tokens_per_step / (ms_step / 1e3)
+
+    # Per-stage timing on the launching stream (stage 1 = prep, 2 = scan).
+    stage_ms = {1: 0.0, 2: 0.0}
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(args.steps):
+        evs[0].record()
+        call.launch(1)
+        evs[1].record()
+        call.launch(2)
+        evs[2].record()
+        torch.cuda.synchronize()
+        stage_ms[1] += evs[0].elapsed_time(evs[1])
+        stage_ms[2] += evs[1].elapsed_time(evs[2])
+    stage_ms = {k: v / args.steps for k, v in stage_ms.items()}
+
+    # e2e through the public API with pinned host buffers.
+    e2e = None
+    if not args.no_e2e:
+        host = {k: (v.cpu().pin_memory() if torch.is_tensor(v) and v.is_cuda else v)
+                for k, v in inp.items()}
+        dev_bufs = {k: (torch.empty_like(v, device=dev) if torch.is_tensor(v) and v.is_pinned() else v)
+                    for k, v in host.items()}
+        h2d = sum(v.numel() * v.element_size() for v in host.values()
+                  if torch.is_tensor(v) and v.is_pinned())
+        o_host = torch.empty(call.o.shape, dtype=call.o.dtype).pin_memory()
+        s_host = torch.empty(call.final.shape, dtype=call.final.dtype).pin_memory()
+        d2h = o_host.numel() * o_host.element_size() + s_host.numel() * s_host.element_size()
+
+        def e2e_step():
+            for k, v in host.items():
+                if torch.is_tensor(v) and v.is_pinned():
+                    dev_bufs[k].copy_(v, non_blocking=True)
+            o, s = chunk_nested_gdn2(**dev_bufs, L=L, output_final_state=True)
+            o_host.copy_(o, non_blocking=True)
+            s_host.copy_(s, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": tokens_per_step / (float(te.item()) / args.steps / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+    peaks, peak_src = load_peaks()
+    flop_th, bytes_th = alg_counts(w)
+    token_heads = w["B"] * w["T"] * w["H"]
+    alg_bytes = bytes_th * token_heads
+    alg_flops = flop_th * token_heads
+    achieved_gbs = alg_bytes / (ms_step / 1e3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        tj = json.loads(tfile.read_text())
+        key = f"{args.config}:{call.path}"
+        if key in tj:
+            traffic = tj[key]["dram_bytes_per_token_head"] * token_heads
+    dominant = max(stage_ms, key=stage_ms.get)
+    roofline = {
+        "bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
+        "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
+        "scope": "whole forward (prep + scan); algorithmic bytes = inputs + o + final state + weights",
+        "alg_bytes_per_launch": alg_bytes,
+        "tensor_tflops": alg_flops / (ms_step / 1e3) / 1e12,
+        "tensor_frac_of_bf16_peak": alg_flops / (ms_step / 1e3) / 1e12 / peaks["bf16_tflops"],
+        "kernels": {"prep_ms": stage_ms[1], "scan_ms": stage_ms[2],
+                    "dominant": "prep" if dominant == 1 else "scan",
+                    "dominant_share": stage_ms[dominant] / max(sum(stage_ms.values()), 1e-9)},
+    }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        heads = 16
+        secs, th = cpu_sample_run(w, heads)
+        cpu = {"value": th / w["H"] / secs, "unit": "tokens/s", "cores": cpu_threads(),
+               "kind": "port",
+               "sample": (f"1 of {w['B']} batch rows, {heads} of {w['H']} heads, T={w['T']} "
+                          f"({secs:.1f} s), fp32 numpy oracle (restated reference "
+                          "naive_chunk_nested_gdn2)")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if "bfloat16" in str(w["dtype"]) else str(w["dtype"]).replace("torch.", ""),
+            "data": "synthetic (seeded; BASELINE config recipe)",
+            "config": config_dict(args, w) | {"kernel_path": call.path},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    w = workload(args.config)
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

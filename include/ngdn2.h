@@ -1,0 +1,179 @@
+/*
+ * ngdn2.h -- C ABI of the B200-native nested Gated DeltaNet (nested GDN-2)
+ * forward hot path.
+ *
+ * Every entry point takes plain pointers, sizes and strides, returns 0 or a
+ * negative NGDN2_ERR_* code, never throws, and never allocates, frees or
+ * retains device memory: the caller passes every input, output and
+ * workspace buffer. Launches go on the caller's CUDA stream (a cudaStream_t
+ * passed as void*; NULL is the legacy default stream). No entry point
+ * synchronises the stream.
+ *
+ * The entry points replace these functions of the reference project
+ * (awehrs/nested_recurrent_memory, paths within that project):
+ *
+ *   ngdn2_fwd            nested_gdn2/ops/chunk.py:159-304  chunk_nested_gdn2_fwd
+ *                        (and the forward of chunk_nested_gdn2, chunk.py:722-766,
+ *                        whose Function.forward calls it, chunk.py:571-648)
+ *   ngdn2_update_state   nested_gdn2/ops/update_fwd.py:131-204  update_state
+ *
+ * Layouts are the reference's (chunk.py:184-217): per-token tensors
+ * [B, T, H, ...], states [B, H, L, K, V] float32, parameters
+ * [L-1, H, ...] contiguous.
+ */
+#ifndef NGDN2_H_
+#define NGDN2_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NGDN2_API __attribute__((visibility("default")))
+#else
+#define NGDN2_API
+#endif
+
+#define NGDN2_ABI_VERSION 1
+#define NGDN2_MAX_LEVELS 8
+#define NGDN2_CHUNK 64
+
+/* Element types of the floating-point tensors. */
+enum {
+  NGDN2_F32 = 0,
+  NGDN2_BF16 = 1,
+  NGDN2_F16 = 2
+};
+
+/* Promotion arms, the keys of the reference's PROBES registry
+ * (nested_gdn2/ops/probe.py:139-142). */
+enum {
+  NGDN2_PROMOTION_LEARNED = 0, /* probe.py:69-102 */
+  NGDN2_PROMOTION_MERGE = 1    /* probe.py:105-136 */
+};
+
+/* Kernel families. AUTO picks the tensor-core path when it supports the
+ * shape and dtype, else the CUDA-core fp32 path. */
+enum {
+  NGDN2_PATH_AUTO = 0,
+  NGDN2_PATH_SIMT = 1,  /* CUDA-core kernels, fp32 arithmetic throughout */
+  NGDN2_PATH_TC = 2     /* tcgen05 tensor-core kernels, bf16/fp16 operands, fp32 accumulate */
+};
+
+/* Return codes. The Python host layer maps each to the reference's
+ * ValueError message. */
+enum {
+  NGDN2_OK = 0,
+  NGDN2_ERR_CHUNK_SIZE = -1,    /* chunk.py:230-231 "chunk_size must be 64" */
+  NGDN2_ERR_N_POW2 = -2,        /* update_fwd.py:162-163 "power of two >= 16" */
+  NGDN2_ERR_BLOCK_V = -3,       /* update_fwd.py:164-165 "block_v must be ..." */
+  NGDN2_ERR_DIVISIBLE = -4,     /* update_fwd.py:166-167 "must be divisible" */
+  NGDN2_ERR_UNIT_STRIDE = -5,   /* update_fwd.py:168-169 "unit-stride" */
+  NGDN2_ERR_INCONSISTENT = -6,  /* update_fwd.py:170-171 "inconsistent" */
+  NGDN2_ERR_SHAPE = -7,         /* a size out of the supported range */
+  NGDN2_ERR_DTYPE = -8,         /* unknown dtype code */
+  NGDN2_ERR_NULL = -9,          /* a required pointer is NULL */
+  NGDN2_ERR_WORKSPACE = -10,    /* workspace smaller than ngdn2_fwd_workspace_size */
+  NGDN2_ERR_UNSUPPORTED = -11,  /* requested path cannot run this shape/dtype */
+  NGDN2_ERR_CUDA = -12,         /* a CUDA runtime call failed */
+  NGDN2_ERR_ABI = -13,          /* abi_version mismatch */
+  NGDN2_ERR_FIRING = -14        /* firing intervals not nested or not >= 1 */
+};
+
+/* Arguments of ngdn2_fwd. */
+typedef struct ngdn2_fwd_args {
+  int32_t abi_version;  /* NGDN2_ABI_VERSION */
+  int32_t path;         /* NGDN2_PATH_* */
+  int32_t B, T, H, K, V, L;
+  int32_t chunk_size;   /* must be 64 (chunk.py:230-231) */
+  int32_t promotion;    /* NGDN2_PROMOTION_* */
+  int32_t dtype;        /* element type of the output o */
+  int32_t param_dtype;  /* of query_banks and the four projections */
+  float scale;          /* read scale; the reference default is K^-1/2 */
+  int32_t n_max;        /* query_banks.shape[2] (N_MAX) */
+  int32_t n_queries[NGDN2_MAX_LEVELS]; /* [l-1] = pairs for level l >= 1 */
+  int32_t firing[NGDN2_MAX_LEVELS];    /* [l] = interval of level l in chunks; [0] == 1 */
+
+  /* Per-token inputs: pointer, element type (NGDN2_F32/BF16/F16) and
+   * element strides. Any strides are accepted, including 0 (broadcast); the
+   * tensor-core path additionally wants unit-stride last dimensions. */
+  const void* q;   int32_t q_dtype;   int64_t q_stride[5];   /* [B, T, H, L, K] */
+  const void* k;   int32_t k_dtype;   int64_t k_stride[4];   /* [B, T, H, K] */
+  const void* v;   int32_t v_dtype;   int64_t v_stride[4];   /* [B, T, H, V] */
+  const void* g;   int32_t g_dtype;   int64_t g_stride[4];   /* [B, T, H, K] level-0 log-decay */
+  const void* b;   int32_t b_dtype;   int64_t b_stride[4];   /* [B, T, H, K] level-0 erase gate */
+  const void* w;   int32_t w_dtype;   int64_t w_stride[4];   /* [B, T, H, V] level-0 write gate */
+  const void* mix; int32_t mix_dtype; int64_t mix_stride[4]; /* [B, T, H, L] read-mix weights */
+
+  const void* query_banks;      /* [L-1, H, n_max, K] contiguous */
+  const void* key_projections;  /* [L-1, H, K, V] */
+  const void* b_projections;    /* [L-1, H, V, K] */
+  const void* w_projections;    /* [L-1, H, V, V] */
+  const void* g_projections;    /* [L-1, H, V, K] */
+
+  const float* initial_state;   /* [B, H, L, K, V] or NULL for zeros */
+  void* o;                      /* [B, T, H, V] contiguous, element type dtype */
+  float* final_state;           /* [B, H, L, K, V] contiguous, always written */
+
+  void* workspace;              /* device scratch, >= ngdn2_fwd_workspace_size */
+  size_t workspace_bytes;
+  int32_t* status;              /* optional device word; kernels OR in NGDN2_STATUS_* */
+} ngdn2_fwd_args;
+
+/* Device status bits (written to ngdn2_fwd_args.status when non-NULL). */
+enum {
+  NGDN2_STATUS_WAIT_TIMEOUT = 1  /* a bounded pipeline wait gave up */
+};
+
+/* Arguments of ngdn2_update_state (update_fwd.py:131-204). */
+typedef struct ngdn2_update_args {
+  int32_t abi_version;
+  int32_t B, NF, NG, H, K, V, N;
+  int32_t block_v;      /* columns per program in the reference; validated the same way */
+  int32_t dtype;        /* of keys, values, b, w */
+  int32_t g_dtype;      /* of g */
+  const void* keys;   int64_t keys_stride[5];   /* [B, NF, H, N, K] element strides; the K stride must be 1 */
+  const void* values;                           /* [B, NF, H, N, V] contiguous */
+  const void* g;                                /* [B, NF, H, K] contiguous */
+  const void* b;                                /* [B, NF, H, N, K] contiguous */
+  const void* w;                                /* [B, NF, H, N, V] contiguous */
+  const float* initial_state;                   /* [B, H, K, V] or NULL */
+  float* states;                                /* [B, NG, H, K, V] out */
+  float* final_state;                           /* [B, H, K, V] out */
+} ngdn2_update_args;
+
+NGDN2_API int ngdn2_abi_version(void);
+/* sizeof the two argument structs, so bindings can check their layout. */
+NGDN2_API size_t ngdn2_sizeof_fwd_args(void);
+NGDN2_API size_t ngdn2_sizeof_update_args(void);
+NGDN2_API const char* ngdn2_error_string(int code);
+
+/* Validates *args and returns the workspace ngdn2_fwd needs, in bytes. */
+NGDN2_API int ngdn2_fwd_workspace_size(const ngdn2_fwd_args* args, size_t* bytes);
+
+/* Which path ngdn2_fwd would run (NGDN2_PATH_SIMT or NGDN2_PATH_TC), or an
+ * error code. */
+NGDN2_API int ngdn2_fwd_select_path(const ngdn2_fwd_args* args);
+
+/* The forward: o and final_state from the inputs. */
+NGDN2_API int ngdn2_fwd(const ngdn2_fwd_args* args, void* stream);
+
+/* One stage of the forward, for profiling: stage 1 launches the
+ * chunk-parallel preparation kernels, stage 2 the sequential scan (which
+ * reads what stage 1 left in the same workspace); stage 0 is ngdn2_fwd. */
+NGDN2_API int ngdn2_fwd_stage(const ngdn2_fwd_args* args, int stage, void* stream);
+
+/* Number of kernel launches ngdn2_fwd makes for these arguments. */
+NGDN2_API int ngdn2_fwd_num_launches(const ngdn2_fwd_args* args);
+
+/* The promotion write scan on its own. */
+NGDN2_API int ngdn2_update_state(const ngdn2_update_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NGDN2_H_ */

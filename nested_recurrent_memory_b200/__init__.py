@@ -1,0 +1,20 @@
+"""B200-native nested Gated DeltaNet (nested GDN-2) forward hot path.
+
+A drop-in for the reference's ``nested_gdn2.ops`` forward ops
+(``chunk_nested_gdn2``, ``chunk_nested_gdn2_fwd``, ``update_state``),
+computed by hand-written sm_100a CUDA kernels behind the C ABI in
+``include/ngdn2.h``.
+"""
+
+from .ops import (  # noqa: F401
+    FwdCall,
+    chunk_nested_gdn2,
+    chunk_nested_gdn2_fwd,
+    fwd_workspace_bytes,
+    last_path,
+    n_firings,
+    n_groups,
+    update_state,
+)
+
+__version__ = "0.1.0"

@@ -1,0 +1,118 @@
+// Shared device helpers for the nested GDN-2 kernels: element loads with
+// conversion to fp32, stores from fp32, a block-wide fp32 GEMM used by the
+// CUDA-core path, and the math of the promotion gates.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ngdn2.h"
+
+namespace ngdn2 {
+
+// ---------------------------------------------------------------------------
+// Element conversion
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float load_elem(const void* p, int64_t i, int dtype) {
+  switch (dtype) {
+    case NGDN2_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    case NGDN2_F16: return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    default: return reinterpret_cast<const float*>(p)[i];
+  }
+}
+
+__device__ __forceinline__ void store_elem(void* p, int64_t i, float x, int dtype) {
+  switch (dtype) {
+    case NGDN2_BF16: reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x); break;
+    case NGDN2_F16: reinterpret_cast<__half*>(p)[i] = __float2half_rn(x); break;
+    default: reinterpret_cast<float*>(p)[i] = x; break;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Gate activations of the promotion probe (nested_gdn2/ops/probe.py:34-66)
+// ---------------------------------------------------------------------------
+
+constexpr float kBLogitInit = -4.0f;  // probe.py:28
+constexpr float kWLogitInit = 0.0f;   // probe.py:29
+constexpr float kGLogitInit = -4.0f;  // probe.py:31
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// torch.nn.functional.softplus with beta=1, threshold=20.
+__device__ __forceinline__ float softplusf_(float x) {
+  return x > 20.0f ? x : log1pf(expf(x));
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide fp32 GEMM on CUDA cores
+//
+// For m < M, n < N: epi(m, n, sum_k la(m, k) * lb(k, n)).
+// ``la`` and ``lb`` are element loaders (so strides, transposes, dtype
+// conversion and elementwise pre-products are free); operands are staged
+// through shared memory in 64x16 and 16x64 tiles and each thread owns a 4x4
+// block of outputs. The block must have exactly kGemmThreads threads and
+// every thread must call it (it synchronises). M and N are arbitrary; Kd
+// must be a multiple of 16. ``smem`` holds kGemmSmemFloats floats.
+// ---------------------------------------------------------------------------
+
+constexpr int kGemmThreads = 256;
+constexpr int kGemmLd = 65;
+constexpr int kGemmSmemFloats = 2 * 16 * kGemmLd;
+
+template <class LA, class LB, class Epi>
+__device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi epi) {
+  float* As = smem;                 // [16][65], k-major
+  float* Bs = smem + 16 * kGemmLd;  // [16][65]
+  const int tid = threadIdx.x;
+  const int tm = (tid / 16) * 4;
+  const int tn = (tid % 16) * 4;
+  for (int m0 = 0; m0 < M; m0 += 64) {
+    for (int n0 = 0; n0 < N; n0 += 64) {
+      float acc[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+      for (int k0 = 0; k0 < Kd; k0 += 16) {
+        for (int e = tid; e < 64 * 16; e += kGemmThreads) {
+          int mm = e / 16, kk = e % 16;
+          int gm = m0 + mm;
+          As[kk * kGemmLd + mm] = gm < M ? la(gm, k0 + kk) : 0.f;
+        }
+        for (int e = tid; e < 64 * 16; e += kGemmThreads) {
+          int kk = e / 64, nn = e % 64;
+          int gn = n0 + nn;
+          Bs[kk * kGemmLd + nn] = gn < N ? lb(k0 + kk, gn) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          float a[4], bb[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + i];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + j];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+        }
+        __syncthreads();
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int gm = m0 + tm + i, gn = n0 + tn + j;
+          if (gm < M && gn < N) epi(gm, gn, acc[i][j]);
+        }
+      __syncthreads();
+    }
+  }
+}
+
+}  // namespace ngdn2

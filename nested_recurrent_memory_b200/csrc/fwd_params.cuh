@@ -1,0 +1,131 @@
+// Host/device description of one forward call: shapes, schedule, tensor
+// views and the workspace layout shared by the CUDA-core and tensor-core
+// kernel families.
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace ngdn2 {
+
+// Element (b, t, h, d) of a per-token tensor, any strides.
+struct TokView {
+  const void* p;
+  int dt;
+  int64_t sb, st, sh, sd;
+  __device__ __forceinline__ int64_t off(int b, int t, int h, int d) const {
+    return b * sb + t * st + h * sh + d * sd;
+  }
+  __device__ __forceinline__ float at(int b, int t, int h, int d) const {
+    return load_elem(p, off(b, t, h, d), dt);
+  }
+};
+
+// Element (b, t, h, l, d) of q [B, T, H, L, K].
+struct QView {
+  const void* p;
+  int dt;
+  int64_t sb, st, sh, sl, sd;
+  __device__ __forceinline__ int64_t off(int b, int t, int h, int l, int d) const {
+    return b * sb + t * st + h * sh + l * sl + d * sd;
+  }
+  __device__ __forceinline__ float at(int b, int t, int h, int l, int d) const {
+    return load_elem(p, off(b, t, h, l, d), dt);
+  }
+};
+
+constexpr int kC = NGDN2_CHUNK;  // tokens per chunk
+
+__host__ __device__ inline int64_t align_floats(int64_t n) { return (n + 63) & ~int64_t(63); }
+
+// Per-chunk record written by the prep kernels and read by the scans, fp32.
+// All offsets in floats from the start of the record.
+struct ChunkRecord {
+  int64_t W, U, A, Q, Kt, eg, size;
+  __host__ __device__ static ChunkRecord make(int K, int V, int L) {
+    ChunkRecord r;
+    r.W = 0;                       // [64, K]  (I + A_kk)^-1 (k * b * e^G)
+    r.U = r.W + kC * K;            // [64, V]  (I + A_kk)^-1 (w * v)
+    r.A = r.U + kC * V;            // [64, 64] mix0 * scale * A_qk, causal
+    r.Q = r.A + kC * kC;           // [L, 64, K] read queries, mix and scale folded
+    r.Kt = r.Q + int64_t(L) * kC * K;  // [64, K] k * e^(G_last - G)
+    r.eg = r.Kt + kC * K;          // [K] e^(G_last)
+    r.size = align_floats(r.eg + K);
+    return r;
+  }
+};
+
+// Parameters converted to fp32, [L-1, H, ...] each.
+struct ParamLayout {
+  int64_t qb, kp, bp, wp, gp, size;
+  __host__ __device__ static ParamLayout make(int L, int H, int n_max, int K, int V) {
+    ParamLayout p;
+    int64_t n = int64_t(L > 1 ? L - 1 : 0) * H;
+    p.qb = 0;
+    p.kp = align_floats(p.qb + n * n_max * K);
+    p.bp = align_floats(p.kp + n * K * V);
+    p.wp = align_floats(p.bp + n * V * K);
+    p.gp = align_floats(p.wp + n * V * V);
+    p.size = align_floats(p.gp + n * V * K);
+    return p;
+  }
+};
+
+// Per-(b, h) scratch of the CUDA-core scan, fp32.
+struct ScanScratch {
+  int64_t vn, ot, vp, keys, bl, wl, gl, vn2, gvec, bdiag, size;
+  __host__ __device__ static ScanScratch make(int K, int V, int NP) {
+    ScanScratch s;
+    s.vn = 0;
+    s.ot = align_floats(s.vn + kC * V);
+    s.vp = align_floats(s.ot + kC * V);
+    s.keys = align_floats(s.vp + int64_t(NP) * V);
+    s.bl = align_floats(s.keys + int64_t(NP) * K);
+    s.wl = align_floats(s.bl + int64_t(NP) * K);
+    s.gl = align_floats(s.wl + int64_t(NP) * V);
+    s.vn2 = align_floats(s.gl + int64_t(NP) * K);
+    s.gvec = align_floats(s.vn2 + int64_t(NP) * V);
+    s.bdiag = align_floats(s.gvec + K);
+    s.size = align_floats(s.bdiag + NP);
+    return s;
+  }
+};
+
+struct FwdParams {
+  int B, T, H, K, V, L, NT, n_max, promotion, dtype, param_dtype;
+  float scale;
+  int nq[NGDN2_MAX_LEVELS];
+  int firing[NGDN2_MAX_LEVELS];
+  int NP;  // most pairs any level writes per firing
+  QView q;
+  TokView k, v, g, b, w, mix;  // mix: d indexes the level
+  const void* raw_params[5];   // query_banks, key/b/w/g projections as passed
+  const float* init;
+  void* o;
+  float* fin;
+  int32_t* status;
+  // workspace regions
+  float* params32;
+  ParamLayout pl;
+  float* chunks;
+  ChunkRecord rec;
+  float* scan;
+  ScanScratch ss;
+};
+
+// Arguments of the update-scan kernel (update_fwd.py:131-204).
+struct UpdParams {
+  int B, NF, NG, H, K, V, N, bv, dtype, g_dtype;
+  const void* keys;
+  int64_t skb, skf, skh, skn;
+  const void* values;
+  const void* g;
+  const void* b;
+  const void* w;
+  const float* init;
+  float* states;
+  float* fin;
+};
+
+}  // namespace ngdn2

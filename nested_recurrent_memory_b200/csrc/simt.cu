@@ -1,0 +1,407 @@
+// CUDA-core (SIMT) kernel family: fp32 arithmetic throughout.
+//
+// This is the precision path (fp32 inputs, parity at rel 1e-4) and the path
+// for shapes the tensor-core family does not cover. It keeps the two-stage
+// structure of the fast path:
+//
+//   prep  -- one CTA per (b, h, chunk), fully parallel. Per chunk it forms
+//            the S-independent operands of the chunkwise gated delta rule
+//            (nested_gdn2/ops/naive.py:329-352): cumulative log-decay G,
+//            the decay-masked K.K^T and Q.K^T blocks, the unit-lower-
+//            triangular solve [U | W] = (I + A_kk)^-1 [w*v | k*b*e^G], the
+//            read queries with mix and scale folded in, k*e^(G_last - G)
+//            and e^(G_last). Decays use the reference's clamped exponent
+//            e^min(G_i - G_j, 0) element by element, exactly as the oracle.
+//   scan  -- one CTA per (b, h), sequential over chunks: the state
+//            recurrence and output of level 0 (naive.py:376-392), the reads
+//            of levels >= 1 (naive.py:382-390) and, at each firing, the
+//            promotion of the level below into the level above
+//            (naive.py:394-415, probe.py:34-136, naive.py:7-39).
+//
+// States live in the caller's final_state buffer (fp32 [B, H, L, K, V]),
+// which doubles as the running state; per-(b, h) temporaries live in the
+// workspace.
+
+#include "fwd_params.cuh"
+
+namespace ngdn2 {
+
+__global__ void convert_params_kernel(FwdParams p) {
+  const int64_t n = int64_t(p.L - 1) * p.H;
+  const int64_t counts[5] = {n * p.n_max * p.K, n * p.K * p.V, n * p.V * p.K,
+                             n * p.V * p.V, n * p.V * p.K};
+  const int64_t offs[5] = {p.pl.qb, p.pl.kp, p.pl.bp, p.pl.wp, p.pl.gp};
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int a = 0; a < 5; ++a) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < counts[a]; i += stride)
+      p.params32[offs[a] + i] = load_elem(p.raw_params[a], i, p.param_dtype);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// prep: grid (NT, H, B), 256 threads.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
+  extern __shared__ float sm[];
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int K = p.K, V = p.V, KP = K + 1;
+  float* Gs = sm;              // [64][K+1] cumulative log-decay
+  float* Qs = Gs + kC * KP;    // [64][K+1] level-0 query
+  float* Ks = Qs + kC * KP;    // [64][K+1] key
+  float* BKs = Ks + kC * KP;   // [64][K+1] b * k
+  float* Akk = BKs + kC * KP;  // [64][65]
+  float* Aqk = Akk + kC * 65;  // [64][65]
+  const int tid = threadIdx.x;
+  const int t0 = n * kC;
+
+  // Load the chunk; tokens past T are zero (naive.py:302-312).
+  for (int e = tid; e < kC * K; e += blockDim.x) {
+    const int i = e / K, d = e % K, t = t0 + i;
+    float vq = 0.f, vk = 0.f, vg = 0.f, vb = 0.f;
+    if (t < p.T) {
+      vq = p.q.at(b, t, h, 0, d);
+      vk = p.k.at(b, t, h, d);
+      vg = p.g.at(b, t, h, d);
+      vb = p.b.at(b, t, h, d);
+    }
+    Qs[i * KP + d] = vq;
+    Ks[i * KP + d] = vk;
+    Gs[i * KP + d] = vg;
+    BKs[i * KP + d] = vb * vk;
+  }
+  __syncthreads();
+  // G = cumsum of g along the chunk (naive.py:329).
+  if (tid < K) {
+    float acc = 0.f;
+    for (int i = 0; i < kC; ++i) {
+      acc += Gs[i * KP + tid];
+      Gs[i * KP + tid] = acc;
+    }
+  }
+  __syncthreads();
+  // A_kk (strictly lower) and A_qk (lower, diagonal included) with the
+  // clamped per-channel decay (naive.py:335-344, 354-358, 377-378).
+  for (int e = tid; e < kC * kC; e += blockDim.x) {
+    const int i = e / kC, j = e % kC;
+    float aq = 0.f, ak = 0.f;
+    if (j <= i) {
+      const float* gi = Gs + i * KP;
+      const float* gj = Gs + j * KP;
+      const float* qi = Qs + i * KP;
+      const float* bki = BKs + i * KP;
+      const float* kj = Ks + j * KP;
+      for (int d = 0; d < K; ++d) {
+        const float kd = kj[d] * expf(fminf(gi[d] - gj[d], 0.f));
+        aq = fmaf(qi[d], kd, aq);
+        ak = fmaf(bki[d], kd, ak);
+      }
+    }
+    Aqk[i * 65 + j] = aq;
+    Akk[i * 65 + j] = (j < i) ? ak : 0.f;
+  }
+  __syncthreads();
+
+  float* rec = p.chunks + ((int64_t(b) * p.H + h) * p.NT + n) * p.rec.size;
+
+  // [U | W] = (I + A_kk)^-1 [w * v | k * b * e^G] by forward substitution,
+  // one column per thread (naive.py:346-351).
+  const int c = tid;
+  if (c < V + K) {
+    float x[kC];
+#pragma unroll
+    for (int i = 0; i < kC; ++i) {
+      const int t = t0 + i;
+      float r;
+      if (c < V) {
+        r = (t < p.T) ? p.w.at(b, t, h, c) *
+                            p.v.at(b, t, h, c)
+                      : 0.f;
+      } else {
+        const int d = c - V;
+        r = BKs[i * KP + d] * expf(Gs[i * KP + d]);
+      }
+#pragma unroll
+      for (int j = 0; j < i; ++j) r = fmaf(-Akk[i * 65 + j], x[j], r);
+      x[i] = r;
+    }
+#pragma unroll
+    for (int i = 0; i < kC; ++i) {
+      if (c < V) rec[p.rec.U + i * V + c] = x[i];
+      else rec[p.rec.W + i * K + (c - V)] = x[i];
+    }
+  }
+
+  // Output-side operands.
+  for (int e = tid; e < kC * kC; e += blockDim.x) {
+    const int i = e / kC, j = e % kC, t = t0 + i;
+    const float m0 = t < p.T ? p.mix.at(b, t, h, 0) : 0.f;
+    rec[p.rec.A + e] = (j <= i) ? Aqk[i * 65 + j] * p.scale * m0 : 0.f;
+  }
+  for (int e = tid; e < kC * K; e += blockDim.x) {
+    const int i = e / K, d = e % K, t = t0 + i;
+    const float m0 = t < p.T ? p.mix.at(b, t, h, 0) : 0.f;
+    const float gi = Gs[i * KP + d];
+    rec[p.rec.Q + e] = m0 * p.scale * Qs[i * KP + d] * expf(gi);
+    rec[p.rec.Kt + e] = Ks[i * KP + d] * expf(Gs[(kC - 1) * KP + d] - gi);
+  }
+  for (int l = 1; l < p.L; ++l) {
+    for (int e = tid; e < kC * K; e += blockDim.x) {
+      const int i = e / K, d = e % K, t = t0 + i;
+      float val = 0.f;
+      if (t < p.T)
+        val = p.mix.at(b, t, h, l) * p.scale *
+              p.q.at(b, t, h, l, d);
+      rec[p.rec.Q + int64_t(l) * kC * K + e] = val;
+    }
+  }
+  if (tid < K) rec[p.rec.eg + tid] = expf(Gs[(kC - 1) * KP + tid]);
+}
+
+// ---------------------------------------------------------------------------
+// scan: grid (H, B), 256 threads.
+// ---------------------------------------------------------------------------
+
+// Promote level l-1 into level l for one (b, h): probe then update.
+__device__ void promote_simt(const FwdParams& p, int b, int h, int l, float* S, float* sc,
+                             float* gsm) {
+  const int K = p.K, V = p.V;
+  const float* Sb = S + int64_t(l - 1) * K * V;
+  float* Sl = S + int64_t(l) * K * V;
+  const int64_t pidx = int64_t(l - 1) * p.H + h;
+  const float* qb = p.params32 + p.pl.qb + pidx * p.n_max * K;
+  const float* kp = p.params32 + p.pl.kp + pidx * K * V;
+  const float* bp = p.params32 + p.pl.bp + pidx * V * K;
+  const float* wp = p.params32 + p.pl.wp + pidx * V * V;
+  const float* gp = p.params32 + p.pl.gp + pidx * V * K;
+  float* Vp = sc + p.ss.vp;
+  float* Kk = sc + p.ss.keys;
+  float* Bl = sc + p.ss.bl;
+  float* Wl = sc + p.ss.wl;
+  float* Gl = sc + p.ss.gl;
+  float* Vn2 = sc + p.ss.vn2;
+  float* gv = sc + p.ss.gvec;
+  float* bd = sc + p.ss.bdiag;
+  const int tid = threadIdx.x;
+  const bool merge = p.promotion == NGDN2_PROMOTION_MERGE;
+  const int m = merge ? K : p.nq[l - 1];
+  // values: the bank's reads of the level below (probe.py:97-98), or the
+  // level below itself for merge (probe.py:133-136).
+  const float* vals = Sb;
+  if (!merge) {
+    block_gemm(m, V, K, [&](int r, int k) { return qb[r * K + k]; },
+               [&](int k, int c) { return Sb[k * V + c]; }, gsm,
+               [&](int r, int c, float a) { Vp[r * V + c] = a; });
+    vals = Vp;
+    // u = values . W_k^T (probe.py:99)
+    block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+               [&](int v, int k) { return kp[k * V + v]; }, gsm,
+               [&](int r, int k, float a) { Kk[r * K + k] = a; });
+  }
+  // gate logits (probe.py:59-62)
+  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+             [&](int v, int k) { return bp[v * K + k]; }, gsm,
+             [&](int r, int k, float a) { Bl[r * K + k] = a; });
+  block_gemm(m, V, V, [&](int r, int v) { return vals[r * V + v]; },
+             [&](int v, int u) { return wp[v * V + u]; }, gsm,
+             [&](int r, int u, float a) { Wl[r * V + u] = a; });
+  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+             [&](int v, int k) { return gp[v * K + k]; }, gsm,
+             [&](int r, int k, float a) { Gl[r * K + k] = a; });
+  if (!merge) {
+    // keys = normalize(u) (probe.py:100): one warp per row.
+    const int warp = tid / 32, lane = tid % 32;
+    for (int r = warp; r < m; r += blockDim.x / 32) {
+      float s = 0.f;
+      for (int k = lane; k < K; k += 32) s = fmaf(Kk[r * K + k], Kk[r * K + k], s);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float nrm = fmaxf(sqrtf(s), 1e-12f);
+      for (int k = lane; k < K; k += 32) Kk[r * K + k] = Kk[r * K + k] / nrm;
+    }
+    __syncthreads();
+    // k * b and v * w (probe.py:63-64, update_fwd.py:121-122)
+    for (int e = tid; e < m * K; e += blockDim.x) Bl[e] = Kk[e] * sigmoidf_(Bl[e] + kBLogitInit);
+    for (int e = tid; e < m * V; e += blockDim.x) Wl[e] = vals[e] * sigmoidf_(Wl[e] + kWLogitInit);
+  } else {
+    for (int r = tid; r < m; r += blockDim.x) bd[r] = sigmoidf_(Bl[r * K + r] + kBLogitInit);
+  }
+  // g = mean over pairs of -softplus(logit - 4) (probe.py:65)
+  for (int k = tid; k < K; k += blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < m; ++r) s += -softplusf_(Gl[r * K + k] + kGLogitInit);
+    gv[k] = s / float(m);
+  }
+  __syncthreads();
+  if (merge) {
+    // Identity keys: pair r writes row r only, so the update is elementwise
+    // (naive.py:32-39 with keys = I).
+    for (int e = tid; e < K * V; e += blockDim.x) {
+      const int k = e / V;
+      const float s = Sl[e] * expf(gv[k]);
+      Sl[e] = s - bd[k] * s + Sb[e] * sigmoidf_(Wl[e] + kWLogitInit);
+    }
+    __syncthreads();
+    return;
+  }
+  // S <- e^g S; vn = v*w - (k*b) S; S <- S + k^T vn  (update_fwd.py:120-123)
+  for (int e = tid; e < K * V; e += blockDim.x) Sl[e] *= expf(gv[e / V]);
+  __syncthreads();
+  block_gemm(m, V, K, [&](int r, int k) { return Bl[r * K + k]; },
+             [&](int k, int c) { return Sl[k * V + c]; }, gsm,
+             [&](int r, int c, float a) { Vn2[r * V + c] = Wl[r * V + c] - a; });
+  block_gemm(K, V, m, [&](int k, int r) { return Kk[r * K + k]; },
+             [&](int r, int c) { return Vn2[r * V + c]; }, gsm,
+             [&](int k, int c, float a) { Sl[k * V + c] += a; });
+}
+
+__global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
+  __shared__ float gsm[kGemmSmemFloats];
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int K = p.K, V = p.V, L = p.L, tid = threadIdx.x;
+  const int64_t bh = int64_t(b) * p.H + h;
+  float* S = p.fin + bh * L * K * V;
+  float* sc = p.scan + bh * p.ss.size;
+  for (int64_t e = tid; e < int64_t(L) * K * V; e += blockDim.x)
+    S[e] = p.init ? p.init[bh * L * K * V + e] : 0.f;
+  __syncthreads();
+  float* Vn = sc + p.ss.vn;
+  float* Ot = sc + p.ss.ot;
+  for (int n = 0; n < p.NT; ++n) {
+    const float* rec = p.chunks + (bh * p.NT + n) * p.rec.size;
+    const float* Wm = rec + p.rec.W;
+    const float* Um = rec + p.rec.U;
+    const float* Am = rec + p.rec.A;
+    const float* Qm = rec + p.rec.Q;
+    const float* Kt = rec + p.rec.Kt;
+    const float* eg = rec + p.rec.eg;
+    // v_new = U - W S0 (naive.py:376)
+    block_gemm(kC, V, K, [&](int i, int k) { return Wm[i * K + k]; },
+               [&](int k, int c) { return S[k * V + c]; }, gsm,
+               [&](int i, int c, float a) { Vn[i * V + c] = Um[i * V + c] - a; });
+    // o = sum_l (mix_l scale q_l [e^G at l=0]) S_l + mix_0 scale A_qk v_new
+    for (int l = 0; l < L; ++l) {
+      const float* Ql = Qm + int64_t(l) * kC * K;
+      const float* Sl = S + int64_t(l) * K * V;
+      block_gemm(kC, V, K, [&](int i, int k) { return Ql[i * K + k]; },
+                 [&](int k, int c) { return Sl[k * V + c]; }, gsm,
+                 [&](int i, int c, float a) {
+                   if (l == 0) Ot[i * V + c] = a; else Ot[i * V + c] += a;
+                 });
+    }
+    block_gemm(kC, V, kC, [&](int i, int j) { return Am[i * kC + j]; },
+               [&](int j, int c) { return Vn[j * V + c]; }, gsm,
+               [&](int i, int c, float a) { Ot[i * V + c] += a; });
+    for (int e = tid; e < kC * V; e += blockDim.x) {
+      const int i = e / V, c = e % V, t = n * kC + i;
+      if (t < p.T) store_elem(p.o, ((int64_t(b) * p.T + t) * p.H + h) * V + c, Ot[e], p.dtype);
+    }
+    // S0 <- e^(G_last) S0 + (k e^(G_last - G))^T v_new (naive.py:392)
+    block_gemm(K, V, kC, [&](int k, int i) { return Kt[i * K + k]; },
+               [&](int i, int c) { return Vn[i * V + c]; }, gsm,
+               [&](int k, int c, float a) { S[k * V + c] = eg[k] * S[k * V + c] + a; });
+    // Levels whose firing this chunk completes, bottom-up (naive.py:394-415).
+    for (int l = 1; l < L; ++l)
+      if ((n + 1) % p.firing[l] == 0) promote_simt(p, b, h, l, S, sc, gsm);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// update_state: grid (V / block_v, H, B), 256 threads.
+// ---------------------------------------------------------------------------
+
+
+
+__global__ void __launch_bounds__(256) update_simt_kernel(UpdParams u) {
+  extern __shared__ float sm[];
+  float* gsm = sm;
+  float* vn = sm + kGemmSmemFloats;  // [N][bv]
+  float* gs = vn + u.N * u.bv;       // [K]
+  const int v0 = blockIdx.x * u.bv, h = blockIdx.y, b = blockIdx.z;
+  const int K = u.K, V = u.V, N = u.N, bv = u.bv, tid = threadIdx.x;
+  const int64_t bh = int64_t(b) * u.H + h;
+  float* S = u.fin + bh * K * V;
+  for (int e = tid; e < K * bv; e += blockDim.x) {
+    const int k = e / bv, c = v0 + e % bv;
+    S[k * V + c] = u.init ? u.init[bh * K * V + k * V + c] : 0.f;
+  }
+  __syncthreads();
+  for (int j = 0; j < u.NG; ++j) {
+    float* st = u.states + ((int64_t(b) * u.NG + j) * u.H + h) * K * V;
+    for (int e = tid; e < K * bv; e += blockDim.x) {
+      const int k = e / bv, c = v0 + e % bv;
+      st[k * V + c] = S[k * V + c];
+    }
+    if (j >= u.NF) continue;
+    const int64_t base = (int64_t(b) * u.NF + j) * u.H + h;
+    for (int k = tid; k < K; k += blockDim.x) gs[k] = load_elem(u.g, base * K + k, u.g_dtype);
+    __syncthreads();
+    for (int e = tid; e < K * bv; e += blockDim.x) {
+      const int k = e / bv, c = v0 + e % bv;
+      S[k * V + c] *= expf(gs[k]);
+    }
+    __syncthreads();
+    const int64_t kbase = b * u.skb + j * u.skf + h * u.skh;
+    block_gemm(N, bv, K,
+               [&](int r, int k) {
+                 return load_elem(u.keys, kbase + r * u.skn + k, u.dtype) *
+                        load_elem(u.b, (base * N + r) * K + k, u.dtype);
+               },
+               [&](int k, int c) { return S[k * V + v0 + c]; }, gsm,
+               [&](int r, int c, float a) {
+                 const int64_t o = (base * N + r) * V + v0 + c;
+                 vn[r * bv + c] = load_elem(u.values, o, u.dtype) * load_elem(u.w, o, u.dtype) - a;
+               });
+    block_gemm(K, bv, N, [&](int k, int r) { return load_elem(u.keys, kbase + r * u.skn + k, u.dtype); },
+               [&](int r, int c) { return vn[r * bv + c]; }, gsm,
+               [&](int k, int c, float a) { S[k * V + v0 + c] += a; });
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+
+size_t prep_simt_smem(int K) { return sizeof(float) * (4 * kC * (K + 1) + 2 * kC * 65); }
+
+int num_launches_simt(const FwdParams& p) {
+  return (p.L > 1 ? 1 : 0) + (p.NT > 0 ? 1 : 0) + 1;
+}
+
+cudaError_t launch_fwd_simt(const FwdParams& p, int stage, cudaStream_t stream) {
+  cudaError_t err;
+  if (stage == 0 || stage == 1) {
+    if (p.L > 1) {
+      int64_t total = p.pl.size;
+      int blocks = int((total + 255) / 256);
+      if (blocks > 4096) blocks = 4096;
+      if (blocks < 1) blocks = 1;
+      convert_params_kernel<<<blocks, 256, 0, stream>>>(p);
+      if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    }
+    if (p.NT > 0) {
+      const size_t smem = prep_simt_smem(p.K);
+      err = cudaFuncSetAttribute(prep_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(smem));
+      if (err != cudaSuccess) return err;
+      prep_simt_kernel<<<dim3(p.NT, p.H, p.B), 256, smem, stream>>>(p);
+      if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    }
+  }
+  if (stage == 0 || stage == 2) {
+    scan_simt_kernel<<<dim3(p.H, p.B), 256, 0, stream>>>(p);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_update_simt(const UpdParams& u, cudaStream_t stream) {
+  const size_t smem = sizeof(float) * (kGemmSmemFloats + size_t(u.N) * u.bv + u.K);
+  cudaError_t err = cudaFuncSetAttribute(update_simt_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (err != cudaSuccess) return err;
+  update_simt_kernel<<<dim3(u.V / u.bv, u.H, u.B), 256, smem, stream>>>(u);
+  return cudaGetLastError();
+}
+
+}  // namespace ngdn2

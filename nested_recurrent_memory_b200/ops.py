@@ -1,0 +1,328 @@
+"""Drop-in replacements for the reference's ``nested_gdn2.ops`` forward ops.
+
+Same names, argument meanings, defaults, return values and ValueError
+messages as the reference (awehrs/nested_recurrent_memory):
+
+* ``chunk_nested_gdn2``      -- nested_gdn2/ops/chunk.py:722-766
+* ``chunk_nested_gdn2_fwd``  -- nested_gdn2/ops/chunk.py:159-304
+* ``update_state``           -- nested_gdn2/ops/update_fwd.py:131-204
+* ``n_groups``, ``n_firings`` -- nested_gdn2/ops/chunk.py:26-36
+
+The work is done by hand-written sm_100a CUDA kernels behind the C ABI of
+``libngdn2.so`` (include/ngdn2.h); this module only validates arguments,
+allocates outputs and workspace with torch, and passes raw pointers and the
+current CUDA stream. There is no CPU or framework fallback: CPU tensors or a
+missing library raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "chunk_nested_gdn2",
+    "chunk_nested_gdn2_fwd",
+    "update_state",
+    "n_groups",
+    "n_firings",
+    "fwd_workspace_bytes",
+    "last_path",
+    "FwdCall",
+]
+
+_DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+_LAST_PATH = [None]
+
+
+def last_path():
+    """Kernel family ("simt" or "tc") that ran the most recent forward."""
+    return _LAST_PATH[0]
+
+
+def n_groups(n_chunks: int, firing_interval: int) -> int:
+    """How many runs of ``firing_interval`` chunks cover ``n_chunks``
+    (chunk.py:26-31). The last run may be short; it is read but never fired."""
+    return (n_chunks + firing_interval - 1) // firing_interval
+
+
+def n_firings(n_chunks: int, firing_interval: int) -> int:
+    """How many firings occur in ``n_chunks``: one per complete run (chunk.py:34-36)."""
+    return n_chunks // firing_interval
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from None
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and t.device.type != "cuda":
+            raise RuntimeError(
+                "nested_recurrent_memory_b200 runs on CUDA tensors only (no CPU fallback); "
+                f"got a tensor on {t.device}")
+
+
+def _fill_tok(args, name, t, rank):
+    setattr(args, name, t.data_ptr())
+    setattr(args, f"{name}_dtype", _code(t))
+    st = getattr(args, f"{name}_stride")
+    for i, s in enumerate(t.stride()[:rank]):
+        st[i] = s
+
+
+def _raise_for(rc: int, what: str, **ctx):
+    if rc == 0:
+        return
+    msg = _lib.error_string(rc)
+    if rc == _lib.ERR_CHUNK_SIZE:
+        raise ValueError(f"chunk_size must be 64 for GDN-2, got {ctx.get('chunk_size')}")
+    if rc == _lib.ERR_N_POW2:
+        raise ValueError(f"pairs per firing must be a power of two >= 16, got {ctx.get('N')}")
+    if rc == _lib.ERR_BLOCK_V:
+        raise ValueError(f"block_v must be a power of two >= 16, got {ctx.get('block_v')}")
+    if rc == _lib.ERR_DIVISIBLE:
+        raise ValueError(f"V={ctx.get('V')} must be divisible by block_v={ctx.get('block_v')}")
+    if rc == _lib.ERR_UNIT_STRIDE:
+        raise ValueError("keys must be unit-stride along K")
+    if rc == _lib.ERR_INCONSISTENT:
+        raise ValueError(f"NF={ctx.get('NF')} inconsistent with n_groups={ctx.get('NG')}")
+    raise RuntimeError(f"{what} failed: {msg} (code {rc})")
+
+
+def _build_fwd_args(q, k, v, g, b, w, mix_weights, params, n_max, nq, firing, L, scale,
+                    init, o, final, chunk_size, promotion, path):
+    B, T, H, _, K = q.shape
+    V = v.shape[-1]
+    a = _lib.FwdArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.path = _lib.PATHS[path]
+    a.B, a.T, a.H, a.K, a.V, a.L = B, T, H, K, V, L
+    a.chunk_size = chunk_size
+    a.promotion = _lib.PROMOTION[promotion]
+    a.dtype = _code(o)
+    a.param_dtype = _code(params[0]) if params else _lib.F32
+    a.scale = float(scale)
+    a.n_max = n_max
+    for i, n in enumerate(nq):
+        a.n_queries[i] = n
+    for i, f in enumerate(firing):
+        a.firing[i] = f
+    _fill_tok(a, "q", q, 5)
+    for name, t in (("k", k), ("v", v), ("g", g), ("b", b), ("w", w), ("mix", mix_weights)):
+        _fill_tok(a, name, t, 4)
+    if params:
+        (a.query_banks, a.key_projections, a.b_projections, a.w_projections,
+         a.g_projections) = (p.data_ptr() for p in params)
+    a.initial_state = init.data_ptr() if init is not None else None
+    a.o = o.data_ptr()
+    a.final_state = final.data_ptr()
+    return a
+
+
+def fwd_workspace_bytes(args: "_lib.FwdArgs") -> int:
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    rc = lib.ngdn2_fwd_workspace_size(ctypes.byref(args), ctypes.byref(nbytes))
+    _raise_for(rc, "ngdn2_fwd_workspace_size", chunk_size=args.chunk_size)
+    return int(nbytes.value)
+
+
+class FwdCall:
+    """One validated forward call bound to its tensors.
+
+    Holds the C-ABI argument struct, the outputs (``o``, ``final``) and the
+    workspace, so the same call can be launched repeatedly (benchmarks,
+    CUDA-graph capture) without re-validating or re-allocating. Launches go
+    on the current CUDA stream of the inputs' device.
+    """
+
+    def __init__(self, q, k, v, g, b, w, mix_weights, query_banks, key_projections,
+                 b_projections, w_projections, g_projections, n_queries_per_level,
+                 firing_intervals, L, scale=None, initial_state=None, chunk_size=64,
+                 promotion="learned", path="auto", workspace=None):
+        B, T, H, _, K = q.shape
+        if chunk_size != 64:  # chunk.py:230-231
+            raise ValueError(f"chunk_size must be 64 for GDN-2, got {chunk_size}")
+        if promotion not in _lib.PROMOTION:
+            raise KeyError(promotion)  # PROBES[promotion] in the reference
+        if path not in _lib.PATHS:
+            raise ValueError(f"path must be one of {sorted(_lib.PATHS)}, got {path!r}")
+        if scale is None:
+            scale = K ** -0.5
+        V = v.shape[-1]
+        firing = [int(x) for x in firing_intervals]
+        nq = [int(x) for x in n_queries_per_level]
+        for lvl in range(1, L):
+            n = K if promotion == "merge" else nq[lvl - 1]
+            if n < 16 or n & (n - 1):  # update_fwd.py:162-163
+                raise ValueError(f"pairs per firing must be a power of two >= 16, got {n}")
+        _require_cuda(q, k, v, g, b, w, mix_weights, initial_state)
+        params, n_max = [], 1
+        if L > 1:
+            pdt = query_banks.dtype
+            params = [t.to(q.device, pdt).contiguous() for t in
+                      (query_banks, key_projections, b_projections, w_projections, g_projections)]
+            _require_cuda(*params)
+            n_max = query_banks.shape[2]
+        init = initial_state.to(torch.float32).contiguous() if initial_state is not None else None
+        self.device = q.device
+        self.T = T
+        self.o = torch.empty(B, T, H, V, dtype=q.dtype, device=q.device)
+        self.final = torch.empty(B, H, L, K, V, dtype=torch.float32, device=q.device)
+        self.init = init
+        self._keep = (q, k, v, g, b, w, mix_weights, params, init)
+        self.path = None
+        self.args = None
+        if T == 0:
+            return
+        lib = _lib.load()
+        self.args = _build_fwd_args(q, k, v, g, b, w, mix_weights, params, n_max, nq, firing, L,
+                                    scale, init, self.o, self.final, chunk_size, promotion, path)
+        sel = lib.ngdn2_fwd_select_path(ctypes.byref(self.args))
+        _raise_for(sel if sel < 0 else 0, "ngdn2_fwd_select_path", chunk_size=chunk_size)
+        self.path = _lib.PATH_NAMES.get(sel)
+        need = fwd_workspace_bytes(self.args)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+        self.workspace = workspace
+        self.args.workspace = workspace.data_ptr()
+        self.args.workspace_bytes = workspace.numel()
+
+    @property
+    def num_launches(self) -> int:
+        if self.args is None:
+            return 0
+        return _lib.load().ngdn2_fwd_num_launches(ctypes.byref(self.args))
+
+    def launch(self, stage: int = 0):
+        """Run the forward (stage 0) or one of its stages (1 = prep, 2 = scan)."""
+        if self.args is None:
+            self.final.copy_(self.init if self.init is not None else torch.zeros_like(self.final))
+            return self.o, self.final
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = _lib.load().ngdn2_fwd_stage(ctypes.byref(self.args), stage, ctypes.c_void_p(stream))
+        _raise_for(rc, "ngdn2_fwd", chunk_size=self.args.chunk_size)
+        _LAST_PATH[0] = self.path
+        return self.o, self.final
+
+
+def chunk_nested_gdn2_fwd(
+    q, k, v, g, b, w, mix_weights, query_banks, key_projections, b_projections,
+    w_projections, g_projections, n_queries_per_level, firing_intervals, L,
+    scale=None, initial_state=None, output_final_state=False, chunk_size=64,
+    return_aux=False, promotion="learned", *, path="auto", workspace=None,
+):
+    """Chunkwise NestedGDN-2 forward (chunk.py:159-304).
+
+    Args and returns as the reference: q [B, T, H, L, K]; k, g, b
+    [B, T, H, K]; v, w [B, T, H, V]; mix_weights [B, T, H, L];
+    query_banks [L-1, H, N, K]; key_projections [L-1, H, K, V];
+    b/g_projections [L-1, H, V, K]; w_projections [L-1, H, V, V];
+    n_queries_per_level [L-1] ints; firing_intervals [L] ints; initial_state
+    [B, H, L, K, V] or None. Returns ``(o, final_state)`` with o in q's dtype
+    and final_state fp32 (None unless ``output_final_state``); with
+    ``return_aux`` also a dict, which here holds only ``scale`` and the
+    per-level ``finals`` -- this forward-only build keeps no backward
+    intermediates.
+
+    Keyword-only extras: ``path`` ("auto", "simt" or "tc") picks the kernel
+    family; ``workspace`` is an optional preallocated uint8 CUDA tensor.
+    """
+    call = FwdCall(q, k, v, g, b, w, mix_weights, query_banks, key_projections, b_projections,
+                   w_projections, g_projections, n_queries_per_level, firing_intervals, L,
+                   scale=scale, initial_state=initial_state, chunk_size=chunk_size,
+                   promotion=promotion, path=path, workspace=workspace)
+    o, final = call.launch()
+    final_state = final if output_final_state else None
+    if not return_aux:
+        return o, final_state
+    aux = dict(scale=scale if scale is not None else q.shape[-1] ** -0.5,
+               finals=list(final.unbind(2)))
+    return o, final_state, aux
+
+
+class ChunkNestedGDN2Function(torch.autograd.Function):
+    """Autograd node for the whole op (chunk.py:567-719), forward only."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, b, w, mix_weights, query_banks, key_projections,
+                b_projections, w_projections, g_projections, n_queries_per_level,
+                firing_intervals, L, scale, initial_state, output_final_state,
+                chunk_size, promotion):
+        o, final_state = chunk_nested_gdn2_fwd(
+            q, k, v, g, b, w, mix_weights, query_banks, key_projections, b_projections,
+            w_projections, g_projections, n_queries_per_level, firing_intervals, L,
+            scale=scale, initial_state=initial_state, output_final_state=True,
+            chunk_size=chunk_size, promotion=promotion)
+        return o, (final_state if output_final_state else None)
+
+    @staticmethod
+    def backward(ctx, do, dfinal):
+        raise NotImplementedError(
+            "nested_recurrent_memory_b200 implements the forward hot path only; "
+            "the chunkwise backward (reference chunk.py:307-564) is not built")
+
+
+def chunk_nested_gdn2(q, k, v, g, b, w, mix_weights, query_banks, key_projections,
+                      b_projections, w_projections, g_projections, n_queries_per_level,
+                      firing_intervals, L, scale=None, initial_state=None,
+                      output_final_state=False, chunk_size=64, promotion="learned"):
+    """Chunkwise NestedGDN-2 (chunk.py:722-766). Signature matches the naive op."""
+    return ChunkNestedGDN2Function.apply(
+        q, k, v, g, b, w, mix_weights, query_banks, key_projections, b_projections,
+        w_projections, g_projections, n_queries_per_level, firing_intervals, L, scale,
+        initial_state, output_final_state, chunk_size, promotion)
+
+
+def update_state(keys, values, g, b, w, n_groups, initial_state=None, block_v=16):
+    """Run one level's write scan over all groups (update_fwd.py:131-204).
+
+    keys [B, NF, H, N, K] (may be a broadcast view; read by stride);
+    values, w [B, NF, H, N, V]; g [B, NF, H, K]; b [B, NF, H, N, K].
+    Returns states [B, NG, H, K, V] (the state entering each group) and the
+    final state [B, H, K, V], both float32.
+    """
+    B, NF, H, N, K = keys.shape
+    V = values.shape[-1]
+    # update_fwd.py:162-171, same checks and order.
+    if N < 16 or N & (N - 1):
+        raise ValueError(f"pairs per firing must be a power of two >= 16, got {N}")
+    if block_v < 16 or block_v & (block_v - 1):
+        raise ValueError(f"block_v must be a power of two >= 16, got {block_v}")
+    if V % block_v:
+        raise ValueError(f"V={V} must be divisible by block_v={block_v}")
+    if keys.stride(-1) != 1:
+        raise ValueError("keys must be unit-stride along K")
+    if not (n_groups - 1 <= NF <= n_groups):
+        raise ValueError(f"NF={NF} inconsistent with n_groups={n_groups}")
+    _require_cuda(keys, values, g, b, w, initial_state)
+    dt = values.dtype
+    if keys.dtype != dt:
+        keys = keys.to(dt)
+    values, b, w = (t.to(dt).contiguous() for t in (values, b, w))
+    g = g.contiguous()
+    states = values.new_empty(B, n_groups, H, K, V, dtype=torch.float32)
+    final = values.new_empty(B, H, K, V, dtype=torch.float32)
+    init = initial_state.to(torch.float32).contiguous() if initial_state is not None else None
+    a = _lib.UpdateArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.B, a.NF, a.NG, a.H, a.K, a.V, a.N = B, NF, n_groups, H, K, V, N
+    a.block_v = block_v
+    a.dtype, a.g_dtype = _code(values), _code(g)
+    a.keys = keys.data_ptr()
+    for i, s in enumerate(keys.stride()):
+        a.keys_stride[i] = s
+    a.values, a.g, a.b, a.w = values.data_ptr(), g.data_ptr(), b.data_ptr(), w.data_ptr()
+    a.initial_state = init.data_ptr() if init is not None else None
+    a.states, a.final_state = states.data_ptr(), final.data_ptr()
+    stream = torch.cuda.current_stream(values.device).cuda_stream
+    rc = _lib.load().ngdn2_update_state(ctypes.byref(a), ctypes.c_void_p(stream))
+    _raise_for(rc, "ngdn2_update_state", N=N, block_v=block_v, V=V, NF=NF, NG=n_groups)
+    return states, final
