@@ -20,12 +20,12 @@ CONSISTENCY = dict(rtol=1e-5, atol=1e-6)
 def _inputs(B, NF, H, K, V, N, *, seed=0, identity_keys=False):
     gen = torch.Generator().manual_seed(seed)
     r = lambda *s: torch.randn(*s, generator=gen)  # noqa: E731
-    keys = (torch.eye(K).expand(B, NF, H, K, K) if identity_keys
-            else F.normalize(r(B, NF, H, N, K), dim=-1))
-    out = dict(keys=keys, values=r(B, NF, H, N, V) * V ** -0.5,
+    keys = (torch.eye(K, device="cuda").expand(B, NF, H, K, K) if identity_keys
+            else F.normalize(r(B, NF, H, N, K), dim=-1).cuda())
+    out = dict(values=r(B, NF, H, N, V) * V ** -0.5,
                g=-F.softplus(r(B, NF, H, K)), b=torch.sigmoid(r(B, NF, H, N, K)),
                w=torch.sigmoid(r(B, NF, H, N, V)))
-    return {k: v.cuda() for k, v in out.items()}
+    return {"keys": keys, **{k: v.cuda() for k, v in out.items()}}
 
 
 def _scan(inp, NG, init=None):
