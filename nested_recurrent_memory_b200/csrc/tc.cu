@@ -1,11 +1,724 @@
-// Tensor-core (tcgen05) kernel family.
+// Tensor-core (tcgen05) kernel family for K = V = 128, 16-bit inputs.
+//
+// Same two-stage structure as the CUDA-core family, with every chunk
+// contraction on the 5th-generation tensor cores (bf16 operands staged in
+// shared memory in UMMA canonical layouts, fp32 accumulators in TMEM):
+//
+//   prep_tc  -- one CTA per (b, h, chunk), two CTAs per SM. Builds the
+//               decay-scaled operands, computes A_qk / A_kk with four
+//               M=64 MMAs (one per 16-token block of queries, each with its
+//               own decay reference point so no factor overflows), inverts
+//               I + A_kk on CUDA cores in fp32 (16x16 diagonal blocks, then
+//               block forward substitution), and forms [U | W] with one
+//               M=64, N=256 MMA. Writes a chunk record whose operand tiles
+//               are already in the scan's shared-memory layout.
+//   scan_tc  -- one CTA per (b, h). The level-0 state S0 lives in TMEM
+//               (fp32, lanes = key index) for the whole sequence, a bf16
+//               copy of every level's state sits in shared memory as the
+//               MMA B operand. Per chunk: one bulk copy brings the record in,
+//               MMA1 forms W.S0 and the multi-level read sum_l Q_l.S_l, the
+//               epilogue forms v_new = U - W.S0 while other warps decay S0 in
+//               TMEM, MMA2 adds A_qk.v_new to the output and K_tail^T.v_new to
+//               S0. Promotions of levels >= 1 run at their firings on CUDA
+//               cores in fp32 against the fp32 master states.
+//
+// Reference: level 0 follows nested_gdn2/ops/naive.py:329-392 (chunk form of
+// fla's GDN-2, chunk.py:236-248), reads and mix naive.py:382-390, promotion
+// naive.py:394-415 with probe.py:34-136.
+
+#include "promote_simt.cuh"
 #include "tc_api.cuh"
+#include "tc_ptx.cuh"
 
 namespace ngdn2 {
 
-bool tc_supports(const ngdn2_fwd_args*) { return false; }
-size_t tc_workspace_bytes(const FwdParams&) { return 0; }
-cudaError_t launch_fwd_tc(FwdParams, void*, int, cudaStream_t) { return cudaErrorNotSupported; }
-int num_launches_tc(const FwdParams&) { return 0; }
+cudaError_t launch_convert_params(const FwdParams& p, cudaStream_t stream);
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+using namespace tc;
+
+constexpr int TK = 128;         // key dim handled by this family
+constexpr int TV = 128;         // value dim
+constexpr int TILE_QK = kC * TK * 2;   // bytes of a [64 x 128] bf16 tile
+constexpr int TILE_A = kC * kC * 2;    // bytes of a [64 x 64] bf16 tile
+
+// Byte offsets inside one chunk record of the tensor-core family.
+struct TcRecord {
+  int64_t W, Q, A, Kt, U, eg, load_bytes, size;
+  __host__ __device__ static TcRecord make(int L) {
+    TcRecord r;
+    r.W = 0;                                  // [64 x K] K-major A operand
+    r.Q = r.W + TILE_QK;                      // L x [64 x K] K-major A operands
+    r.A = r.Q + int64_t(L) * TILE_QK;         // [64 x 64] K-major A operand
+    r.Kt = r.A + TILE_A;                      // [64 tok x K] MN-major A operand (K_tail^T)
+    r.load_bytes = r.Kt + TILE_QK;            // the part the scan copies to smem
+    r.U = r.load_bytes;                       // [64 x V] row-major bf16
+    r.eg = r.U + kC * TV * 2;                 // [K] fp32 e^(G_last)
+    r.size = (r.eg + TK * 4 + 127) & ~int64_t(127);
+    return r;
+  }
+};
+
+struct TcLayout {
+  TcRecord rec;
+  int64_t params32_off, chunks_off, scan_off, total;
+};
+
+__host__ __device__ inline TcLayout tc_layout(const FwdParams& p) {
+  TcLayout t;
+  t.rec = TcRecord::make(p.L);
+  t.params32_off = 0;
+  t.chunks_off = (p.pl.size * 4 + 255) & ~int64_t(255);
+  t.scan_off = t.chunks_off + int64_t(p.B) * p.H * p.NT * t.rec.size;
+  t.scan_off = (t.scan_off + 255) & ~int64_t(255);
+  t.total = t.scan_off + int64_t(p.B) * p.H * p.ss.size * 4;
+  return t;
+}
+
+__device__ __forceinline__ void set_status(const FwdParams& p, int bits) {
+  if (p.status) atomicOr(p.status, bits);
+}
+
+// 8 consecutive elements starting at element offset ``o`` (element stride
+// ``sd``), as fp32. Uses one 16-byte load when the data are contiguous and
+// 16-byte aligned, else element loads.
+__device__ __forceinline__ void load8_raw(const void* p, int dt, int64_t o, int64_t sd, float* out) {
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+  if (sd == 1 && aligned16) {
+    if (dt != NGDN2_F32 && (o & 7) == 0) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + o);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f;
+        if (dt == NGDN2_BF16) f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        else f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+      }
+      return;
+    }
+    if (dt == NGDN2_F32 && (o & 3) == 0) {
+      const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + o);
+      const float4 c = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + o + 4);
+      out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+      out[4] = c.x; out[5] = c.y; out[6] = c.z; out[7] = c.w;
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = load_elem(p, o + i * sd, dt);
+}
+
+__device__ __forceinline__ void load8(const TokView& tv, int b, int t, int h, int d, float* out) {
+  load8_raw(tv.p, tv.dt, tv.off(b, t, h, d), tv.sd, out);
+}
+
+__device__ __forceinline__ void load8q(const QView& qv, int b, int t, int h, int l, int d, float* out) {
+  load8_raw(qv.p, qv.dt, qv.off(b, t, h, l, d), qv.sd, out);
+}
+
+// Pack 8 floats as 8 bf16 (16 bytes).
+__device__ __forceinline__ uint4 pack8(const float* x) {
+  uint4 r;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 v2 = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&v2);
+  }
+  return r;
+}
+
+}  // namespace
+}  // namespace ngdn2
+
+namespace ngdn2 {
+namespace {
+
+// ---------------------------------------------------------------------------
+// prep_tc: grid (NT, H, B), 256 threads, two CTAs per SM.
+// ---------------------------------------------------------------------------
+
+constexpr int kPrepThreads = 256;
+constexpr int kPrepCols = 256;  // TMEM columns
+
+// Shared-memory plan (bytes). Phase 1 (operands of the A_qk / A_kk MMAs)
+// and phase 2 (inverse and the [U | W] MMA) share one region.
+constexpr int P_G = 0;                   // fp32 [64][128] cumulative log-decay
+constexpr int P_R0 = 32768;
+constexpr int P_KG = P_R0;               // K^(J), J = 0..3: 20 groups of 8 rows x 128, K-major
+constexpr int P_QB = P_R0 + 40960;       // 4 x [32 x 128] K-major: 16 query rows, 16 b*k rows
+constexpr int P_AF = P_R0;               // fp32 [64][65] strictly lower A_kk
+constexpr int P_XF = P_AF + 16640;       // fp32 [64][65] (I + A_kk)^-1
+constexpr int P_R = P_XF + 16640;        // bf16 [64 x 256] MN-major [w*v | k*b*e^G]
+constexpr int P_XB = P_R + 32768;        // bf16 [64 x 64] K-major inverse
+constexpr int kPrepSmem = P_XB + 8192;   // 107008
+
+// Row-group offset (in elements) of K^(J) inside the P_KG region: K^(J)
+// keeps rows 0 .. 16J+15 (later rows are never needed), so the four tiles
+// pack into 2 + 4 + 6 + 8 groups. The J-th MMA still reads 64 rows; rows
+// past 16J+15 belong to the next tile and land in masked entries.
+__device__ __forceinline__ int kgroup_elems(int J) {
+  return (J == 0 ? 0 : J == 1 ? 2 : J == 2 ? 6 : 12) * 1024;
+}
+
+__global__ void __launch_bounds__(kPrepThreads, 2)
+prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tbase;
+  __shared__ float mix0s[kC];
+  __shared__ float Tt[3 * 256];
+  float* Gs = reinterpret_cast<float*>(sm + P_G);
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = n * kC;
+  char* rec = ws + lay.chunks_off + ((int64_t(b) * p.H + h) * p.NT + n) * lay.rec.size;
+
+  if (warp == 0) tmem_alloc(&tbase, kPrepCols);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (tid < kC) mix0s[tid] = (t0 + tid < p.T) ? p.mix.at(b, t0 + tid, h, 0) : 0.f;
+
+  // 1. G = cumsum of g along the chunk (naive.py:329); zero past T.
+  {
+    const int d = tid & 127, half = tid >> 7;
+    float gv[32];
+    float acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      const int t = t0 + half * 32 + r;
+      acc += (t < p.T) ? p.g.at(b, t, h, d) : 0.f;
+      gv[r] = acc;
+    }
+    if (half == 0) {
+#pragma unroll
+      for (int r = 0; r < 32; ++r) Gs[r * 128 + d] = gv[r];
+    }
+    __syncthreads();
+    if (half == 1) {
+      const float base = Gs[31 * 128 + d];
+#pragma unroll
+      for (int r = 0; r < 32; ++r) Gs[(32 + r) * 128 + d] = gv[r] + base;
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tb = tbase;
+
+  // 2. Operands of the A_qk / A_kk MMAs. Row block I of queries uses the
+  //    reference point rho_I = G[16I + 7] (per channel):
+  //      Q_I[i]  = q_i * e^(G_i - rho_I),  BK_I[i] = b_i * k_i * e^(G_i - rho_I)
+  //      K^(J)[j] = k_j * e^(rho_J - G_j) for j <= 16J + 15
+  //    so Q_I[i] . K^(I)[j] = q_i . k_j e^(G_i - G_j) with both factors
+  //    bounded by the decay over 8 tokens (naive.py:335-344, 377-378).
+  bf16* KG = reinterpret_cast<bf16*>(sm + P_KG);
+  bf16* QB = reinterpret_cast<bf16*>(sm + P_QB);
+  for (int it = tid; it < kC * 16; it += kPrepThreads) {
+    const int r = it >> 4, d0 = (it & 15) * 8, t = t0 + r;
+    float kk[8], qq[8], bb[8], G[8], o1[8], o2[8];
+    if (t < p.T) {
+      load8(p.k, b, t, h, d0, kk);
+      load8q(p.q, b, t, h, 0, d0, qq);
+      load8(p.b, b, t, h, d0, bb);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) kk[u] = qq[u] = bb[u] = 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) G[u] = Gs[r * 128 + d0 + u];
+    const int I = r >> 4;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float e = __expf(G[u] - Gs[(16 * I + 7) * 128 + d0 + u]);
+      o1[u] = qq[u] * e;
+      o2[u] = bb[u] * kk[u] * e;
+    }
+    bf16* tile = QB + I * (32 * 128);
+    *reinterpret_cast<uint4*>(tile + kmajor_off(r & 15, d0, 128)) = pack8(o1);
+    *reinterpret_cast<uint4*>(tile + kmajor_off(16 + (r & 15), d0, 128)) = pack8(o2);
+    for (int J = I; J < 4; ++J) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o1[u] = kk[u] * __expf(Gs[(16 * J + 7) * 128 + d0 + u] - G[u]);
+      *reinterpret_cast<uint4*>(KG + kgroup_elems(J) + kmajor_off(r, d0, 128)) = pack8(o1);
+    }
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+
+  // 3. MMA1: D[j, 32J + c] = K^(J)[j] . [Q_J ; BK_J][c], M=64, N=32, K=128.
+  if (tid == 0) {
+    const uint32_t id = idesc_f16(64, 32, true, false, false);
+    for (int J = 0; J < 4; ++J)
+      mma_tile(tb + 32 * J, smem_u32(KG + kgroup_elems(J)), smem_u32(QB + J * 32 * 128), 128, id,
+               false);
+    mma_commit(&bar);
+  }
+  __syncwarp();
+
+  // 4. While MMA1 runs: read queries, K_tail and e^(G_last) into the record.
+  {
+    bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
+    bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
+    for (int it = tid; it < kC * 16; it += kPrepThreads) {
+      const int r = it >> 4, d0 = (it & 15) * 8, t = t0 + r;
+      const bool valid = t < p.T;
+      float qq[8], kk[8], out[8];
+      if (valid) {
+        load8q(p.q, b, t, h, 0, d0, qq);
+        load8(p.k, b, t, h, d0, kk);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) qq[u] = kk[u] = 0.f;
+      }
+      const float m0 = mix0s[r] * p.scale;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) out[u] = m0 * qq[u] * __expf(Gs[r * 128 + d0 + u]);
+      *reinterpret_cast<uint4*>(Qg + kmajor_off(r, d0, 128)) = pack8(out);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        out[u] = kk[u] * __expf(Gs[63 * 128 + d0 + u] - Gs[r * 128 + d0 + u]);
+      *reinterpret_cast<uint4*>(Ktg + mnmajor_off(r, d0, 64)) = pack8(out);
+      for (int l = 1; l < p.L; ++l) {
+        if (valid) load8q(p.q, b, t, h, l, d0, qq);
+        const float ml = valid ? p.mix.at(b, t, h, l) * p.scale : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) out[u] = ml * qq[u];
+        *reinterpret_cast<uint4*>(Qg + l * (kC * 128) + kmajor_off(r, d0, 128)) = pack8(out);
+      }
+    }
+    if (tid < 128)
+      reinterpret_cast<float*>(rec + lay.rec.eg)[tid] = __expf(Gs[63 * 128 + tid]);
+  }
+
+  if (!mbar_wait(&bar, 0)) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
+  fence_after_sync();
+
+  // 5. E1: masks; A_kk to shared fp32, mix0 * scale * A_qk to the record.
+  float* Af = reinterpret_cast<float*>(sm + P_AF);
+  {
+    bf16* Ag = reinterpret_cast<bf16*>(rec + lay.rec.A);
+    const int q = warp & 3, ch = warp >> 2, j = 16 * q + lane;
+    for (int c16 = 0; c16 < 4; ++c16) {
+      float v[16];
+      const int col0 = 64 * ch + 16 * c16;
+      tmem_ld16(taddr(tb, 32 * q, col0), v);
+      tmem_wait_ld();
+      if (lane < 16) {
+        const int J = col0 >> 5;
+        if (col0 & 16) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int i = 16 * J + c;
+            Af[i * 65 + j] = (j < i) ? v[c] : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int i = 16 * J + c;
+            Ag[kmajor_off(i, j, 64)] =
+                __float2bfloat16_rn(j <= i ? v[c] * p.scale * mix0s[i] : 0.f);
+          }
+        }
+      }
+    }
+  }
+
+  // 6. B operand of the [U | W] MMA: R = [w * v | k * b * e^G], MN-major.
+  bf16* Rs = reinterpret_cast<bf16*>(sm + P_R);
+  for (int it = tid; it < kC * 32; it += kPrepThreads) {
+    const int j = it >> 5, n0 = (it & 31) * 8, t = t0 + j;
+    float out[8];
+    if (t >= p.T) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) out[u] = 0.f;
+    } else if (n0 < 128) {
+      float vv[8], ww[8];
+      load8(p.v, b, t, h, n0, vv);
+      load8(p.w, b, t, h, n0, ww);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) out[u] = ww[u] * vv[u];
+    } else {
+      const int d0 = n0 - 128;
+      float kk[8], bb[8];
+      load8(p.k, b, t, h, d0, kk);
+      load8(p.b, b, t, h, d0, bb);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) out[u] = kk[u] * bb[u] * __expf(Gs[j * 128 + d0 + u]);
+    }
+    *reinterpret_cast<uint4*>(Rs + mnmajor_off(j, n0, 64)) = pack8(out);
+  }
+  __syncthreads();
+
+  // 7. (I + A_kk)^-1 in fp32: 16x16 diagonal blocks by forward substitution,
+  //    then X_IJ = -X_II sum_{K=J}^{I-1} A_IK X_KJ block row by block row.
+  float* Xf = reinterpret_cast<float*>(sm + P_XF);
+  if (tid < 64) {
+    const int o = 16 * (tid >> 4), c = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float s = (r == c) ? 1.f : 0.f;
+#pragma unroll
+      for (int u = 0; u < r; ++u) s = fmaf(-Af[(o + r) * 65 + o + u], x[u], s);
+      x[r] = s;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) Xf[(o + r) * 65 + o + c] = x[r];
+  }
+  __syncthreads();
+  for (int I = 1; I < 4; ++I) {
+    for (int e = tid; e < I * 256; e += kPrepThreads) {
+      const int J = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      float s = 0.f;
+      for (int K2 = J; K2 < I; ++K2)
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          s = fmaf(Af[(16 * I + r) * 65 + 16 * K2 + m], Xf[(16 * K2 + m) * 65 + 16 * J + c], s);
+      Tt[e] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < I * 256; e += kPrepThreads) {
+      const int J = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      float s = 0.f;
+      for (int m = 0; m <= r; ++m) s = fmaf(Xf[(16 * I + r) * 65 + 16 * I + m], Tt[(J << 8) + m * 16 + c], s);
+      Xf[(16 * I + r) * 65 + 16 * J + c] = -s;
+    }
+    __syncthreads();
+  }
+  bf16* Xb = reinterpret_cast<bf16*>(sm + P_XB);
+  for (int it = tid; it < kC * 8; it += kPrepThreads) {
+    const int i = it >> 3, j0 = (it & 7) * 8;
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = (j0 + u <= i) ? Xf[i * 65 + j0 + u] : 0.f;
+    *reinterpret_cast<uint4*>(Xb + kmajor_off(i, j0, 64)) = pack8(x);
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+
+  // 8. MMA2: [U | W] = X . R, M=64, N=256, K=64 (naive.py:346-351).
+  if (tid == 0) {
+    mma_tile(tb, smem_u32(Xb), smem_u32(Rs), 64, idesc_f16(64, 256, true, false, true), false);
+    mma_commit(&bar);
+  }
+  __syncwarp();
+  if (!mbar_wait(&bar, 1)) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
+  fence_after_sync();
+
+  // 9. E2: U (row-major) and W (K-major A operand) to the record.
+  {
+    bf16* Ug = reinterpret_cast<bf16*>(rec + lay.rec.U);
+    bf16* Wg = reinterpret_cast<bf16*>(rec + lay.rec.W);
+    const int q = warp & 3, ch = warp >> 2, i = 16 * q + lane;
+    for (int c16 = 0; c16 < 8; ++c16) {
+      float v[16];
+      tmem_ld16(taddr(tb, 32 * q, 128 * ch + 16 * c16), v);
+      tmem_wait_ld();
+      if (lane < 16) {
+        const int d0 = 16 * c16;
+        if (ch == 0) {
+          *reinterpret_cast<uint4*>(Ug + i * 128 + d0) = pack8(v);
+          *reinterpret_cast<uint4*>(Ug + i * 128 + d0 + 8) = pack8(v + 8);
+        } else {
+          *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0, 128)) = pack8(v);
+          *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0 + 8, 128)) = pack8(v + 8);
+        }
+      }
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tb, kPrepCols);
+}
+
+}  // namespace
+}  // namespace ngdn2
+
+namespace ngdn2 {
+namespace {
+
+// ---------------------------------------------------------------------------
+// scan_tc: grid (H, B), 256 threads, one CTA per SM.
+// ---------------------------------------------------------------------------
+
+constexpr int kScanThreads = 256;
+constexpr int kScanCols = 256;          // TMEM: S0 in 0..127, chunk accumulators 128..255
+constexpr int TILE_S = TK * TV * 2;     // bf16 state copy
+
+__host__ __device__ inline int64_t scan_tc_smem(int L, const TcRecord& rec) {
+  return int64_t(L) * TILE_S + rec.load_bytes + TILE_QK + kGemmSmemFloats * 4;
+}
+
+// fp32 master [K][V] -> bf16 MN-major B operand copy [Kd = K][N = V].
+__device__ __forceinline__ void refresh_copy(bf16* dst, const float* src) {
+  for (int it = threadIdx.x; it < TK * (TV / 8); it += kScanThreads) {
+    const int k = it / (TV / 8), v0 = (it % (TV / 8)) * 8;
+    const float4 a = *reinterpret_cast<const float4*>(src + k * TV + v0);
+    const float4 c = *reinterpret_cast<const float4*>(src + k * TV + v0 + 4);
+    const float x[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+    *reinterpret_cast<uint4*>(dst + mnmajor_off(k, v0, TK)) = pack8(x);
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads, 1)
+scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ uint64_t bar_ld, bar_mma;
+  __shared__ uint32_t tbase;
+  __shared__ int abort_flag;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int L = p.L;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int64_t bh = int64_t(b) * p.H + h;
+  const uint32_t load_bytes = static_cast<uint32_t>(lay.rec.load_bytes);
+  bf16* Sbf = reinterpret_cast<bf16*>(sm);
+  uint8_t* Rec = sm + int64_t(L) * TILE_S;
+  bf16* Vn = reinterpret_cast<bf16*>(Rec + lay.rec.load_bytes);
+  float* gsm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Vn) + TILE_QK);
+  float* Sg = p.fin + bh * L * TK * TV;
+  float* sc = p.scan + bh * p.ss.size;
+  const char* rec0 = ws + lay.chunks_off + bh * p.NT * lay.rec.size;
+
+  if (warp == 0) tmem_alloc(&tbase, kScanCols);
+  if (tid == 0) {
+    mbar_init(&bar_ld, 1);
+    mbar_init(&bar_mma, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  for (int64_t e = tid; e < int64_t(L) * TK * TV; e += kScanThreads)
+    Sg[e] = p.init ? p.init[bh * L * TK * TV + e] : 0.f;
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tb = tbase;
+  const uint32_t tS0 = tb;        // S0 [K lanes x V cols], fp32
+  const uint32_t tD = tb + 128;   // lanes +0: W.S0 (M=64); lanes +16: output (M=64)
+
+  // S0 into TMEM, bf16 copies of every level into shared memory.
+  {
+    const int k = 32 * quarter + lane;
+    for (int c16 = 0; c16 < 4; ++c16) {
+      const int v0 = 64 * half + 16 * c16;
+      float x[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) x[u] = Sg[k * TV + v0 + u];
+      tmem_st16(taddr(tS0, 32 * quarter, v0), x);
+    }
+    tmem_wait_st();
+  }
+  for (int l = 0; l < L; ++l) refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+
+  const uint32_t id_read = idesc_f16(64, 128, true, false, true);    // [64 x K] . [K x V]
+  const uint32_t id_state = idesc_f16(128, 128, true, true, true);   // K_tail^T [K x 64] . [64 x V]
+  uint32_t ph_ld = 0, ph_mma = 0;
+  if (tid == 0 && p.NT > 0) {
+    mbar_arrive_expect_tx(&bar_ld, load_bytes);
+    bulk_g2s(Rec, rec0, load_bytes, &bar_ld);
+  }
+  for (int n = 0; n < p.NT; ++n) {
+    const char* recg = rec0 + int64_t(n) * lay.rec.size;
+    if (!mbar_wait(&bar_ld, ph_ld)) abort_flag = 1;
+    ph_ld ^= 1;
+
+    // MMA1: W.S0 and the multi-level read (naive.py:376, 379, 382-385).
+    if (tid == 0) {
+      fence_after_sync();
+      mma_tile(tD, smem_u32(Rec + lay.rec.W), smem_u32(Sbf), TK, id_read, false);
+      for (int l = 0; l < L; ++l)
+        mma_tile(tD + (16u << 16), smem_u32(Rec + lay.rec.Q + l * TILE_QK),
+                 smem_u32(Sbf + l * TK * TV), TK, id_read, l > 0);
+      mma_commit(&bar_mma);
+    }
+    __syncwarp();
+
+    // Decay S0 in TMEM by e^(G_last) while MMA1 runs (naive.py:392, first term).
+    {
+      const int k = 32 * quarter + lane;
+      const float e = reinterpret_cast<const float*>(recg + lay.rec.eg)[k];
+      for (int c16 = 0; c16 < 4; ++c16) {
+        const uint32_t ta = taddr(tS0, 32 * quarter, 64 * half + 16 * c16);
+        float x[16];
+        tmem_ld16(ta, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 16; ++u) x[u] *= e;
+        tmem_st16(ta, x);
+      }
+      tmem_wait_st();
+    }
+    if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
+    ph_mma ^= 1;
+    fence_after_sync();
+
+    // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376).
+    {
+      const int i = 16 * quarter + lane;
+      const bf16* Ug = reinterpret_cast<const bf16*>(recg + lay.rec.U);
+      for (int c16 = 0; c16 < 4; ++c16) {
+        const int v0 = 64 * half + 16 * c16;
+        float x[16];
+        tmem_ld16(taddr(tD, 32 * quarter, v0), x);
+        tmem_wait_ld();
+        if (lane < 16) {
+          float u[16];
+          load8_raw(Ug, NGDN2_BF16, i * TV + v0, 1, u);
+          load8_raw(Ug, NGDN2_BF16, i * TV + v0 + 8, 1, u + 8);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) x[t] = u[t] - x[t];
+          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, v0, kC)) = pack8(x);
+          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, v0 + 8, kC)) = pack8(x + 8);
+        }
+      }
+    }
+    fence_proxy_async();
+    fence_before_sync();
+    __syncthreads();
+    if (abort_flag) break;
+
+    // MMA2: o += (mix0 scale A_qk) v_new; S0 += K_tail^T v_new (naive.py:379, 392).
+    if (tid == 0) {
+      fence_after_sync();
+      mma_tile(tD + (16u << 16), smem_u32(Rec + lay.rec.A), smem_u32(Vn), kC, id_read, true);
+      mma_tile(tS0, smem_u32(Rec + lay.rec.Kt), smem_u32(Vn), kC, id_state, true);
+      mma_commit(&bar_mma);
+    }
+    __syncwarp();
+    if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
+    ph_mma ^= 1;
+    fence_after_sync();
+    if (tid == 0 && n + 1 < p.NT) {
+      mbar_arrive_expect_tx(&bar_ld, load_bytes);
+      bulk_g2s(Rec, recg + lay.rec.size, load_bytes, &bar_ld);
+    }
+    bool fires = false;
+    for (int l = 1; l < L; ++l) fires |= ((n + 1) % p.firing[l]) == 0;
+    const bool write_master = fires || n + 1 == p.NT;
+
+    // E2: output rows (lanes 16..31) and the new S0 (all lanes).
+    {
+      const int i = 16 * quarter + lane - 16, t = n * kC + i;
+      for (int c16 = 0; c16 < 4; ++c16) {
+        const int v0 = 64 * half + 16 * c16;
+        float x[16];
+        tmem_ld16(taddr(tD, 32 * quarter, v0), x);
+        tmem_wait_ld();
+        if (lane >= 16 && t < p.T) {
+          const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + v0;
+          if (p.dtype == NGDN2_BF16) {
+            bf16* og = reinterpret_cast<bf16*>(p.o) + o;
+            *reinterpret_cast<uint4*>(og) = pack8(x);
+            *reinterpret_cast<uint4*>(og + 8) = pack8(x + 8);
+          } else {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) store_elem(p.o, o + u, x[u], p.dtype);
+          }
+        }
+      }
+      const int k = 32 * quarter + lane;
+      for (int c16 = 0; c16 < 4; ++c16) {
+        const int v0 = 64 * half + 16 * c16;
+        float x[16];
+        tmem_ld16(taddr(tS0, 32 * quarter, v0), x);
+        tmem_wait_ld();
+        *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, v0, TK)) = pack8(x);
+        *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, v0 + 8, TK)) = pack8(x + 8);
+        if (write_master) {
+#pragma unroll
+          for (int u = 0; u < 16; u += 4)
+            *reinterpret_cast<float4*>(Sg + k * TV + v0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
+        }
+      }
+    }
+    fence_proxy_async();
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (abort_flag) break;
+
+    // Promotions at this chunk's firings, bottom-up (naive.py:394-415).
+    if (fires) {
+      for (int l = 1; l < L; ++l) {
+        if ((n + 1) % p.firing[l] != 0) continue;
+        promote_simt(p, b, h, l, Sg, sc, gsm);
+        refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
+        fence_proxy_async();
+        __syncthreads();
+      }
+      fence_before_sync();
+      __syncthreads();
+      fence_after_sync();
+    }
+  }
+  if (abort_flag && tid == 0) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tb, kScanCols);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+static bool is16(int dt) { return dt == NGDN2_BF16 || dt == NGDN2_F16; }
+
+bool tc_supports(const ngdn2_fwd_args* a) {
+  if (a->K != TK || a->V != TV || a->L < 1 || a->L > 3) return false;
+  if (!is16(a->q_dtype) || !is16(a->k_dtype) || !is16(a->v_dtype) || !is16(a->b_dtype) ||
+      !is16(a->w_dtype) || !is16(a->dtype))
+    return false;
+  return true;
+}
+
+size_t tc_workspace_bytes(const FwdParams& p) { return size_t(tc_layout(p).total); }
+
+int num_launches_tc(const FwdParams& p) {
+  return (p.L > 1 ? 1 : 0) + (p.NT > 0 ? 1 : 0) + 1;
+}
+
+cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t stream) {
+  const TcLayout lay = tc_layout(p);
+  char* ws = static_cast<char*>(workspace);
+  p.params32 = reinterpret_cast<float*>(ws + lay.params32_off);
+  p.scan = reinterpret_cast<float*>(ws + lay.scan_off);
+  p.chunks = nullptr;
+  cudaError_t err;
+  if (stage == 0 || stage == 1) {
+    if ((err = launch_convert_params(p, stream)) != cudaSuccess) return err;
+    if (p.NT > 0) {
+      err = cudaFuncSetAttribute(prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kPrepSmem);
+      if (err != cudaSuccess) return err;
+      prep_tc_kernel<<<dim3(p.NT, p.H, p.B), kPrepThreads, kPrepSmem, stream>>>(p, lay, ws);
+      if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    }
+  }
+  if (stage == 0 || stage == 2) {
+    const int smem = int(scan_tc_smem(p.L, lay.rec));
+    err = cudaFuncSetAttribute(scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return err;
+    scan_tc_kernel<<<dim3(p.H, p.B), kScanThreads, smem, stream>>>(p, lay, ws);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  }
+  return cudaSuccess;
+}
 
 }  // namespace ngdn2

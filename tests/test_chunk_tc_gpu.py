@@ -1,0 +1,139 @@
+"""The tensor-core (tcgen05) forward against the CPU oracle: bf16/fp16
+inputs at K = V = 128, parity bar 2e-2 (max |got - ref| / max |ref|) on
+outputs and final states, the oracle running on the same cast-back inputs."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _util import LOWP_REL, OP_ARGS, rel_err
+from nested_recurrent_memory_b200 import FwdCall, chunk_nested_gdn2
+from nested_recurrent_memory_b200.synthetic import config_inputs, op_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(inp):
+    return {k: (v.cuda() if torch.is_tensor(v) and v.is_floating_point() else v)
+            for k, v in inp.items()}
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _oracle(inp, L, promotion="learned", initial_state=None):
+    a = {k: (_np(v) if torch.is_tensor(v) else v) for k, v in inp.items() if k in OP_ARGS}
+    init = _np(initial_state) if initial_state is not None else None
+    return oracle.chunk_forward(**a, L=L, initial_state=init, output_final_state=True,
+                                promotion=promotion)
+
+
+def _run(inp, L, path="tc", **kw):
+    call = FwdCall(**_dev(inp), L=L, path=path, **kw)
+    o, s = call.launch()
+    torch.cuda.synchronize()
+    assert call.path == path
+    return o, s
+
+
+@pytest.mark.parametrize("promotion", ["learned", "merge"])
+@pytest.mark.parametrize(("L", "firing", "T"), [
+    (1, (1,), 256), (2, (1, 2), 256), (3, (1, 2, 4), 512), (3, (1, 4, 16), 1024),
+])
+def test_config_recipe_bf16(L, firing, T, promotion):
+    inp = config_inputs(2, T, 2, 128, 128, L, 64, firing, dtype=torch.bfloat16, seed=5,
+                        gate_proj_std=128 ** -0.5)
+    inp.pop("L")
+    o, s = _run(inp, L, promotion=promotion)
+    ro, rs = _oracle(inp, L, promotion)
+    assert rel_err(_np(o), ro) < LOWP_REL
+    assert rel_err(_np(s), rs) < LOWP_REL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_reference_recipe_k128(dtype):
+    """tests/ops/test_chunk.py case (1, 256, 2, 128, 128, 2, 16, (1, 2)) in 16-bit."""
+    inp = op_inputs(1, 256, 2, 128, 128, 2, 16, firing_intervals=(1, 2), dtype=dtype)
+    L = inp.pop("L")
+    o, s = _run(inp, L)
+    assert o.dtype == dtype
+    ro, rs = _oracle(inp, L)
+    assert rel_err(_np(o), ro) < LOWP_REL
+    assert rel_err(_np(s), rs) < LOWP_REL
+
+
+@pytest.mark.parametrize("T", [64, 100, 200, 320])
+def test_ragged_and_short(T):
+    inp = config_inputs(1, T, 2, 128, 128, 3, 32, (1, 2, 4), dtype=torch.bfloat16, seed=2)
+    inp.pop("L")
+    o, s = _run(inp, 3)
+    ro, rs = _oracle(inp, 3)
+    assert rel_err(_np(o), ro) < LOWP_REL
+    assert rel_err(_np(s), rs) < LOWP_REL
+
+
+def test_initial_state():
+    inp = config_inputs(2, 256, 2, 128, 128, 3, 64, (1, 2, 4), dtype=torch.bfloat16, seed=3)
+    inp.pop("L")
+    init = torch.randn(2, 2, 3, 128, 128, generator=torch.Generator().manual_seed(4)) * 0.1
+    o, s = _run(inp, 3, initial_state=init.cuda())
+    ro, rs = _oracle(inp, 3, initial_state=init)
+    assert rel_err(_np(o), ro) < LOWP_REL
+    assert rel_err(_np(s), rs) < LOWP_REL
+
+
+def test_strong_decay_stays_finite_and_close():
+    """Per-channel log-decays down to about -1.3 per token (a decay of e^-80
+    over a chunk): the per-block reference points keep every factor finite."""
+    inp = op_inputs(1, 256, 2, 128, 128, 2, 16, firing_intervals=(1, 2), dtype=torch.bfloat16)
+    L = inp.pop("L")
+    inp["g"] = (inp["g"].float() * 1.6).to(torch.bfloat16)
+    o, s = _run(inp, L)
+    assert torch.isfinite(o).all() and torch.isfinite(s).all()
+    ro, rs = _oracle(inp, L)
+    assert rel_err(_np(o), ro) < LOWP_REL
+    assert rel_err(_np(s), rs) < LOWP_REL
+
+
+def test_tc_agrees_with_simt():
+    inp = config_inputs(1, 512, 4, 128, 128, 3, 64, (1, 2, 4), dtype=torch.bfloat16, seed=9)
+    inp.pop("L")
+    o1, s1 = _run(inp, 3, path="tc")
+    o2, s2 = _run(inp, 3, path="simt")
+    assert rel_err(_np(o1), _np(o2)) < LOWP_REL
+    assert rel_err(_np(s1), _np(s2)) < LOWP_REL
+
+
+def test_auto_selects_tc_and_is_repeatable():
+    inp = config_inputs(1, 256, 2, 128, 128, 2, 32, (1, 2), dtype=torch.bfloat16, seed=6)
+    inp.pop("L")
+    d = _dev(inp)
+    o1, s1 = chunk_nested_gdn2(**d, L=2, output_final_state=True)
+    o2, s2 = chunk_nested_gdn2(**d, L=2, output_final_state=True)
+    from nested_recurrent_memory_b200 import last_path
+    assert last_path() == "tc"
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+def test_broadcast_gates_match_dense():
+    kw = dict(dtype=torch.bfloat16, seed=8)
+    dense = config_inputs(1, 256, 2, 128, 128, 2, 16, (1, 2), **kw)
+    bcast = config_inputs(1, 256, 2, 128, 128, 2, 16, (1, 2), dense_gates=False, **kw)
+    dense.pop("L")
+    bcast.pop("L")
+    o1, s1 = _run(dense, 2)
+    o2, s2 = _run(bcast, 2)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+def test_status_word_stays_clear():
+    inp = config_inputs(1, 256, 2, 128, 128, 2, 16, (1, 2), dtype=torch.bfloat16, seed=8)
+    inp.pop("L")
+    call = FwdCall(**_dev(inp), L=2, path="tc")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    call.args.status = status.data_ptr()
+    call.launch()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
