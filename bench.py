@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--path", choices=("auto", "simt", "tc"), default="auto")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the per-GPU batch (profiling runs on a smaller case)")
     return ap.parse_args()
 
 
@@ -374,6 +376,8 @@ def run_ours(args, w):
 def main():
     args = parse_args()
     w = workload(args.config)
+    if args.batch is not None:
+        w["B"] = args.batch
     if args.impl == "reference":
         run_reference(args, w)
     else:

@@ -61,21 +61,34 @@ struct TcRecord {
   }
 };
 
+// Promotion operands of one (level, head), bf16, in the scan's shared-memory
+// layouts: the query bank as a K-major A operand padded to 64 or 128 rows
+// with zeros, and the two B operands of the gate GEMMs
+// [W_k^T | W_b] and [W_w | W_g] (N = 256 each, K-major over V).
+constexpr int64_t PT_QB = 0;
+constexpr int64_t PT_W2A = 32768;
+constexpr int64_t PT_W2B = PT_W2A + 65536;
+constexpr int64_t PT_SIZE = PT_W2B + 65536;
+
 struct TcLayout {
   TcRecord rec;
-  int64_t params32_off, chunks_off, scan_off, total;
+  int64_t params32_off, ptc_off, chunks_off, scan_off, total;
 };
 
 __host__ __device__ inline TcLayout tc_layout(const FwdParams& p) {
   TcLayout t;
   t.rec = TcRecord::make(p.L);
   t.params32_off = 0;
-  t.chunks_off = (p.pl.size * 4 + 255) & ~int64_t(255);
+  t.ptc_off = (p.pl.size * 4 + 255) & ~int64_t(255);
+  t.chunks_off = t.ptc_off + int64_t(p.L > 1 ? p.L - 1 : 0) * p.H * PT_SIZE;
   t.scan_off = t.chunks_off + int64_t(p.B) * p.H * p.NT * t.rec.size;
   t.scan_off = (t.scan_off + 255) & ~int64_t(255);
   t.total = t.scan_off + int64_t(p.B) * p.H * p.ss.size * 4;
   return t;
 }
+
+// Rows of the promotion MMAs for ``nq`` pairs: 64 or 128.
+__host__ __device__ inline int pad_pairs(int nq) { return nq <= 64 ? 64 : 128; }
 
 __device__ __forceinline__ void set_status(const FwdParams& p, int bits) {
   if (p.status) atomicOr(p.status, bits);
@@ -137,6 +150,51 @@ __device__ __forceinline__ uint4 pack8(const float* x) {
 
 namespace ngdn2 {
 namespace {
+
+// ---------------------------------------------------------------------------
+// tc_params: grid (L-1, H). Promotion operands of each (level, head) in the
+// scan's shared-memory layouts (bf16), read by bulk copies at firings.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) tc_params_kernel(FwdParams p, TcLayout lay, char* ws) {
+  const int l = blockIdx.x + 1, h = blockIdx.y;
+  const int64_t pidx = int64_t(l - 1) * p.H + h;
+  char* base = ws + lay.ptc_off + pidx * PT_SIZE;
+  bf16* qb = reinterpret_cast<bf16*>(base + PT_QB);
+  bf16* w2a = reinterpret_cast<bf16*>(base + PT_W2A);
+  bf16* w2b = reinterpret_cast<bf16*>(base + PT_W2B);
+  const int nq = p.nq[l - 1], mp = pad_pairs(nq);
+  const int dt = p.param_dtype;
+  // Query bank rows past n_queries are ignored (probe.py:97): zero rows.
+  for (int it = threadIdx.x; it < mp * 16; it += blockDim.x) {
+    const int r = it >> 4, k0 = (it & 15) * 8;
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      x[u] = r < nq ? load_elem(p.raw_params[0], (pidx * p.n_max + r) * TK + k0 + u, dt) : 0.f;
+    *reinterpret_cast<uint4*>(qb + kmajor_off(r, k0, TK)) = pack8(x);
+  }
+  // B operands over the reduction index v: row n < 128 of W2A is W_k[n][:]
+  // (u = values . W_k^T, probe.py:99), row 128 + k is W_b[:][k]; W2B holds
+  // W_w[:][n] and W_g[:][k] (probe.py:60-62).
+  for (int it = threadIdx.x; it < 256 * 16; it += blockDim.x) {
+    const int n = it >> 4, v0 = (it & 15) * 8;
+    float xa[8], xb[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int v = v0 + u;
+      if (n < 128) {
+        xa[u] = load_elem(p.raw_params[1], (pidx * TK + n) * TV + v, dt);
+        xb[u] = load_elem(p.raw_params[3], (pidx * TV + v) * TV + n, dt);
+      } else {
+        xa[u] = load_elem(p.raw_params[2], (pidx * TV + v) * TK + (n - 128), dt);
+        xb[u] = load_elem(p.raw_params[4], (pidx * TV + v) * TK + (n - 128), dt);
+      }
+    }
+    *reinterpret_cast<uint4*>(w2a + kmajor_off(n, v0, TV)) = pack8(xa);
+    *reinterpret_cast<uint4*>(w2b + kmajor_off(n, v0, TV)) = pack8(xb);
+  }
+}
 
 // ---------------------------------------------------------------------------
 // prep_tc: grid (NT, H, B), 256 threads, two CTAs per SM.
@@ -453,11 +511,15 @@ namespace {
 // ---------------------------------------------------------------------------
 
 constexpr int kScanThreads = 256;
-constexpr int kScanCols = 256;          // TMEM: S0 in 0..127, chunk accumulators 128..255
+constexpr int kScanCols = 512;          // TMEM: S0 0..127, chunk accumulators 128..255, promotion 128..511
 constexpr int TILE_S = TK * TV * 2;     // bf16 state copy
+// Promotion scratch (the record region and what follows it): a 64 KB slot
+// for weights / gate partials / keys, and a 32 KB slot for the pairs.
+constexpr int kPromoScratch = 98304;
 
 __host__ __device__ inline int64_t scan_tc_smem(int L, const TcRecord& rec) {
-  return int64_t(L) * TILE_S + rec.load_bytes + TILE_QK + kGemmSmemFloats * 4;
+  const int64_t tail = rec.load_bytes + TILE_QK + kGemmSmemFloats * 4;
+  return int64_t(L) * TILE_S + (tail > kPromoScratch ? tail : kPromoScratch);
 }
 
 // fp32 master [K][V] -> bf16 MN-major B operand copy [Kd = K][N = V].
@@ -471,12 +533,238 @@ __device__ __forceinline__ void refresh_copy(bf16* dst, const float* src) {
   }
 }
 
+// Learned promotion of level l - 1 into level l on the tensor cores
+// (probe.py:69-102 with _gates :34-66, then update_fwd.py:120-123):
+//   P1  V'  = Q_bank . S_{l-1}
+//   P2b [w_logit | g_logit] = V' . [W_w | W_g]   -> v*w, g = mean(-softplus(. - 4))
+//   P2a [u | b_logit]       = V' . [W_k^T | W_b] -> keys = u / |u|, b = sigmoid(. - 4)
+//   P3  (keys * b * e^g) . S_l                    -> vn = v*w - that
+//   P4  S_l <- e^g S_l + keys^T . vn
+// fp32 accumulators in TMEM columns 128..511 (the chunk accumulators are
+// free between chunks); bf16 operands in ``X`` (the record buffer, reloaded
+// after the promotion). The fp32 master of S_l is in global memory.
+__device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* ws, int h, int l,
+                           uint32_t tb, bf16* Sbf, uint8_t* X, float* Sg, uint64_t* bar_ld,
+                           uint64_t* bar_mma, uint32_t& ph_ld, uint32_t& ph_mma, float* egp,
+                           float* nrm, int* abort_flag) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int nq = p.nq[l - 1], mp = pad_pairs(nq);
+  const char* pt = ws + lay.ptc_off + (int64_t(l - 1) * p.H + h) * PT_SIZE;
+  bf16* XW = reinterpret_cast<bf16*>(X);
+  bf16* XQ = reinterpret_cast<bf16*>(X + 65536);
+  float* Sl = Sg + int64_t(l) * TK * TV;
+  const uint32_t tV = tb + 128, tG = tb + 256, tS = tb + 384;
+  const int row = (mp == 128) ? 32 * quarter + lane : (lane < 16 ? 16 * quarter + lane : -1);
+  const uint32_t id_read = idesc_f16(mp, 128, true, false, true);
+  const uint32_t id_gate = idesc_f16(mp, 256, true, false, false);
+  const uint32_t id_upd = idesc_f16(128, 128, true, true, true);
+
+  // Query bank and [W_w | W_g] in.
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_ld, uint32_t(mp * 256 + 65536));
+    bulk_g2s(XQ, pt + PT_QB, uint32_t(mp * 256), bar_ld);
+    bulk_g2s(XW, pt + PT_W2B, 65536u, bar_ld);
+  }
+  if (!mbar_wait(bar_ld, ph_ld)) *abort_flag = 1;
+  ph_ld ^= 1;
+  // P1
+  if (tid == 0) {
+    fence_after_sync();
+    mma_tile(tV, smem_u32(XQ), smem_u32(Sbf + (l - 1) * TK * TV), TK, id_read, false);
+    mma_commit(bar_mma);
+  }
+  __syncwarp();
+  if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
+  ph_mma ^= 1;
+  fence_after_sync();
+  // V' -> bf16 A operand (over the bank, which P1 has consumed).
+  for (int c16 = 0; c16 < 4; ++c16) {
+    const int v0 = 64 * half + 16 * c16;
+    float x[16];
+    tmem_ld16(taddr(tV, 32 * quarter, v0), x);
+    tmem_wait_ld();
+    if (row >= 0) {
+      *reinterpret_cast<uint4*>(XQ + kmajor_off(row, v0, TV)) = pack8(x);
+      *reinterpret_cast<uint4*>(XQ + kmajor_off(row, v0 + 8, TV)) = pack8(x + 8);
+    }
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  // P2b
+  if (tid == 0) {
+    fence_after_sync();
+    mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    mma_commit(bar_mma);
+  }
+  __syncwarp();
+  if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
+  ph_mma ^= 1;
+  fence_after_sync();
+  // v * w back into TMEM; -softplus(g_logit - 4) per pair into shared memory
+  // (columns XOR-swizzled by row so both the row writes and the column sums
+  // are free of bank conflicts).
+  float* gpart = reinterpret_cast<float*>(X);
+  for (int c16 = 0; c16 < 4; ++c16) {
+    const int c0 = 64 * half + 16 * c16;
+    float vp[16], wl[16], gl[16];
+    tmem_ld16(taddr(tV, 32 * quarter, c0), vp);
+    tmem_ld16(taddr(tG, 32 * quarter, c0), wl);
+    tmem_ld16(taddr(tG, 32 * quarter, 128 + c0), gl);
+    tmem_wait_ld();
+#pragma unroll
+    for (int u = 0; u < 16; ++u) vp[u] *= sigmoidf_(wl[u] + kWLogitInit);
+    tmem_st16(taddr(tV, 32 * quarter, c0), vp);
+    if (row >= 0) {
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -softplusf_(gl[u] + kGLogitInit);
+    }
+  }
+  tmem_wait_st();
+  __syncthreads();
+  if (tid < 128) {
+    float s = 0.f;
+    for (int r = 0; r < nq; ++r) s += gpart[r * 128 + (tid ^ (r & 31))];
+    egp[tid] = expf(s / float(nq));
+  }
+  fence_proxy_async();
+  __syncthreads();
+  // [W_k^T | W_b] in over the gate scratch.
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_ld, 65536u);
+    bulk_g2s(XW, pt + PT_W2A, 65536u, bar_ld);
+  }
+  if (!mbar_wait(bar_ld, ph_ld)) *abort_flag = 1;
+  ph_ld ^= 1;
+  // P2a
+  if (tid == 0) {
+    fence_after_sync();
+    mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    mma_commit(bar_mma);
+  }
+  __syncwarp();
+  if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
+  ph_mma ^= 1;
+  fence_after_sync();
+  // keys = u / max(|u|, 1e-12) (probe.py:100): row norms across both halves.
+  {
+    float ss = 0.f;
+    for (int c16 = 0; c16 < 4; ++c16) {
+      float x[16];
+      tmem_ld16(taddr(tG, 32 * quarter, 64 * half + 16 * c16), x);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 16; ++u) ss = fmaf(x[u], x[u], ss);
+    }
+    if (row >= 0) nrm[half * 128 + row] = ss;
+  }
+  __syncthreads();
+  bf16* keysT = XW;                      // MN-major A: keys^T [K x mp]
+  bf16* kbg = XW + 16384;                // K-major A: keys * b * e^g [mp x K]
+  {
+    const float den = row >= 0 ? fmaxf(sqrtf(nrm[row] + nrm[128 + row]), 1e-12f) : 1.f;
+    for (int c16 = 0; c16 < 4; ++c16) {
+      const int k0 = 64 * half + 16 * c16;
+      float u[16], bl[16];
+      tmem_ld16(taddr(tG, 32 * quarter, k0), u);
+      tmem_ld16(taddr(tG, 32 * quarter, 128 + k0), bl);
+      tmem_wait_ld();
+      if (row >= 0) {
+        float kk[16], kb[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          kk[t] = u[t] / den;
+          kb[t] = kk[t] * sigmoidf_(bl[t] + kBLogitInit) * egp[k0 + t];
+        }
+        *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, k0, mp)) = pack8(kk);
+        *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, k0 + 8, mp)) = pack8(kk + 8);
+        *reinterpret_cast<uint4*>(kbg + kmajor_off(row, k0, TK)) = pack8(kb);
+        *reinterpret_cast<uint4*>(kbg + kmajor_off(row, k0 + 8, TK)) = pack8(kb + 8);
+      }
+    }
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  // P3: (keys * b * e^g) . S_l; meanwhile e^g * S_l (fp32 master) into TMEM.
+  if (tid == 0) {
+    fence_after_sync();
+    mma_tile(tG, smem_u32(kbg), smem_u32(Sbf + l * TK * TV), TK, id_read, false);
+    mma_commit(bar_mma);
+  }
+  __syncwarp();
+  {
+    const int k = 32 * quarter + lane;
+    const float e = egp[k];
+    for (int c16 = 0; c16 < 4; ++c16) {
+      const int v0 = 64 * half + 16 * c16;
+      float x[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) x[u] = Sl[k * TV + v0 + u] * e;
+      tmem_st16(taddr(tS, 32 * quarter, v0), x);
+    }
+    tmem_wait_st();
+  }
+  if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
+  ph_mma ^= 1;
+  fence_after_sync();
+  // vn = v * w - (keys * b * e^g) . S_l -> MN-major B operand [mp x V].
+  for (int c16 = 0; c16 < 4; ++c16) {
+    const int v0 = 64 * half + 16 * c16;
+    float vw[16], d[16];
+    tmem_ld16(taddr(tV, 32 * quarter, v0), vw);
+    tmem_ld16(taddr(tG, 32 * quarter, v0), d);
+    tmem_wait_ld();
+    if (row >= 0) {
+#pragma unroll
+      for (int u = 0; u < 16; ++u) vw[u] -= d[u];
+      *reinterpret_cast<uint4*>(XQ + mnmajor_off(row, v0, mp)) = pack8(vw);
+      *reinterpret_cast<uint4*>(XQ + mnmajor_off(row, v0 + 8, mp)) = pack8(vw + 8);
+    }
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  // P4: S_l += keys^T . vn
+  if (tid == 0) {
+    fence_after_sync();
+    mma_tile(tS, smem_u32(keysT), smem_u32(XQ), mp, id_upd, true);
+    mma_commit(bar_mma);
+  }
+  __syncwarp();
+  if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
+  ph_mma ^= 1;
+  fence_after_sync();
+  {
+    const int k = 32 * quarter + lane;
+    for (int c16 = 0; c16 < 4; ++c16) {
+      const int v0 = 64 * half + 16 * c16;
+      float x[16];
+      tmem_ld16(taddr(tS, 32 * quarter, v0), x);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 16; u += 4)
+        *reinterpret_cast<float4*>(Sl + k * TV + v0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
+      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0, TK)) = pack8(x);
+      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0 + 8, TK)) = pack8(x + 8);
+    }
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+}
+
 __global__ void __launch_bounds__(kScanThreads, 1)
 scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ uint64_t bar_ld, bar_mma;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
+  __shared__ float egp[128];
+  __shared__ float nrm[256];
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = p.L;
@@ -603,12 +891,14 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
-    if (tid == 0 && n + 1 < p.NT) {
+    bool fires = false;
+    for (int l = 1; l < L; ++l) fires |= ((n + 1) % p.firing[l]) == 0;
+    // The next record streams in during the epilogue, unless a promotion
+    // needs the record buffer as scratch first.
+    if (tid == 0 && n + 1 < p.NT && !fires) {
       mbar_arrive_expect_tx(&bar_ld, load_bytes);
       bulk_g2s(Rec, recg + lay.rec.size, load_bytes, &bar_ld);
     }
-    bool fires = false;
-    for (int l = 1; l < L; ++l) fires |= ((n + 1) % p.firing[l]) == 0;
     const bool write_master = fires || n + 1 == p.NT;
 
     // E2: output rows (lanes 16..31) and the new S0 (all lanes).
@@ -656,14 +946,24 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     if (fires) {
       for (int l = 1; l < L; ++l) {
         if ((n + 1) % p.firing[l] != 0) continue;
-        promote_simt(p, b, h, l, Sg, sc, gsm);
-        refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
-        fence_proxy_async();
-        __syncthreads();
+        if (p.promotion == NGDN2_PROMOTION_MERGE) {
+          promote_simt(p, b, h, l, Sg, sc, gsm);
+          refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
+          fence_proxy_async();
+          __syncthreads();
+        } else {
+          promote_tc(p, lay, ws, h, l, tb, Sbf, Rec, Sg, &bar_ld, &bar_mma, ph_ld, ph_mma, egp,
+                     nrm, &abort_flag);
+        }
       }
       fence_before_sync();
       __syncthreads();
       fence_after_sync();
+      if (abort_flag) break;
+      if (tid == 0 && n + 1 < p.NT) {
+        mbar_arrive_expect_tx(&bar_ld, load_bytes);
+        bulk_g2s(Rec, recg + lay.rec.size, load_bytes, &bar_ld);
+      }
     }
   }
   if (abort_flag && tid == 0) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
@@ -691,7 +991,7 @@ bool tc_supports(const ngdn2_fwd_args* a) {
 size_t tc_workspace_bytes(const FwdParams& p) { return size_t(tc_layout(p).total); }
 
 int num_launches_tc(const FwdParams& p) {
-  return (p.L > 1 ? 1 : 0) + (p.NT > 0 ? 1 : 0) + 1;
+  return (p.L > 1 ? 2 : 0) + (p.NT > 0 ? 1 : 0) + 1;
 }
 
 cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t stream) {
@@ -703,6 +1003,10 @@ cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t 
   cudaError_t err;
   if (stage == 0 || stage == 1) {
     if ((err = launch_convert_params(p, stream)) != cudaSuccess) return err;
+    if (p.L > 1) {
+      tc_params_kernel<<<dim3(p.L - 1, p.H), 256, 0, stream>>>(p, lay, ws);
+      if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    }
     if (p.NT > 0) {
       err = cudaFuncSetAttribute(prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kPrepSmem);
