@@ -172,6 +172,21 @@ NGDN2_API int ngdn2_fwd_num_launches(const ngdn2_fwd_args* args);
 /* The promotion write scan on its own. */
 NGDN2_API int ngdn2_update_state(const ngdn2_update_args* args, void* stream);
 
+/* Capacity of the fixed scratch buffer behind ngdn2_fwd_noalloc. */
+#define NGDN2_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/* The forward without a caller workspace and without any allocation: for
+ * callers that cannot allocate device memory per call (a host process that
+ * owns all device memory through its own pool, a serving loop whose memory
+ * budget is fixed at start-up). It has no counterpart in the reference.
+ * args->workspace and args->workspace_bytes are ignored; scratch comes from
+ * one buffer of NGDN2_NOALLOC_SCRATCH_BYTES compiled into the library, held
+ * on every GPU that loads it until exit. Calls needing more scratch than
+ * that return NGDN2_ERR_WORKSPACE. All calls on a device share the buffer,
+ * so calls that overlap on the GPU race; the first call on each device
+ * looks the buffer up and should come before any stream capture. */
+NGDN2_API int ngdn2_fwd_noalloc(const ngdn2_fwd_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

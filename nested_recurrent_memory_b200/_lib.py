@@ -68,6 +68,7 @@ EXPORTS = (
     "ngdn2_abi_version", "ngdn2_sizeof_fwd_args", "ngdn2_sizeof_update_args",
     "ngdn2_error_string", "ngdn2_fwd_workspace_size", "ngdn2_fwd_select_path",
     "ngdn2_fwd", "ngdn2_fwd_stage", "ngdn2_fwd_num_launches", "ngdn2_update_state",
+    "ngdn2_fwd_noalloc",
 )
 
 _LIB = None
@@ -101,6 +102,8 @@ def load(path: str | os.PathLike | None = None):
     lib.ngdn2_fwd_num_launches.restype = ctypes.c_int
     lib.ngdn2_update_state.argtypes = [ctypes.POINTER(UpdateArgs), c_ptr]
     lib.ngdn2_update_state.restype = ctypes.c_int
+    lib.ngdn2_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), c_ptr]
+    lib.ngdn2_fwd_noalloc.restype = ctypes.c_int
     if path is None:
         _LIB = lib
     return lib
