@@ -72,7 +72,7 @@ constexpr int64_t PT_SIZE = PT_W2B + 65536;
 
 struct TcLayout {
   TcRecord rec;
-  int64_t params32_off, ptc_off, chunks_off, scan_off, total;
+  int64_t params32_off, ptc_off, chunks_off, scan_off, mast_off, total;
 };
 
 __host__ __device__ inline TcLayout tc_layout(const FwdParams& p) {
@@ -83,7 +83,10 @@ __host__ __device__ inline TcLayout tc_layout(const FwdParams& p) {
   t.chunks_off = t.ptc_off + int64_t(p.L > 1 ? p.L - 1 : 0) * p.H * PT_SIZE;
   t.scan_off = t.chunks_off + int64_t(p.B) * p.H * p.NT * t.rec.size;
   t.scan_off = (t.scan_off + 255) & ~int64_t(255);
-  t.total = t.scan_off + int64_t(p.B) * p.H * p.ss.size * 4;
+  t.mast_off = t.scan_off + int64_t(p.B) * p.H * p.ss.size * 4;
+  t.mast_off = (t.mast_off + 255) & ~int64_t(255);
+  // fp32 masters of levels >= 1, transposed [V][K], per (b, h)
+  t.total = t.mast_off + int64_t(p.B) * p.H * (p.L > 1 ? p.L - 1 : 0) * TK * TV * 4;
   return t;
 }
 
@@ -92,6 +95,14 @@ __host__ __device__ inline int pad_pairs(int nq) { return nq <= 64 ? 64 : 128; }
 
 __device__ __forceinline__ void set_status(const FwdParams& p, int bits) {
   if (p.status) atomicOr(p.status, bits);
+}
+
+// Gate activations of the promotion on the tensor-core path, from the fast
+// hardware exponential / logarithm / reciprocal (outputs feed bf16 MMA
+// operands or fp32 decays averaged over pairs).
+__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.f + __expf(-x)); }
+__device__ __forceinline__ float fast_softplus(float x) {
+  return x > 20.f ? x : __logf(1.f + __expf(x));
 }
 
 // 8 consecutive elements starting at element offset ``o`` (element stride
@@ -131,6 +142,32 @@ __device__ __forceinline__ void load8(const TokView& tv, int b, int t, int h, in
 
 __device__ __forceinline__ void load8q(const QView& qv, int b, int t, int h, int l, int d, float* out) {
   load8_raw(qv.p, qv.dt, qv.off(b, t, h, l, d), qv.sd, out);
+}
+
+// 8 consecutive 16-bit elements of a token row as their raw 16 bytes: one
+// vector load when contiguous and aligned, else element loads re-packed in
+// the tensor's own 16-bit format (exact).
+__device__ __forceinline__ uint4 raw8_at(const void* p, int dt, int64_t o, int64_t sd) {
+  if (sd == 1 && (o & 7) == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0)
+    return __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + o));
+  uint4 r;
+  uint16_t* h = reinterpret_cast<uint16_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = reinterpret_cast<const uint16_t*>(p)[o + i * sd];
+  (void)dt;
+  return r;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& raw, int dt, float* out) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f;
+    if (dt == NGDN2_BF16) f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    else f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
 }
 
 // Pack 8 floats as 8 bf16 (16 bytes).
@@ -203,17 +240,16 @@ __global__ void __launch_bounds__(256) tc_params_kernel(FwdParams p, TcLayout la
 constexpr int kPrepThreads = 256;
 constexpr int kPrepCols = 256;  // TMEM columns
 
-// Shared-memory plan (bytes). Phase 1 (operands of the A_qk / A_kk MMAs)
-// and phase 2 (inverse and the [U | W] MMA) share one region.
-constexpr int P_G = 0;                   // fp32 [64][128] cumulative log-decay
-constexpr int P_R0 = 32768;
-constexpr int P_KG = P_R0;               // K^(J), J = 0..3: 20 groups of 8 rows x 128, K-major
-constexpr int P_QB = P_R0 + 40960;       // 4 x [32 x 128] K-major: 16 query rows, 16 b*k rows
-constexpr int P_AF = P_R0;               // fp32 [64][65] strictly lower A_kk
+// Shared-memory plan (bytes). Phase 1 holds the operands of the A_qk / A_kk
+// MMAs and the B operand of the [U | W] MMA; phase 2 reuses the first region
+// for the inverse.
+constexpr int P_KG = 0;                  // K^(J), J = 0..3: 20 groups of 8 rows x 128, K-major
+constexpr int P_QB = 40960;              // 4 x [32 x 128] K-major: 16 query rows, 16 b*k rows
+constexpr int P_AF = 0;                  // fp32 [64][65] strictly lower A_kk
 constexpr int P_XF = P_AF + 16640;       // fp32 [64][65] (I + A_kk)^-1
-constexpr int P_R = P_XF + 16640;        // bf16 [64 x 256] MN-major [w*v | k*b*e^G]
-constexpr int P_XB = P_R + 32768;        // bf16 [64 x 64] K-major inverse
-constexpr int kPrepSmem = P_XB + 8192;   // 107008
+constexpr int P_XB = P_XF + 16640;       // bf16 [64 x 64] K-major: staged A_qk, then the inverse
+constexpr int P_R = 73728;               // bf16 [64 x 256] MN-major [w*v | k*b*e^G]
+constexpr int kPrepSmem = P_R + 32768;   // 106496
 
 // Row-group offset (in elements) of K^(J) inside the P_KG region: K^(J)
 // keeps rows 0 .. 16J+15 (later rows are never needed), so the four tiles
@@ -223,14 +259,20 @@ __device__ __forceinline__ int kgroup_elems(int J) {
   return (J == 0 ? 0 : J == 1 ? 2 : J == 2 ? 6 : 12) * 1024;
 }
 
+__device__ __forceinline__ void scale8(float* x, float s) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u) x[u] *= s;
+}
+
 __global__ void __launch_bounds__(kPrepThreads, 2)
 prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tbase;
-  __shared__ float mix0s[kC];
+  __shared__ float mixs[3][kC];             // mix_l * scale per row
+  __shared__ __align__(16) float tot[TK];   // G[31] (carry into rows 32..63)
+  __shared__ __align__(16) float rho[5][TK];  // G[16J + 7] for J = 0..3, then G[63]
   __shared__ float Tt[3 * 256];
-  float* Gs = reinterpret_cast<float*>(sm + P_G);
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = n * kC;
@@ -241,78 +283,177 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
-  if (tid < kC) mix0s[tid] = (t0 + tid < p.T) ? p.mix.at(b, t0 + tid, h, 0) : 0.f;
+  if (tid < kC * p.L) {
+    const int l = tid / kC, i = tid % kC;
+    mixs[l][i] = (t0 + i < p.T) ? p.mix.at(b, t0 + i, h, l) * p.scale : 0.f;
+  }
 
-  // 1. G = cumsum of g along the chunk (naive.py:329); zero past T.
-  {
-    const int d = tid & 127, half = tid >> 7;
-    float gv[32];
-    float acc = 0.f;
+  // Phase A mapping: lanes are rows (32 * rh + lane), each warp owns four
+  // 8-column chunks. 16-byte stores of 8 consecutive rows then fill one
+  // contiguous 128-byte core matrix, so shared stores are conflict-free and
+  // global stores coalesce.
+  const int rh = warp & 1, cw = warp >> 1;
+  const int r = 32 * rh + lane, t = t0 + r;
+  const bool valid = t < p.T;
+
+  // A1. G = cumsum of g along the chunk (naive.py:329): a warp scan over
+  //     lanes for each of this thread's 32 columns, plus the carry from rows
+  //     0..31 into rows 32..63.
+  float G[4][8];
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      const int t = t0 + half * 32 + r;
-      acc += (t < p.T) ? p.g.at(b, t, h, d) : 0.f;
-      gv[r] = acc;
-    }
-    if (half == 0) {
+  for (int ci = 0; ci < 4; ++ci) {
+    const int d0 = 8 * (cw + 4 * ci);
+    if (valid) load8(p.g, b, t, h, d0, G[ci]);
+    else {
 #pragma unroll
-      for (int r = 0; r < 32; ++r) Gs[r * 128 + d] = gv[r];
-    }
-    __syncthreads();
-    if (half == 1) {
-      const float base = Gs[31 * 128 + d];
-#pragma unroll
-      for (int r = 0; r < 32; ++r) Gs[(32 + r) * 128 + d] = gv[r] + base;
+      for (int u = 0; u < 8; ++u) G[ci][u] = 0.f;
     }
   }
-  fence_before_sync();
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float y = __shfl_up_sync(0xffffffffu, G[ci][u], off);
+        if (lane >= off) G[ci][u] += y;
+      }
+  }
+  if (rh == 0 && lane == 31) {
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) tot[8 * (cw + 4 * ci) + u] = G[ci][u];
+  }
   __syncthreads();
-  fence_after_sync();
+  if (rh == 1) {
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) G[ci][u] += tot[8 * (cw + 4 * ci) + u];
+  }
+  // Reference points rho_J = G[16J + 7] (rows 7, 23, 39, 55) and G[63].
+  if (lane == 7 || lane == 23 || (rh == 1 && lane == 31)) {
+    const int slot = lane == 31 ? 4 : 2 * rh + (lane == 23);
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) rho[slot][8 * (cw + 4 * ci) + u] = G[ci][u];
+  }
+  __syncthreads();
   const uint32_t tb = tbase;
 
-  // 2. Operands of the A_qk / A_kk MMAs. Row block I of queries uses the
-  //    reference point rho_I = G[16I + 7] (per channel):
-  //      Q_I[i]  = q_i * e^(G_i - rho_I),  BK_I[i] = b_i * k_i * e^(G_i - rho_I)
-  //      K^(J)[j] = k_j * e^(rho_J - G_j) for j <= 16J + 15
-  //    so Q_I[i] . K^(I)[j] = q_i . k_j e^(G_i - G_j) with both factors
-  //    bounded by the decay over 8 tokens (naive.py:335-344, 377-378).
+  // A2. Operands. Row block I of queries uses rho_I so that
+  //       Q_I[i] . K^(I)[j] = q_i . k_j e^(G_i - G_j)
+  //     with Q_I[i] = q_i e^(G_i - rho_I), K^(J)[j] = k_j e^(rho_J - G_j):
+  //     every factor is bounded by the decay over 8 tokens
+  //     (naive.py:335-344, 377-378). The record gets the read queries, K_tail
+  //     and e^(G_last); R = [w * v | k * b * e^G] is the B operand of the
+  //     [U | W] MMA (naive.py:346-352).
   bf16* KG = reinterpret_cast<bf16*>(sm + P_KG);
   bf16* QB = reinterpret_cast<bf16*>(sm + P_QB);
-  for (int it = tid; it < kC * 16; it += kPrepThreads) {
-    const int r = it >> 4, d0 = (it & 15) * 8, t = t0 + r;
-    float kk[8], qq[8], bb[8], G[8], o1[8], o2[8];
-    if (t < p.T) {
-      load8(p.k, b, t, h, d0, kk);
-      load8q(p.q, b, t, h, 0, d0, qq);
-      load8(p.b, b, t, h, d0, bb);
+  bf16* Rs = reinterpret_cast<bf16*>(sm + P_R);
+  bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
+  bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
+  const int I = r >> 4;
+  // Raw 16-byte chunks of q_0, k, b, v, w, q_1, q_2 for one column chunk;
+  // the next chunk's loads are issued before the current one is used.
+  auto fetch = [&](int ci, uint4* raw) {
+    const int d0 = 8 * (cw + 4 * ci);
+    if (valid) {
+      raw[0] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, 0, d0), p.q.sd);
+      raw[1] = raw8_at(p.k.p, p.k.dt, p.k.off(b, t, h, d0), p.k.sd);
+      raw[2] = raw8_at(p.b.p, p.b.dt, p.b.off(b, t, h, d0), p.b.sd);
+      raw[3] = raw8_at(p.v.p, p.v.dt, p.v.off(b, t, h, d0), p.v.sd);
+      raw[4] = raw8_at(p.w.p, p.w.dt, p.w.off(b, t, h, d0), p.w.sd);
+#pragma unroll
+      for (int l = 1; l < 3; ++l)
+        if (l < p.L) raw[4 + l] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, l, d0), p.q.sd);
     } else {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) kk[u] = qq[u] = bb[u] = 0.f;
+      for (int i = 0; i < 7; ++i) raw[i] = make_uint4(0, 0, 0, 0);
     }
+  };
+  uint4 cur[7], nxt[7];
+  fetch(0, cur);
 #pragma unroll
-    for (int u = 0; u < 8; ++u) G[u] = Gs[r * 128 + d0 + u];
-    const int I = r >> 4;
+  for (int ci = 0; ci < 4; ++ci) {
+    if (ci < 3) fetch(ci + 1, nxt);
+    const int d0 = 8 * (cw + 4 * ci);
+    float qq[8], kk[8], bb[8], o1[8], o2[8], rr[8], gl[8];
+    unpack8(cur[0], p.q.dt, qq);
+    unpack8(cur[1], p.k.dt, kk);
+    unpack8(cur[2], p.b.dt, bb);
+    const float* g = G[ci];
+    {
+      const float4* rp = reinterpret_cast<const float4*>(&rho[I][d0]);
+      const float4* gp = reinterpret_cast<const float4*>(&rho[4][d0]);
+      const float4 a0 = rp[0], a1 = rp[1], c0 = gp[0], c1 = gp[1];
+      rr[0] = a0.x; rr[1] = a0.y; rr[2] = a0.z; rr[3] = a0.w;
+      rr[4] = a1.x; rr[5] = a1.y; rr[6] = a1.z; rr[7] = a1.w;
+      gl[0] = c0.x; gl[1] = c0.y; gl[2] = c0.z; gl[3] = c0.w;
+      gl[4] = c1.x; gl[5] = c1.y; gl[6] = c1.z; gl[7] = c1.w;
+    }
+    // Q_I, BK_I rows (MMA1 B operand)
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const float e = __expf(G[u] - Gs[(16 * I + 7) * 128 + d0 + u]);
+      const float e = __expf(g[u] - rr[u]);
       o1[u] = qq[u] * e;
       o2[u] = bb[u] * kk[u] * e;
     }
     bf16* tile = QB + I * (32 * 128);
     *reinterpret_cast<uint4*>(tile + kmajor_off(r & 15, d0, 128)) = pack8(o1);
     *reinterpret_cast<uint4*>(tile + kmajor_off(16 + (r & 15), d0, 128)) = pack8(o2);
+    // K^(J) rows for every J >= I (MMA1 A operands)
     for (int J = I; J < 4; ++J) {
+      const float4* rp = reinterpret_cast<const float4*>(&rho[J][d0]);
+      const float4 a0 = rp[0], a1 = rp[1];
+      const float rj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-      for (int u = 0; u < 8; ++u) o1[u] = kk[u] * __expf(Gs[(16 * J + 7) * 128 + d0 + u] - G[u]);
+      for (int u = 0; u < 8; ++u) o1[u] = kk[u] * __expf(rj[u] - g[u]);
       *reinterpret_cast<uint4*>(KG + kgroup_elems(J) + kmajor_off(r, d0, 128)) = pack8(o1);
     }
+    // e^G: level-0 read query and the k*b*e^G half of R; w*v half of R
+    {
+      float vv[8], ww[8];
+      unpack8(cur[3], p.v.dt, vv);
+      unpack8(cur[4], p.w.dt, ww);
+      const float m0 = mixs[0][r];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float e = __expf(g[u]);
+        o1[u] = m0 * qq[u] * e;
+        o2[u] = kk[u] * bb[u] * e;
+        ww[u] *= vv[u];
+      }
+      *reinterpret_cast<uint4*>(Qg + kmajor_off(r, d0, 128)) = pack8(o1);
+      *reinterpret_cast<uint4*>(Rs + mnmajor_off(r, 128 + d0, 64)) = pack8(o2);
+      *reinterpret_cast<uint4*>(Rs + mnmajor_off(r, d0, 64)) = pack8(ww);
+    }
+    // K_tail = k e^(G_last - G) as the MN-major A operand of K_tail^T . v_new
+#pragma unroll
+    for (int u = 0; u < 8; ++u) o1[u] = kk[u] * __expf(gl[u] - g[u]);
+    *reinterpret_cast<uint4*>(Ktg + mnmajor_off(r, d0, 64)) = pack8(o1);
+    // upper-level read queries mix_l * scale * q_l
+#pragma unroll
+    for (int l = 1; l < 3; ++l) {
+      if (l >= p.L) continue;
+      unpack8(cur[4 + l], p.q.dt, qq);
+      scale8(qq, mixs[l][r]);
+      *reinterpret_cast<uint4*>(Qg + l * (kC * 128) + kmajor_off(r, d0, 128)) = pack8(qq);
+    }
+    if (ci < 3) {
+#pragma unroll
+      for (int i = 0; i < 7; ++i) cur[i] = nxt[i];
+    }
   }
+  if (tid < TK) reinterpret_cast<float*>(rec + lay.rec.eg)[tid] = __expf(rho[4][tid]);
   fence_proxy_async();
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
 
-  // 3. MMA1: D[j, 32J + c] = K^(J)[j] . [Q_J ; BK_J][c], M=64, N=32, K=128.
+  // B. MMA1: D[j, 32J + c] = K^(J)[j] . [Q_J ; BK_J][c], M=64, N=32, K=128.
   if (tid == 0) {
     const uint32_t id = idesc_f16(64, 32, true, false, false);
     for (int J = 0; J < 4; ++J)
@@ -321,49 +462,14 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     mma_commit(&bar);
   }
   __syncwarp();
-
-  // 4. While MMA1 runs: read queries, K_tail and e^(G_last) into the record.
-  {
-    bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
-    bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
-    for (int it = tid; it < kC * 16; it += kPrepThreads) {
-      const int r = it >> 4, d0 = (it & 15) * 8, t = t0 + r;
-      const bool valid = t < p.T;
-      float qq[8], kk[8], out[8];
-      if (valid) {
-        load8q(p.q, b, t, h, 0, d0, qq);
-        load8(p.k, b, t, h, d0, kk);
-      } else {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) qq[u] = kk[u] = 0.f;
-      }
-      const float m0 = mix0s[r] * p.scale;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) out[u] = m0 * qq[u] * __expf(Gs[r * 128 + d0 + u]);
-      *reinterpret_cast<uint4*>(Qg + kmajor_off(r, d0, 128)) = pack8(out);
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        out[u] = kk[u] * __expf(Gs[63 * 128 + d0 + u] - Gs[r * 128 + d0 + u]);
-      *reinterpret_cast<uint4*>(Ktg + mnmajor_off(r, d0, 64)) = pack8(out);
-      for (int l = 1; l < p.L; ++l) {
-        if (valid) load8q(p.q, b, t, h, l, d0, qq);
-        const float ml = valid ? p.mix.at(b, t, h, l) * p.scale : 0.f;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) out[u] = ml * qq[u];
-        *reinterpret_cast<uint4*>(Qg + l * (kC * 128) + kmajor_off(r, d0, 128)) = pack8(out);
-      }
-    }
-    if (tid < 128)
-      reinterpret_cast<float*>(rec + lay.rec.eg)[tid] = __expf(Gs[63 * 128 + tid]);
-  }
-
   if (!mbar_wait(&bar, 0)) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
   fence_after_sync();
 
-  // 5. E1: masks; A_kk to shared fp32, mix0 * scale * A_qk to the record.
+  // C. Masks: A_kk to shared fp32, mix0 * scale * A_qk staged as a K-major
+  //    bf16 tile and copied to the record with 16-byte stores.
   float* Af = reinterpret_cast<float*>(sm + P_AF);
+  bf16* Xb = reinterpret_cast<bf16*>(sm + P_XB);
   {
-    bf16* Ag = reinterpret_cast<bf16*>(rec + lay.rec.A);
     const int q = warp & 3, ch = warp >> 2, j = 16 * q + lane;
     for (int c16 = 0; c16 < 4; ++c16) {
       float v[16];
@@ -382,77 +488,55 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const int i = 16 * J + c;
-            Ag[kmajor_off(i, j, 64)] =
-                __float2bfloat16_rn(j <= i ? v[c] * p.scale * mix0s[i] : 0.f);
+            Xb[kmajor_off(i, j, 64)] = __float2bfloat16_rn(j <= i ? v[c] * mixs[0][i] : 0.f);
           }
         }
       }
     }
   }
-
-  // 6. B operand of the [U | W] MMA: R = [w * v | k * b * e^G], MN-major.
-  bf16* Rs = reinterpret_cast<bf16*>(sm + P_R);
-  for (int it = tid; it < kC * 32; it += kPrepThreads) {
-    const int j = it >> 5, n0 = (it & 31) * 8, t = t0 + j;
-    float out[8];
-    if (t >= p.T) {
-#pragma unroll
-      for (int u = 0; u < 8; ++u) out[u] = 0.f;
-    } else if (n0 < 128) {
-      float vv[8], ww[8];
-      load8(p.v, b, t, h, n0, vv);
-      load8(p.w, b, t, h, n0, ww);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) out[u] = ww[u] * vv[u];
-    } else {
-      const int d0 = n0 - 128;
-      float kk[8], bb[8];
-      load8(p.k, b, t, h, d0, kk);
-      load8(p.b, b, t, h, d0, bb);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) out[u] = kk[u] * bb[u] * __expf(Gs[j * 128 + d0 + u]);
-    }
-    *reinterpret_cast<uint4*>(Rs + mnmajor_off(j, n0, 64)) = pack8(out);
-  }
   __syncthreads();
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(Xb);
+    uint4* dst = reinterpret_cast<uint4*>(rec + lay.rec.A);
+    for (int e = tid; e < TILE_A / 16; e += kPrepThreads) dst[e] = src[e];
+  }
 
-  // 7. (I + A_kk)^-1 in fp32: 16x16 diagonal blocks by forward substitution,
+  // D. (I + A_kk)^-1 in fp32: 16x16 diagonal blocks by forward substitution,
   //    then X_IJ = -X_II sum_{K=J}^{I-1} A_IK X_KJ block row by block row.
   float* Xf = reinterpret_cast<float*>(sm + P_XF);
   if (tid < 64) {
     const int o = 16 * (tid >> 4), c = tid & 15;
     float x[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float s = (r == c) ? 1.f : 0.f;
+    for (int rr = 0; rr < 16; ++rr) {
+      float s = (rr == c) ? 1.f : 0.f;
 #pragma unroll
-      for (int u = 0; u < r; ++u) s = fmaf(-Af[(o + r) * 65 + o + u], x[u], s);
-      x[r] = s;
+      for (int u = 0; u < rr; ++u) s = fmaf(-Af[(o + rr) * 65 + o + u], x[u], s);
+      x[rr] = s;
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) Xf[(o + r) * 65 + o + c] = x[r];
+    for (int rr = 0; rr < 16; ++rr) Xf[(o + rr) * 65 + o + c] = x[rr];
   }
   __syncthreads();
-  for (int I = 1; I < 4; ++I) {
-    for (int e = tid; e < I * 256; e += kPrepThreads) {
-      const int J = e >> 8, r = (e >> 4) & 15, c = e & 15;
+  for (int I2 = 1; I2 < 4; ++I2) {
+    for (int e = tid; e < I2 * 256; e += kPrepThreads) {
+      const int J = e >> 8, rr = (e >> 4) & 15, c = e & 15;
       float s = 0.f;
-      for (int K2 = J; K2 < I; ++K2)
+      for (int K2 = J; K2 < I2; ++K2)
 #pragma unroll
         for (int m = 0; m < 16; ++m)
-          s = fmaf(Af[(16 * I + r) * 65 + 16 * K2 + m], Xf[(16 * K2 + m) * 65 + 16 * J + c], s);
+          s = fmaf(Af[(16 * I2 + rr) * 65 + 16 * K2 + m], Xf[(16 * K2 + m) * 65 + 16 * J + c], s);
       Tt[e] = s;
     }
     __syncthreads();
-    for (int e = tid; e < I * 256; e += kPrepThreads) {
-      const int J = e >> 8, r = (e >> 4) & 15, c = e & 15;
+    for (int e = tid; e < I2 * 256; e += kPrepThreads) {
+      const int J = e >> 8, rr = (e >> 4) & 15, c = e & 15;
       float s = 0.f;
-      for (int m = 0; m <= r; ++m) s = fmaf(Xf[(16 * I + r) * 65 + 16 * I + m], Tt[(J << 8) + m * 16 + c], s);
-      Xf[(16 * I + r) * 65 + 16 * J + c] = -s;
+      for (int m = 0; m <= rr; ++m) s = fmaf(Xf[(16 * I2 + rr) * 65 + 16 * I2 + m], Tt[(J << 8) + m * 16 + c], s);
+      Xf[(16 * I2 + rr) * 65 + 16 * J + c] = -s;
     }
     __syncthreads();
   }
-  bf16* Xb = reinterpret_cast<bf16*>(sm + P_XB);
   for (int it = tid; it < kC * 8; it += kPrepThreads) {
     const int i = it >> 3, j0 = (it & 7) * 8;
     float x[8];
@@ -465,7 +549,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   __syncthreads();
   fence_after_sync();
 
-  // 8. MMA2: [U | W] = X . R, M=64, N=256, K=64 (naive.py:346-351).
+  // E. MMA2: [U | W] = X . R, M=64, N=256, K=64 (naive.py:346-351).
   if (tid == 0) {
     mma_tile(tb, smem_u32(Xb), smem_u32(Rs), 64, idesc_f16(64, 256, true, false, true), false);
     mma_commit(&bar);
@@ -474,7 +558,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   if (!mbar_wait(&bar, 1)) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
   fence_after_sync();
 
-  // 9. E2: U (row-major) and W (K-major A operand) to the record.
+  // F. U (row-major) and W (K-major A operand) to the record.
   {
     bf16* Ug = reinterpret_cast<bf16*>(rec + lay.rec.U);
     bf16* Wg = reinterpret_cast<bf16*>(rec + lay.rec.W);
@@ -542,9 +626,11 @@ __device__ __forceinline__ void refresh_copy(bf16* dst, const float* src) {
 //   P4  S_l <- e^g S_l + keys^T . vn
 // fp32 accumulators in TMEM columns 128..511 (the chunk accumulators are
 // free between chunks); bf16 operands in ``X`` (the record buffer, reloaded
-// after the promotion). The fp32 master of S_l is in global memory.
+// after the promotion). The fp32 master of S_l is in global memory,
+// transposed ([V][K]) so that lane-per-key TMEM traffic reads and writes it
+// in coalesced 128-byte rows.
 __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* ws, int h, int l,
-                           uint32_t tb, bf16* Sbf, uint8_t* X, float* Sg, uint64_t* bar_ld,
+                           uint32_t tb, bf16* Sbf, uint8_t* X, float* Mt, uint64_t* bar_ld,
                            uint64_t* bar_mma, uint32_t& ph_ld, uint32_t& ph_mma, float* egp,
                            float* nrm, int* abort_flag) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -553,7 +639,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   const char* pt = ws + lay.ptc_off + (int64_t(l - 1) * p.H + h) * PT_SIZE;
   bf16* XW = reinterpret_cast<bf16*>(X);
   bf16* XQ = reinterpret_cast<bf16*>(X + 65536);
-  float* Sl = Sg + int64_t(l) * TK * TV;
+  float* Sl = Mt + int64_t(l - 1) * TK * TV;  // fp32 master of level l, [V][K]
   const uint32_t tV = tb + 128, tG = tb + 256, tS = tb + 384;
   const int row = (mp == 128) ? 32 * quarter + lane : (lane < 16 ? 16 * quarter + lane : -1);
   const uint32_t id_read = idesc_f16(mp, 128, true, false, true);
@@ -614,12 +700,12 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
     tmem_ld16(taddr(tG, 32 * quarter, 128 + c0), gl);
     tmem_wait_ld();
 #pragma unroll
-    for (int u = 0; u < 16; ++u) vp[u] *= sigmoidf_(wl[u] + kWLogitInit);
+    for (int u = 0; u < 16; ++u) vp[u] *= fast_sigmoid(wl[u] + kWLogitInit);
     tmem_st16(taddr(tV, 32 * quarter, c0), vp);
     if (row >= 0) {
 #pragma unroll
       for (int u = 0; u < 16; ++u)
-        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -softplusf_(gl[u] + kGLogitInit);
+        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -fast_softplus(gl[u] + kGLogitInit);
     }
   }
   tmem_wait_st();
@@ -664,7 +750,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   bf16* keysT = XW;                      // MN-major A: keys^T [K x mp]
   bf16* kbg = XW + 16384;                // K-major A: keys * b * e^g [mp x K]
   {
-    const float den = row >= 0 ? fmaxf(sqrtf(nrm[row] + nrm[128 + row]), 1e-12f) : 1.f;
+    const float inv = row >= 0 ? __frcp_rn(fmaxf(sqrtf(nrm[row] + nrm[128 + row]), 1e-12f)) : 0.f;
     for (int c16 = 0; c16 < 4; ++c16) {
       const int k0 = 64 * half + 16 * c16;
       float u[16], bl[16];
@@ -675,8 +761,8 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
         float kk[16], kb[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          kk[t] = u[t] / den;
-          kb[t] = kk[t] * sigmoidf_(bl[t] + kBLogitInit) * egp[k0 + t];
+          kk[t] = u[t] * inv;
+          kb[t] = kk[t] * fast_sigmoid(bl[t] + kBLogitInit) * egp[k0 + t];
         }
         *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, k0, mp)) = pack8(kk);
         *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, k0 + 8, mp)) = pack8(kk + 8);
@@ -702,7 +788,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
       const int v0 = 64 * half + 16 * c16;
       float x[16];
 #pragma unroll
-      for (int u = 0; u < 16; ++u) x[u] = Sl[k * TV + v0 + u] * e;
+      for (int u = 0; u < 16; ++u) x[u] = Sl[(v0 + u) * TK + k] * e;
       tmem_st16(taddr(tS, 32 * quarter, v0), x);
     }
     tmem_wait_st();
@@ -745,8 +831,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
       tmem_ld16(taddr(tS, 32 * quarter, v0), x);
       tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 16; u += 4)
-        *reinterpret_cast<float4*>(Sl + k * TV + v0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
+      for (int u = 0; u < 16; ++u) Sl[(v0 + u) * TK + k] = x[u];
       *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0, TK)) = pack8(x);
       *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0 + 8, TK)) = pack8(x + 8);
     }
@@ -777,6 +862,10 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   float* gsm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Vn) + TILE_QK);
   float* Sg = p.fin + bh * L * TK * TV;
   float* sc = p.scan + bh * p.ss.size;
+  const bool learned = p.promotion != NGDN2_PROMOTION_MERGE;
+  // Learned promotions keep the upper levels' fp32 masters transposed in
+  // the workspace; merge promotions (CUDA cores) use final_state as is.
+  float* Mt = reinterpret_cast<float*>(ws + lay.mast_off) + bh * (L > 1 ? L - 1 : 0) * TK * TV;
   const char* rec0 = ws + lay.chunks_off + bh * p.NT * lay.rec.size;
 
   if (warp == 0) tmem_alloc(&tbase, kScanCols);
@@ -788,6 +877,12 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   }
   for (int64_t e = tid; e < int64_t(L) * TK * TV; e += kScanThreads)
     Sg[e] = p.init ? p.init[bh * L * TK * TV + e] : 0.f;
+  if (learned) {
+    for (int64_t e = tid; e < int64_t(L - 1) * TK * TV; e += kScanThreads) {
+      const int64_t l1 = e / (TK * TV), r2 = e % (TK * TV), v = r2 / TK, k = r2 % TK;
+      Mt[e] = p.init ? p.init[bh * L * TK * TV + (l1 + 1) * TK * TV + k * TV + v] : 0.f;
+    }
+  }
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -899,7 +994,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       mbar_arrive_expect_tx(&bar_ld, load_bytes);
       bulk_g2s(Rec, recg + lay.rec.size, load_bytes, &bar_ld);
     }
-    const bool write_master = fires || n + 1 == p.NT;
+    const bool write_master = (fires && !learned) || n + 1 == p.NT;
 
     // E2: output rows (lanes 16..31) and the new S0 (all lanes).
     {
@@ -952,7 +1047,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
           fence_proxy_async();
           __syncthreads();
         } else {
-          promote_tc(p, lay, ws, h, l, tb, Sbf, Rec, Sg, &bar_ld, &bar_mma, ph_ld, ph_mma, egp,
+          promote_tc(p, lay, ws, h, l, tb, Sbf, Rec, Mt, &bar_ld, &bar_mma, ph_ld, ph_mma, egp,
                      nrm, &abort_flag);
         }
       }
@@ -967,6 +1062,14 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     }
   }
   if (abort_flag && tid == 0) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
+  // Upper levels' final states from the transposed masters.
+  if (learned) {
+    __syncthreads();
+    for (int64_t e = tid; e < int64_t(L - 1) * TK * TV; e += kScanThreads) {
+      const int64_t l1 = e / (TK * TV), r2 = e % (TK * TV), k = r2 / TV, v = r2 % TV;
+      Sg[(l1 + 1) * TK * TV + r2] = Mt[l1 * TK * TV + v * TK + k];
+    }
+  }
   fence_before_sync();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tb, kScanCols);
