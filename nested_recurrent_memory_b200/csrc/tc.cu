@@ -100,7 +100,9 @@ __device__ __forceinline__ void set_status(const FwdParams& p, int bits) {
 // Gate activations of the promotion on the tensor-core path, from the fast
 // hardware exponential / logarithm / reciprocal (outputs feed bf16 MMA
 // operands or fp32 decays averaged over pairs).
-__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.f + __expf(-x)); }
+__device__ __forceinline__ float fast_sigmoid(float x) {
+  return __fdividef(1.f, 1.f + __expf(fminf(-x, 80.f)));
+}
 __device__ __forceinline__ float fast_softplus(float x) {
   return x > 20.f ? x : __logf(1.f + __expf(x));
 }
@@ -246,8 +248,10 @@ constexpr int kPrepCols = 256;  // TMEM columns
 constexpr int P_KG = 0;                  // K^(J), J = 0..3: 20 groups of 8 rows x 128, K-major
 constexpr int P_QB = 40960;              // 4 x [32 x 128] K-major: 16 query rows, 16 b*k rows
 constexpr int P_AF = 0;                  // fp32 [64][65] strictly lower A_kk
-constexpr int P_XF = P_AF + 16640;       // fp32 [64][65] (I + A_kk)^-1
-constexpr int P_XB = P_XF + 16640;       // bf16 [64 x 64] K-major: staged A_qk, then the inverse
+constexpr int XS = 68;                   // row stride (floats) of the inverse: float4 rows
+constexpr int P_XF = P_AF + 16640;       // fp32 [64][XS] (I + A_kk)^-1
+constexpr int P_XB = P_XF + 64 * XS * 4; // bf16 [64 x 64] K-major: staged A_qk, then the inverse
+constexpr int P_TT = P_XB + 8192;        // fp32 [3][16][16] block products of the inverse
 constexpr int P_R = 73728;               // bf16 [64 x 256] MN-major [w*v | k*b*e^G]
 constexpr int kPrepSmem = P_R + 32768;   // 106496
 
@@ -270,9 +274,10 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   __shared__ uint64_t bar;
   __shared__ uint32_t tbase;
   __shared__ float mixs[3][kC];             // mix_l * scale per row
-  __shared__ __align__(16) float tot[TK];   // G[31] (carry into rows 32..63)
   __shared__ __align__(16) float rho[5][TK];  // G[16J + 7] for J = 0..3, then G[63]
-  __shared__ float Tt[3 * 256];
+  __shared__ __align__(16) float rat[4][TK];  // e^(rho_J - rho_(J-1)) for J = 1..3; [0]: e^(G_63 - rho_3)
+  float* tot = rho[4];                        // G[31] carry; later overwritten by G[63]
+  float* Tt = reinterpret_cast<float*>(sm + P_TT);
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = n * kC;
@@ -332,6 +337,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
 #pragma unroll
       for (int u = 0; u < 8; ++u) G[ci][u] += tot[8 * (cw + 4 * ci) + u];
   }
+  __syncthreads();  // the carry row is reused for G[63] below
   // Reference points rho_J = G[16J + 7] (rows 7, 23, 39, 55) and G[63].
   if (lane == 7 || lane == 23 || (rh == 1 && lane == 31)) {
     const int slot = lane == 31 ? 4 : 2 * rh + (lane == 23);
@@ -339,6 +345,12 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
       for (int u = 0; u < 8; ++u) rho[slot][8 * (cw + 4 * ci) + u] = G[ci][u];
+  }
+  __syncthreads();
+  if (tid < TK) {
+    rat[0][tid] = __expf(rho[4][tid] - rho[3][tid]);
+#pragma unroll
+    for (int J = 1; J < 4; ++J) rat[J][tid] = __expf(rho[J][tid] - rho[J - 1][tid]);
   }
   __syncthreads();
   const uint32_t tb = tbase;
@@ -380,19 +392,16 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   for (int ci = 0; ci < 4; ++ci) {
     if (ci < 3) fetch(ci + 1, nxt);
     const int d0 = 8 * (cw + 4 * ci);
-    float qq[8], kk[8], bb[8], o1[8], o2[8], rr[8], gl[8];
+    float qq[8], kk[8], bb[8], o1[8], o2[8], rr[8];
     unpack8(cur[0], p.q.dt, qq);
     unpack8(cur[1], p.k.dt, kk);
     unpack8(cur[2], p.b.dt, bb);
     const float* g = G[ci];
     {
       const float4* rp = reinterpret_cast<const float4*>(&rho[I][d0]);
-      const float4* gp = reinterpret_cast<const float4*>(&rho[4][d0]);
-      const float4 a0 = rp[0], a1 = rp[1], c0 = gp[0], c1 = gp[1];
+      const float4 a0 = rp[0], a1 = rp[1];
       rr[0] = a0.x; rr[1] = a0.y; rr[2] = a0.z; rr[3] = a0.w;
       rr[4] = a1.x; rr[5] = a1.y; rr[6] = a1.z; rr[7] = a1.w;
-      gl[0] = c0.x; gl[1] = c0.y; gl[2] = c0.z; gl[3] = c0.w;
-      gl[4] = c1.x; gl[5] = c1.y; gl[6] = c1.z; gl[7] = c1.w;
     }
     // Q_I, BK_I rows (MMA1 B operand)
 #pragma unroll
@@ -404,13 +413,22 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     bf16* tile = QB + I * (32 * 128);
     *reinterpret_cast<uint4*>(tile + kmajor_off(r & 15, d0, 128)) = pack8(o1);
     *reinterpret_cast<uint4*>(tile + kmajor_off(16 + (r & 15), d0, 128)) = pack8(o2);
-    // K^(J) rows for every J >= I (MMA1 A operands)
-    for (int J = I; J < 4; ++J) {
-      const float4* rp = reinterpret_cast<const float4*>(&rho[J][d0]);
-      const float4 a0 = rp[0], a1 = rp[1];
-      const float rj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    // K^(J) rows for every J >= I (MMA1 A operands): e^(rho_J - G) by a
+    // chain of per-channel factors e^(rho_J - rho_(J-1)) <= 1, ending in
+    // e^(rho_3 - G), which also gives K_tail below.
+    float ech[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) o1[u] = kk[u] * __expf(rj[u] - g[u]);
+    for (int u = 0; u < 8; ++u) ech[u] = __expf(rr[u] - g[u]);
+    for (int J = I; J < 4; ++J) {
+      if (J > I) {
+        const float4* rp = reinterpret_cast<const float4*>(&rat[J][d0]);
+        const float4 a0 = rp[0], a1 = rp[1];
+        const float rj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ech[u] *= rj[u];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o1[u] = kk[u] * ech[u];
       *reinterpret_cast<uint4*>(KG + kgroup_elems(J) + kmajor_off(r, d0, 128)) = pack8(o1);
     }
     // e^G: level-0 read query and the k*b*e^G half of R; w*v half of R
@@ -430,9 +448,15 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       *reinterpret_cast<uint4*>(Rs + mnmajor_off(r, 128 + d0, 64)) = pack8(o2);
       *reinterpret_cast<uint4*>(Rs + mnmajor_off(r, d0, 64)) = pack8(ww);
     }
-    // K_tail = k e^(G_last - G) as the MN-major A operand of K_tail^T . v_new
+    // K_tail = k e^(G_last - G) = k e^(rho_3 - G) e^(G_last - rho_3), the
+    // MN-major A operand of K_tail^T . v_new
+    {
+      const float4* rp = reinterpret_cast<const float4*>(&rat[0][d0]);
+      const float4 a0 = rp[0], a1 = rp[1];
+      const float rj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-    for (int u = 0; u < 8; ++u) o1[u] = kk[u] * __expf(gl[u] - g[u]);
+      for (int u = 0; u < 8; ++u) o1[u] = kk[u] * ech[u] * rj[u];
+    }
     *reinterpret_cast<uint4*>(Ktg + mnmajor_off(r, d0, 64)) = pack8(o1);
     // upper-level read queries mix_l * scale * q_l
 #pragma unroll
@@ -515,25 +539,42 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       x[rr] = s;
     }
 #pragma unroll
-    for (int rr = 0; rr < 16; ++rr) Xf[(o + rr) * 65 + o + c] = x[rr];
+    for (int rr = 0; rr < 16; ++rr) Xf[(o + rr) * XS + o + c] = x[rr];
   }
   __syncthreads();
+  // Off-diagonal block rows; each thread owns 4 consecutive columns of one
+  // row of one block (float4 operands of X and T).
   for (int I2 = 1; I2 < 4; ++I2) {
-    for (int e = tid; e < I2 * 256; e += kPrepThreads) {
-      const int J = e >> 8, rr = (e >> 4) & 15, c = e & 15;
-      float s = 0.f;
-      for (int K2 = J; K2 < I2; ++K2)
+    const bool active = tid < I2 * 64;
+    const int J = tid >> 6, rr = (tid >> 2) & 15, c0 = (tid & 3) * 4;
+    if (active) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int K2 = J; K2 < I2; ++K2) {
 #pragma unroll
-        for (int m = 0; m < 16; ++m)
-          s = fmaf(Af[(16 * I2 + rr) * 65 + 16 * K2 + m], Xf[(16 * K2 + m) * 65 + 16 * J + c], s);
-      Tt[e] = s;
+        for (int m = 0; m < 16; ++m) {
+          const float a = Af[(16 * I2 + rr) * 65 + 16 * K2 + m];
+          const float4 x = *reinterpret_cast<const float4*>(&Xf[(16 * K2 + m) * XS + 16 * J + c0]);
+          acc.x = fmaf(a, x.x, acc.x);
+          acc.y = fmaf(a, x.y, acc.y);
+          acc.z = fmaf(a, x.z, acc.z);
+          acc.w = fmaf(a, x.w, acc.w);
+        }
+      }
+      *reinterpret_cast<float4*>(&Tt[(J << 8) + rr * 16 + c0]) = acc;
     }
     __syncthreads();
-    for (int e = tid; e < I2 * 256; e += kPrepThreads) {
-      const int J = e >> 8, rr = (e >> 4) & 15, c = e & 15;
-      float s = 0.f;
-      for (int m = 0; m <= rr; ++m) s = fmaf(Xf[(16 * I2 + rr) * 65 + 16 * I2 + m], Tt[(J << 8) + m * 16 + c], s);
-      Xf[(16 * I2 + rr) * 65 + 16 * J + c] = -s;
+    if (active) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int m = 0; m <= rr; ++m) {
+        const float a = Xf[(16 * I2 + rr) * XS + 16 * I2 + m];
+        const float4 tv = *reinterpret_cast<const float4*>(&Tt[(J << 8) + m * 16 + c0]);
+        acc.x = fmaf(a, tv.x, acc.x);
+        acc.y = fmaf(a, tv.y, acc.y);
+        acc.z = fmaf(a, tv.z, acc.z);
+        acc.w = fmaf(a, tv.w, acc.w);
+      }
+      *reinterpret_cast<float4*>(&Xf[(16 * I2 + rr) * XS + 16 * J + c0]) =
+          make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     }
     __syncthreads();
   }
@@ -541,7 +582,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     const int i = it >> 3, j0 = (it & 7) * 8;
     float x[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) x[u] = (j0 + u <= i) ? Xf[i * 65 + j0 + u] : 0.f;
+    for (int u = 0; u < 8; ++u) x[u] = (j0 + u <= i) ? Xf[i * XS + j0 + u] : 0.f;
     *reinterpret_cast<uint4*>(Xb + kmajor_off(i, j0, 64)) = pack8(x);
   }
   fence_proxy_async();
@@ -665,23 +706,32 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   ph_mma ^= 1;
   fence_after_sync();
   // V' -> bf16 A operand (over the bank, which P1 has consumed).
-  for (int c16 = 0; c16 < 4; ++c16) {
-    const int v0 = 64 * half + 16 * c16;
-    float x[16];
-    tmem_ld16(taddr(tV, 32 * quarter, v0), x);
-    tmem_wait_ld();
+  {
+    const int v0 = 64 * half;
+    float x[64];
+    tmem_ld64(taddr(tV, 32 * quarter, v0), x);
     if (row >= 0) {
-      *reinterpret_cast<uint4*>(XQ + kmajor_off(row, v0, TV)) = pack8(x);
-      *reinterpret_cast<uint4*>(XQ + kmajor_off(row, v0 + 8, TV)) = pack8(x + 8);
+#pragma unroll
+      for (int c = 0; c < 64; c += 8)
+        *reinterpret_cast<uint4*>(XQ + kmajor_off(row, v0 + c, TV)) = pack8(x + c);
     }
   }
   fence_proxy_async();
   fence_before_sync();
   __syncthreads();
-  // P2b
+  // P2b. With 64 pairs the two halves of the N=256 product go to the two
+  // half-lane groups of the same TMEM columns (w logits at lanes +0, g logits
+  // at lanes +16), so every lane of the epilogue has work.
+  const bool split = mp == 64;
+  const uint32_t id_half = idesc_f16(64, 128, true, false, false);
   if (tid == 0) {
     fence_after_sync();
-    mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    if (split) {
+      mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_half, false);
+      mma_tile(tG + (16u << 16), smem_u32(XQ), smem_u32(XW + 128 * 128), TV, id_half, false);
+    } else {
+      mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    }
     mma_commit(bar_mma);
   }
   __syncwarp();
@@ -692,29 +742,45 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   // (columns XOR-swizzled by row so both the row writes and the column sums
   // are free of bank conflicts).
   float* gpart = reinterpret_cast<float*>(X);
-  for (int c16 = 0; c16 < 4; ++c16) {
-    const int c0 = 64 * half + 16 * c16;
-    float vp[16], wl[16], gl[16];
-    tmem_ld16(taddr(tV, 32 * quarter, c0), vp);
-    tmem_ld16(taddr(tG, 32 * quarter, c0), wl);
-    tmem_ld16(taddr(tG, 32 * quarter, 128 + c0), gl);
-    tmem_wait_ld();
+  {
+    const int c0 = 64 * half;
+    float a[64], vp[64];
+    if (split) {
+      tmem_ld64(taddr(tG, 32 * quarter, c0), a);
+      tmem_ld64(taddr(tV, 32 * quarter, c0), vp);
+      if (lane < 16) {
 #pragma unroll
-    for (int u = 0; u < 16; ++u) vp[u] *= fast_sigmoid(wl[u] + kWLogitInit);
-    tmem_st16(taddr(tV, 32 * quarter, c0), vp);
-    if (row >= 0) {
+        for (int u = 0; u < 64; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
+      } else {
+        const int gr = 16 * quarter + lane - 16;
 #pragma unroll
-      for (int u = 0; u < 16; ++u)
-        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -fast_softplus(gl[u] + kGLogitInit);
+        for (int u = 0; u < 64; ++u)
+          gpart[gr * 128 + ((c0 + u) ^ (gr & 31))] = -fast_softplus(a[u] + kGLogitInit);
+      }
+      tmem_st64(taddr(tV, 32 * quarter, c0), vp);  // lanes 16..31 of tV are unused
+    } else {
+      tmem_ld64(taddr(tV, 32 * quarter, c0), vp);
+      tmem_ld64(taddr(tG, 32 * quarter, c0), a);
+#pragma unroll
+      for (int u = 0; u < 64; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
+      tmem_st64(taddr(tV, 32 * quarter, c0), vp);
+      tmem_ld64(taddr(tG, 32 * quarter, 128 + c0), a);
+#pragma unroll
+      for (int u = 0; u < 64; ++u)
+        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -fast_softplus(a[u] + kGLogitInit);
     }
   }
   tmem_wait_st();
   __syncthreads();
-  if (tid < 128) {
+  {
+    // g = mean over the real pairs, two threads per column.
+    const int k = tid & 127, hh = tid >> 7, r0 = hh * (nq >> 1), r1 = r0 + (nq >> 1);
     float s = 0.f;
-    for (int r = 0; r < nq; ++r) s += gpart[r * 128 + (tid ^ (r & 31))];
-    egp[tid] = expf(s / float(nq));
+    for (int r = r0; r < r1; ++r) s += gpart[r * 128 + (k ^ (r & 31))];
+    nrm[hh * 128 + k] = s;
   }
+  __syncthreads();
+  if (tid < 128) egp[tid] = expf((nrm[tid] + nrm[128 + tid]) / float(nq));
   fence_proxy_async();
   __syncthreads();
   // [W_k^T | W_b] in over the gate scratch.
@@ -724,10 +790,15 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   }
   if (!mbar_wait(bar_ld, ph_ld)) *abort_flag = 1;
   ph_ld ^= 1;
-  // P2a
+  // P2a (u at lanes +0, b logits at lanes +16 when split)
   if (tid == 0) {
     fence_after_sync();
-    mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    if (split) {
+      mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_half, false);
+      mma_tile(tG + (16u << 16), smem_u32(XQ), smem_u32(XW + 128 * 128), TV, id_half, false);
+    } else {
+      mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    }
     mma_commit(bar_mma);
   }
   __syncwarp();
@@ -737,37 +808,44 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   // keys = u / max(|u|, 1e-12) (probe.py:100): row norms across both halves.
   {
     float ss = 0.f;
-    for (int c16 = 0; c16 < 4; ++c16) {
-      float x[16];
-      tmem_ld16(taddr(tG, 32 * quarter, 64 * half + 16 * c16), x);
-      tmem_wait_ld();
+    float x[64];
+    tmem_ld64(taddr(tG, 32 * quarter, 64 * half), x);
 #pragma unroll
-      for (int u = 0; u < 16; ++u) ss = fmaf(x[u], x[u], ss);
-    }
-    if (row >= 0) nrm[half * 128 + row] = ss;
+    for (int u = 0; u < 64; ++u) ss = fmaf(x[u], x[u], ss);
+    if (row >= 0 && (!split || lane < 16)) nrm[half * 128 + row] = ss;
   }
   __syncthreads();
   bf16* keysT = XW;                      // MN-major A: keys^T [K x mp]
   bf16* kbg = XW + 16384;                // K-major A: keys * b * e^g [mp x K]
   {
-    const float inv = row >= 0 ? __frcp_rn(fmaxf(sqrtf(nrm[row] + nrm[128 + row]), 1e-12f)) : 0.f;
-    for (int c16 = 0; c16 < 4; ++c16) {
-      const int k0 = 64 * half + 16 * c16;
-      float u[16], bl[16];
-      tmem_ld16(taddr(tG, 32 * quarter, k0), u);
-      tmem_ld16(taddr(tG, 32 * quarter, 128 + k0), bl);
-      tmem_wait_ld();
-      if (row >= 0) {
-        float kk[16], kb[16];
+    const float inv = row >= 0 ? __fdividef(1.f, fmaxf(sqrtf(nrm[row] + nrm[128 + row]), 1e-12f)) : 0.f;
+    const int kb0 = 64 * half;
+    float u[64], bl[64];
+    tmem_ld64(taddr(tG, 32 * quarter, kb0), u);
+    if (split) {
+      // lanes 16..31 hold the b logits of row (lane - 16): they form
+      // sigmoid(b - 4) * e^g and hand it to the u lane.
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          kk[t] = u[t] * inv;
-          kb[t] = kk[t] * fast_sigmoid(bl[t] + kBLogitInit) * egp[k0 + t];
+      for (int t = 0; t < 64; ++t) {
+        const float sb = lane >= 16 ? fast_sigmoid(u[t] + kBLogitInit) * egp[kb0 + t] : 0.f;
+        bl[t] = __shfl_down_sync(0xffffffffu, sb, 16);
+      }
+    } else {
+      tmem_ld64(taddr(tG, 32 * quarter, 128 + kb0), bl);
+#pragma unroll
+      for (int t = 0; t < 64; ++t) bl[t] = fast_sigmoid(bl[t] + kBLogitInit) * egp[kb0 + t];
+    }
+    if (row >= 0) {
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        float kk[8], kb[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          kk[t] = u[c + t] * inv;
+          kb[t] = kk[t] * bl[c + t];
         }
-        *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, k0, mp)) = pack8(kk);
-        *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, k0 + 8, mp)) = pack8(kk + 8);
-        *reinterpret_cast<uint4*>(kbg + kmajor_off(row, k0, TK)) = pack8(kb);
-        *reinterpret_cast<uint4*>(kbg + kmajor_off(row, k0 + 8, TK)) = pack8(kb + 8);
+        *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, kb0 + c, mp)) = pack8(kk);
+        *reinterpret_cast<uint4*>(kbg + kmajor_off(row, kb0 + c, TK)) = pack8(kb);
       }
     }
   }
@@ -784,30 +862,28 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   {
     const int k = 32 * quarter + lane;
     const float e = egp[k];
-    for (int c16 = 0; c16 < 4; ++c16) {
-      const int v0 = 64 * half + 16 * c16;
-      float x[16];
+    const int v0 = 64 * half;
+    float x[64];
 #pragma unroll
-      for (int u = 0; u < 16; ++u) x[u] = Sl[(v0 + u) * TK + k] * e;
-      tmem_st16(taddr(tS, 32 * quarter, v0), x);
-    }
+    for (int u = 0; u < 64; ++u) x[u] = Sl[(v0 + u) * TK + k] * e;
+    tmem_st64(taddr(tS, 32 * quarter, v0), x);
     tmem_wait_st();
   }
   if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
   ph_mma ^= 1;
   fence_after_sync();
   // vn = v * w - (keys * b * e^g) . S_l -> MN-major B operand [mp x V].
-  for (int c16 = 0; c16 < 4; ++c16) {
-    const int v0 = 64 * half + 16 * c16;
-    float vw[16], d[16];
-    tmem_ld16(taddr(tV, 32 * quarter, v0), vw);
-    tmem_ld16(taddr(tG, 32 * quarter, v0), d);
-    tmem_wait_ld();
+  {
+    const int v0 = 64 * half;
+    float vw[64], d[64];
+    tmem_ld64(taddr(tV, 32 * quarter, v0), vw);
+    tmem_ld64(taddr(tG, 32 * quarter, v0), d);
     if (row >= 0) {
 #pragma unroll
-      for (int u = 0; u < 16; ++u) vw[u] -= d[u];
-      *reinterpret_cast<uint4*>(XQ + mnmajor_off(row, v0, mp)) = pack8(vw);
-      *reinterpret_cast<uint4*>(XQ + mnmajor_off(row, v0 + 8, mp)) = pack8(vw + 8);
+      for (int u = 0; u < 64; ++u) vw[u] -= d[u];
+#pragma unroll
+      for (int c = 0; c < 64; c += 8)
+        *reinterpret_cast<uint4*>(XQ + mnmajor_off(row, v0 + c, mp)) = pack8(vw + c);
     }
   }
   fence_proxy_async();
@@ -825,16 +901,14 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   fence_after_sync();
   {
     const int k = 32 * quarter + lane;
-    for (int c16 = 0; c16 < 4; ++c16) {
-      const int v0 = 64 * half + 16 * c16;
-      float x[16];
-      tmem_ld16(taddr(tS, 32 * quarter, v0), x);
-      tmem_wait_ld();
+    const int v0 = 64 * half;
+    float x[64];
+    tmem_ld64(taddr(tS, 32 * quarter, v0), x);
 #pragma unroll
-      for (int u = 0; u < 16; ++u) Sl[(v0 + u) * TK + k] = x[u];
-      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0, TK)) = pack8(x);
-      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0 + 8, TK)) = pack8(x + 8);
-    }
+    for (int u = 0; u < 64; ++u) Sl[(v0 + u) * TK + k] = x[u];
+#pragma unroll
+    for (int c = 0; c < 64; c += 8)
+      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0 + c, TK)) = pack8(x + c);
   }
   fence_proxy_async();
   fence_before_sync();
@@ -931,19 +1005,24 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     }
     __syncwarp();
 
+    // U rows for epilogue 1, fetched while MMA1 runs.
+    uint4 urow[8];
+    if (lane < 16) {
+      const uint4* Ug = reinterpret_cast<const uint4*>(recg + lay.rec.U) +
+                        ((16 * quarter + lane) * TV + 64 * half) / 8;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) urow[c] = __ldg(Ug + c);
+    }
     // Decay S0 in TMEM by e^(G_last) while MMA1 runs (naive.py:392, first term).
     {
       const int k = 32 * quarter + lane;
       const float e = reinterpret_cast<const float*>(recg + lay.rec.eg)[k];
-      for (int c16 = 0; c16 < 4; ++c16) {
-        const uint32_t ta = taddr(tS0, 32 * quarter, 64 * half + 16 * c16);
-        float x[16];
-        tmem_ld16(ta, x);
-        tmem_wait_ld();
+      const uint32_t ta = taddr(tS0, 32 * quarter, 64 * half);
+      float x[64];
+      tmem_ld64(ta, x);
 #pragma unroll
-        for (int u = 0; u < 16; ++u) x[u] *= e;
-        tmem_st16(ta, x);
-      }
+      for (int u = 0; u < 64; ++u) x[u] *= e;
+      tmem_st64(ta, x);
       tmem_wait_st();
     }
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
@@ -953,20 +1032,17 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376).
     {
       const int i = 16 * quarter + lane;
-      const bf16* Ug = reinterpret_cast<const bf16*>(recg + lay.rec.U);
-      for (int c16 = 0; c16 < 4; ++c16) {
-        const int v0 = 64 * half + 16 * c16;
-        float x[16];
-        tmem_ld16(taddr(tD, 32 * quarter, v0), x);
-        tmem_wait_ld();
-        if (lane < 16) {
-          float u[16];
-          load8_raw(Ug, NGDN2_BF16, i * TV + v0, 1, u);
-          load8_raw(Ug, NGDN2_BF16, i * TV + v0 + 8, 1, u + 8);
+      const int v0 = 64 * half;
+      float x[64];
+      tmem_ld64(taddr(tD, 32 * quarter, v0), x);
+      if (lane < 16) {
 #pragma unroll
-          for (int t = 0; t < 16; ++t) x[t] = u[t] - x[t];
-          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, v0, kC)) = pack8(x);
-          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, v0 + 8, kC)) = pack8(x + 8);
+        for (int c = 0; c < 8; ++c) {
+          float u[8];
+          unpack8(urow[c], NGDN2_BF16, u);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) u[t] -= x[8 * c + t];
+          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, v0 + 8 * c, kC)) = pack8(u);
         }
       }
     }
@@ -999,36 +1075,29 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     // E2: output rows (lanes 16..31) and the new S0 (all lanes).
     {
       const int i = 16 * quarter + lane - 16, t = n * kC + i;
-      for (int c16 = 0; c16 < 4; ++c16) {
-        const int v0 = 64 * half + 16 * c16;
-        float x[16];
-        tmem_ld16(taddr(tD, 32 * quarter, v0), x);
-        tmem_wait_ld();
-        if (lane >= 16 && t < p.T) {
-          const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + v0;
-          if (p.dtype == NGDN2_BF16) {
-            bf16* og = reinterpret_cast<bf16*>(p.o) + o;
-            *reinterpret_cast<uint4*>(og) = pack8(x);
-            *reinterpret_cast<uint4*>(og + 8) = pack8(x + 8);
-          } else {
+      const int v0 = 64 * half;
+      float x[64];
+      tmem_ld64(taddr(tD, 32 * quarter, v0), x);
+      if (lane >= 16 && t < p.T) {
+        const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + v0;
+        if (p.dtype == NGDN2_BF16) {
+          bf16* og = reinterpret_cast<bf16*>(p.o) + o;
 #pragma unroll
-            for (int u = 0; u < 16; ++u) store_elem(p.o, o + u, x[u], p.dtype);
-          }
+          for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(og + c) = pack8(x + c);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 64; ++u) store_elem(p.o, o + u, x[u], p.dtype);
         }
       }
       const int k = 32 * quarter + lane;
-      for (int c16 = 0; c16 < 4; ++c16) {
-        const int v0 = 64 * half + 16 * c16;
-        float x[16];
-        tmem_ld16(taddr(tS0, 32 * quarter, v0), x);
-        tmem_wait_ld();
-        *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, v0, TK)) = pack8(x);
-        *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, v0 + 8, TK)) = pack8(x + 8);
-        if (write_master) {
+      tmem_ld64(taddr(tS0, 32 * quarter, v0), x);
 #pragma unroll
-          for (int u = 0; u < 16; u += 4)
-            *reinterpret_cast<float4*>(Sg + k * TV + v0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
-        }
+      for (int c = 0; c < 64; c += 8)
+        *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, v0 + c, TK)) = pack8(x + c);
+      if (write_master) {
+#pragma unroll
+        for (int u = 0; u < 64; u += 4)
+          *reinterpret_cast<float4*>(Sg + k * TV + v0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
       }
     }
     fence_proxy_async();
