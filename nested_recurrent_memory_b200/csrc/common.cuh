@@ -54,8 +54,8 @@ __device__ __forceinline__ float softplusf_(float x) {
 // ``la`` and ``lb`` are element loaders (so strides, transposes, dtype
 // conversion and elementwise pre-products are free); operands are staged
 // through shared memory in 64x16 and 16x64 tiles and each thread owns a 4x4
-// block of outputs. The block must have exactly kGemmThreads threads and
-// every thread must call it (it synchronises). M and N are arbitrary; Kd
+// block of outputs. The block needs at least kGemmThreads threads (more
+// only join the barriers) and every thread must call it (it synchronises). M and N are arbitrary; Kd
 // must be a multiple of 16. ``smem`` holds kGemmSmemFloats floats.
 // ---------------------------------------------------------------------------
 
@@ -68,6 +68,7 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
   float* As = smem;                 // [16][65], k-major
   float* Bs = smem + 16 * kGemmLd;  // [16][65]
   const int tid = threadIdx.x;
+  const bool act = tid < kGemmThreads;  // larger blocks: the rest only join the barriers
   const int tm = (tid / 16) * 4;
   const int tn = (tid % 16) * 4;
   for (int m0 = 0; m0 < M; m0 += 64) {
@@ -78,38 +79,44 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
       for (int k0 = 0; k0 < Kd; k0 += 16) {
-        for (int e = tid; e < 64 * 16; e += kGemmThreads) {
-          int mm = e / 16, kk = e % 16;
-          int gm = m0 + mm;
-          As[kk * kGemmLd + mm] = gm < M ? la(gm, k0 + kk) : 0.f;
-        }
-        for (int e = tid; e < 64 * 16; e += kGemmThreads) {
-          int kk = e / 64, nn = e % 64;
-          int gn = n0 + nn;
-          Bs[kk * kGemmLd + nn] = gn < N ? lb(k0 + kk, gn) : 0.f;
+        if (act) {
+          for (int e = tid; e < 64 * 16; e += kGemmThreads) {
+            int mm = e / 16, kk = e % 16;
+            int gm = m0 + mm;
+            As[kk * kGemmLd + mm] = gm < M ? la(gm, k0 + kk) : 0.f;
+          }
+          for (int e = tid; e < 64 * 16; e += kGemmThreads) {
+            int kk = e / 64, nn = e % 64;
+            int gn = n0 + nn;
+            Bs[kk * kGemmLd + nn] = gn < N ? lb(k0 + kk, gn) : 0.f;
+          }
         }
         __syncthreads();
+        if (act) {
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
-          float a[4], bb[4];
+          for (int kk = 0; kk < 16; ++kk) {
+            float a[4], bb[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + i];
+            for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + i];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + j];
+            for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + j];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+              for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+          }
         }
         __syncthreads();
       }
+      if (act) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          int gm = m0 + tm + i, gn = n0 + tn + j;
-          if (gm < M && gn < N) epi(gm, gn, acc[i][j]);
-        }
+          for (int j = 0; j < 4; ++j) {
+            int gm = m0 + tm + i, gn = n0 + tn + j;
+            if (gm < M && gn < N) epi(gm, gn, acc[i][j]);
+          }
+      }
       __syncthreads();
     }
   }

@@ -635,7 +635,7 @@ namespace {
 // scan_tc: grid (H, B), 256 threads, one CTA per SM.
 // ---------------------------------------------------------------------------
 
-constexpr int kScanThreads = 256;
+constexpr int kScanThreads = 512;
 constexpr int kScanCols = 512;          // TMEM: S0 0..127, chunk accumulators 128..255, promotion 128..511
 constexpr int TILE_S = TK * TV * 2;     // bf16 state copy
 // Promotion scratch (the record region and what follows it): a 64 KB slot
@@ -669,13 +669,15 @@ __device__ __forceinline__ void refresh_copy(bf16* dst, const float* src) {
 // free between chunks); bf16 operands in ``X`` (the record buffer, reloaded
 // after the promotion). The fp32 master of S_l is in global memory,
 // transposed ([V][K]) so that lane-per-key TMEM traffic reads and writes it
-// in coalesced 128-byte rows.
+// in coalesced 128-byte rows. With 64 pairs the gate products go to the two
+// half-lane groups of the same TMEM columns so every lane has work.
+// 512 threads: warp w reads TMEM lane quarter (w & 3), columns 32 * (w >> 2).
 __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* ws, int h, int l,
                            uint32_t tb, bf16* Sbf, uint8_t* X, float* Mt, uint64_t* bar_ld,
                            uint64_t* bar_mma, uint32_t& ph_ld, uint32_t& ph_mma, float* egp,
-                           float* nrm, int* abort_flag) {
+                           float* red, int* abort_flag) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, half = warp >> 2;
+  const int quarter = warp & 3, c0 = 32 * (warp >> 2);
   const int nq = p.nq[l - 1], mp = pad_pairs(nq);
   const char* pt = ws + lay.ptc_off + (int64_t(l - 1) * p.H + h) * PT_SIZE;
   bf16* XW = reinterpret_cast<bf16*>(X);
@@ -683,8 +685,10 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   float* Sl = Mt + int64_t(l - 1) * TK * TV;  // fp32 master of level l, [V][K]
   const uint32_t tV = tb + 128, tG = tb + 256, tS = tb + 384;
   const int row = (mp == 128) ? 32 * quarter + lane : (lane < 16 ? 16 * quarter + lane : -1);
+  const bool split = mp == 64;
   const uint32_t id_read = idesc_f16(mp, 128, true, false, true);
   const uint32_t id_gate = idesc_f16(mp, 256, true, false, false);
+  const uint32_t id_half = idesc_f16(64, 128, true, false, false);
   const uint32_t id_upd = idesc_f16(128, 128, true, true, true);
 
   // Query bank and [W_w | W_g] in.
@@ -707,23 +711,18 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   fence_after_sync();
   // V' -> bf16 A operand (over the bank, which P1 has consumed).
   {
-    const int v0 = 64 * half;
-    float x[64];
-    tmem_ld64(taddr(tV, 32 * quarter, v0), x);
+    float x[32];
+    tmem_ld32(taddr(tV, 32 * quarter, c0), x);
     if (row >= 0) {
 #pragma unroll
-      for (int c = 0; c < 64; c += 8)
-        *reinterpret_cast<uint4*>(XQ + kmajor_off(row, v0 + c, TV)) = pack8(x + c);
+      for (int c = 0; c < 32; c += 8)
+        *reinterpret_cast<uint4*>(XQ + kmajor_off(row, c0 + c, TV)) = pack8(x + c);
     }
   }
   fence_proxy_async();
   fence_before_sync();
   __syncthreads();
-  // P2b. With 64 pairs the two halves of the N=256 product go to the two
-  // half-lane groups of the same TMEM columns (w logits at lanes +0, g logits
-  // at lanes +16), so every lane of the epilogue has work.
-  const bool split = mp == 64;
-  const uint32_t id_half = idesc_f16(64, 128, true, false, false);
+  // P2b
   if (tid == 0) {
     fence_after_sync();
     if (split) {
@@ -743,44 +742,44 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   // are free of bank conflicts).
   float* gpart = reinterpret_cast<float*>(X);
   {
-    const int c0 = 64 * half;
-    float a[64], vp[64];
+    float a[32], vp[32];
     if (split) {
-      tmem_ld64(taddr(tG, 32 * quarter, c0), a);
-      tmem_ld64(taddr(tV, 32 * quarter, c0), vp);
+      tmem_ld32(taddr(tG, 32 * quarter, c0), a);
+      tmem_ld32(taddr(tV, 32 * quarter, c0), vp);
       if (lane < 16) {
 #pragma unroll
-        for (int u = 0; u < 64; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
+        for (int u = 0; u < 32; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
       } else {
         const int gr = 16 * quarter + lane - 16;
 #pragma unroll
-        for (int u = 0; u < 64; ++u)
+        for (int u = 0; u < 32; ++u)
           gpart[gr * 128 + ((c0 + u) ^ (gr & 31))] = -fast_softplus(a[u] + kGLogitInit);
       }
-      tmem_st64(taddr(tV, 32 * quarter, c0), vp);  // lanes 16..31 of tV are unused
+      tmem_st32(taddr(tV, 32 * quarter, c0), vp);  // lanes 16..31 of tV are unused
     } else {
-      tmem_ld64(taddr(tV, 32 * quarter, c0), vp);
-      tmem_ld64(taddr(tG, 32 * quarter, c0), a);
+      tmem_ld32(taddr(tV, 32 * quarter, c0), vp);
+      tmem_ld32(taddr(tG, 32 * quarter, c0), a);
 #pragma unroll
-      for (int u = 0; u < 64; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
-      tmem_st64(taddr(tV, 32 * quarter, c0), vp);
-      tmem_ld64(taddr(tG, 32 * quarter, 128 + c0), a);
+      for (int u = 0; u < 32; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
+      tmem_st32(taddr(tV, 32 * quarter, c0), vp);
+      tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), a);
 #pragma unroll
-      for (int u = 0; u < 64; ++u)
+      for (int u = 0; u < 32; ++u)
         gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -fast_softplus(a[u] + kGLogitInit);
     }
   }
   tmem_wait_st();
   __syncthreads();
   {
-    // g = mean over the real pairs, two threads per column.
-    const int k = tid & 127, hh = tid >> 7, r0 = hh * (nq >> 1), r1 = r0 + (nq >> 1);
+    // g = mean over the real pairs, four threads per column.
+    const int k = tid & 127, qq = tid >> 7, r0 = qq * (nq >> 2), r1 = r0 + (nq >> 2);
     float s = 0.f;
     for (int r = r0; r < r1; ++r) s += gpart[r * 128 + (k ^ (r & 31))];
-    nrm[hh * 128 + k] = s;
+    red[qq * 128 + k] = s;
   }
   __syncthreads();
-  if (tid < 128) egp[tid] = expf((nrm[tid] + nrm[128 + tid]) / float(nq));
+  if (tid < 128)
+    egp[tid] = expf((red[tid] + red[128 + tid] + red[256 + tid] + red[384 + tid]) / float(nq));
   fence_proxy_async();
   __syncthreads();
   // [W_k^T | W_b] in over the gate scratch.
@@ -805,47 +804,48 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
   ph_mma ^= 1;
   fence_after_sync();
-  // keys = u / max(|u|, 1e-12) (probe.py:100): row norms across both halves.
+  // keys = u / max(|u|, 1e-12) (probe.py:100): row norms across the four parts.
+  float u[32];
+  tmem_ld32(taddr(tG, 32 * quarter, c0), u);
   {
     float ss = 0.f;
-    float x[64];
-    tmem_ld64(taddr(tG, 32 * quarter, 64 * half), x);
 #pragma unroll
-    for (int u = 0; u < 64; ++u) ss = fmaf(x[u], x[u], ss);
-    if (row >= 0 && (!split || lane < 16)) nrm[half * 128 + row] = ss;
+    for (int t = 0; t < 32; ++t) ss = fmaf(u[t], u[t], ss);
+    if (row >= 0 && (!split || lane < 16)) red[(warp >> 2) * 128 + row] = ss;
   }
   __syncthreads();
   bf16* keysT = XW;                      // MN-major A: keys^T [K x mp]
   bf16* kbg = XW + 16384;                // K-major A: keys * b * e^g [mp x K]
   {
-    const float inv = row >= 0 ? __fdividef(1.f, fmaxf(sqrtf(nrm[row] + nrm[128 + row]), 1e-12f)) : 0.f;
-    const int kb0 = 64 * half;
-    float u[64], bl[64];
-    tmem_ld64(taddr(tG, 32 * quarter, kb0), u);
+    const float inv =
+        row >= 0 ? __fdividef(1.f, fmaxf(sqrtf(red[row] + red[128 + row] + red[256 + row] +
+                                               red[384 + row]), 1e-12f))
+                 : 0.f;
+    float bl[32];
     if (split) {
       // lanes 16..31 hold the b logits of row (lane - 16): they form
       // sigmoid(b - 4) * e^g and hand it to the u lane.
 #pragma unroll
-      for (int t = 0; t < 64; ++t) {
-        const float sb = lane >= 16 ? fast_sigmoid(u[t] + kBLogitInit) * egp[kb0 + t] : 0.f;
+      for (int t = 0; t < 32; ++t) {
+        const float sb = lane >= 16 ? fast_sigmoid(u[t] + kBLogitInit) * egp[c0 + t] : 0.f;
         bl[t] = __shfl_down_sync(0xffffffffu, sb, 16);
       }
     } else {
-      tmem_ld64(taddr(tG, 32 * quarter, 128 + kb0), bl);
+      tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), bl);
 #pragma unroll
-      for (int t = 0; t < 64; ++t) bl[t] = fast_sigmoid(bl[t] + kBLogitInit) * egp[kb0 + t];
+      for (int t = 0; t < 32; ++t) bl[t] = fast_sigmoid(bl[t] + kBLogitInit) * egp[c0 + t];
     }
     if (row >= 0) {
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) {
+      for (int c = 0; c < 32; c += 8) {
         float kk[8], kb[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
           kk[t] = u[c + t] * inv;
           kb[t] = kk[t] * bl[c + t];
         }
-        *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, kb0 + c, mp)) = pack8(kk);
-        *reinterpret_cast<uint4*>(kbg + kmajor_off(row, kb0 + c, TK)) = pack8(kb);
+        *reinterpret_cast<uint4*>(keysT + mnmajor_off(row, c0 + c, mp)) = pack8(kk);
+        *reinterpret_cast<uint4*>(kbg + kmajor_off(row, c0 + c, TK)) = pack8(kb);
       }
     }
   }
@@ -862,11 +862,10 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   {
     const int k = 32 * quarter + lane;
     const float e = egp[k];
-    const int v0 = 64 * half;
-    float x[64];
+    float x[32];
 #pragma unroll
-    for (int u = 0; u < 64; ++u) x[u] = Sl[(v0 + u) * TK + k] * e;
-    tmem_st64(taddr(tS, 32 * quarter, v0), x);
+    for (int t = 0; t < 32; ++t) x[t] = Sl[(c0 + t) * TK + k] * e;
+    tmem_st32(taddr(tS, 32 * quarter, c0), x);
     tmem_wait_st();
   }
   if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
@@ -874,16 +873,15 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   fence_after_sync();
   // vn = v * w - (keys * b * e^g) . S_l -> MN-major B operand [mp x V].
   {
-    const int v0 = 64 * half;
-    float vw[64], d[64];
-    tmem_ld64(taddr(tV, 32 * quarter, v0), vw);
-    tmem_ld64(taddr(tG, 32 * quarter, v0), d);
+    float vw[32], d[32];
+    tmem_ld32(taddr(tV, 32 * quarter, c0), vw);
+    tmem_ld32(taddr(tG, 32 * quarter, c0), d);
     if (row >= 0) {
 #pragma unroll
-      for (int u = 0; u < 64; ++u) vw[u] -= d[u];
+      for (int t = 0; t < 32; ++t) vw[t] -= d[t];
 #pragma unroll
-      for (int c = 0; c < 64; c += 8)
-        *reinterpret_cast<uint4*>(XQ + mnmajor_off(row, v0 + c, mp)) = pack8(vw + c);
+      for (int c = 0; c < 32; c += 8)
+        *reinterpret_cast<uint4*>(XQ + mnmajor_off(row, c0 + c, mp)) = pack8(vw + c);
     }
   }
   fence_proxy_async();
@@ -901,14 +899,13 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   fence_after_sync();
   {
     const int k = 32 * quarter + lane;
-    const int v0 = 64 * half;
-    float x[64];
-    tmem_ld64(taddr(tS, 32 * quarter, v0), x);
+    float x[32];
+    tmem_ld32(taddr(tS, 32 * quarter, c0), x);
 #pragma unroll
-    for (int u = 0; u < 64; ++u) Sl[(v0 + u) * TK + k] = x[u];
+    for (int t = 0; t < 32; ++t) Sl[(c0 + t) * TK + k] = x[t];
 #pragma unroll
-    for (int c = 0; c < 64; c += 8)
-      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, v0 + c, TK)) = pack8(x + c);
+    for (int c = 0; c < 32; c += 8)
+      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, c0 + c, TK)) = pack8(x + c);
   }
   fence_proxy_async();
   fence_before_sync();
@@ -923,11 +920,11 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   __shared__ float egp[128];
-  __shared__ float nrm[256];
+  __shared__ float red[512];
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = p.L;
-  const int quarter = warp & 3, half = warp >> 2;
+  const int quarter = warp & 3, c0 = 32 * (warp >> 2);
   const int64_t bh = int64_t(b) * p.H + h;
   const uint32_t load_bytes = static_cast<uint32_t>(lay.rec.load_bytes);
   bf16* Sbf = reinterpret_cast<bf16*>(sm);
@@ -967,13 +964,10 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   // S0 into TMEM, bf16 copies of every level into shared memory.
   {
     const int k = 32 * quarter + lane;
-    for (int c16 = 0; c16 < 4; ++c16) {
-      const int v0 = 64 * half + 16 * c16;
-      float x[16];
+    float x[32];
 #pragma unroll
-      for (int u = 0; u < 16; ++u) x[u] = Sg[k * TV + v0 + u];
-      tmem_st16(taddr(tS0, 32 * quarter, v0), x);
-    }
+    for (int t = 0; t < 32; ++t) x[t] = Sg[k * TV + c0 + t];
+    tmem_st32(taddr(tS0, 32 * quarter, c0), x);
     tmem_wait_st();
   }
   for (int l = 0; l < L; ++l) refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
@@ -1006,23 +1000,23 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     __syncwarp();
 
     // U rows for epilogue 1, fetched while MMA1 runs.
-    uint4 urow[8];
+    uint4 urow[4];
     if (lane < 16) {
       const uint4* Ug = reinterpret_cast<const uint4*>(recg + lay.rec.U) +
-                        ((16 * quarter + lane) * TV + 64 * half) / 8;
+                        ((16 * quarter + lane) * TV + c0) / 8;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) urow[c] = __ldg(Ug + c);
+      for (int c = 0; c < 4; ++c) urow[c] = __ldg(Ug + c);
     }
     // Decay S0 in TMEM by e^(G_last) while MMA1 runs (naive.py:392, first term).
     {
       const int k = 32 * quarter + lane;
       const float e = reinterpret_cast<const float*>(recg + lay.rec.eg)[k];
-      const uint32_t ta = taddr(tS0, 32 * quarter, 64 * half);
-      float x[64];
-      tmem_ld64(ta, x);
+      const uint32_t ta = taddr(tS0, 32 * quarter, c0);
+      float x[32];
+      tmem_ld32(ta, x);
 #pragma unroll
-      for (int u = 0; u < 64; ++u) x[u] *= e;
-      tmem_st64(ta, x);
+      for (int t = 0; t < 32; ++t) x[t] *= e;
+      tmem_st32(ta, x);
       tmem_wait_st();
     }
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
@@ -1032,17 +1026,16 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376).
     {
       const int i = 16 * quarter + lane;
-      const int v0 = 64 * half;
-      float x[64];
-      tmem_ld64(taddr(tD, 32 * quarter, v0), x);
+      float x[32];
+      tmem_ld32(taddr(tD, 32 * quarter, c0), x);
       if (lane < 16) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float u[8];
-          unpack8(urow[c], NGDN2_BF16, u);
+        for (int c = 0; c < 4; ++c) {
+          float uu[8];
+          unpack8(urow[c], NGDN2_BF16, uu);
 #pragma unroll
-          for (int t = 0; t < 8; ++t) u[t] -= x[8 * c + t];
-          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, v0 + 8 * c, kC)) = pack8(u);
+          for (int t = 0; t < 8; ++t) uu[t] -= x[8 * c + t];
+          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, c0 + 8 * c, kC)) = pack8(uu);
         }
       }
     }
@@ -1075,29 +1068,28 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     // E2: output rows (lanes 16..31) and the new S0 (all lanes).
     {
       const int i = 16 * quarter + lane - 16, t = n * kC + i;
-      const int v0 = 64 * half;
-      float x[64];
-      tmem_ld64(taddr(tD, 32 * quarter, v0), x);
+      float x[32];
+      tmem_ld32(taddr(tD, 32 * quarter, c0), x);
       if (lane >= 16 && t < p.T) {
-        const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + v0;
+        const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + c0;
         if (p.dtype == NGDN2_BF16) {
           bf16* og = reinterpret_cast<bf16*>(p.o) + o;
 #pragma unroll
-          for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(og + c) = pack8(x + c);
+          for (int c = 0; c < 32; c += 8) *reinterpret_cast<uint4*>(og + c) = pack8(x + c);
         } else {
 #pragma unroll
-          for (int u = 0; u < 64; ++u) store_elem(p.o, o + u, x[u], p.dtype);
+          for (int u = 0; u < 32; ++u) store_elem(p.o, o + u, x[u], p.dtype);
         }
       }
       const int k = 32 * quarter + lane;
-      tmem_ld64(taddr(tS0, 32 * quarter, v0), x);
+      tmem_ld32(taddr(tS0, 32 * quarter, c0), x);
 #pragma unroll
-      for (int c = 0; c < 64; c += 8)
-        *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, v0 + c, TK)) = pack8(x + c);
+      for (int c = 0; c < 32; c += 8)
+        *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, c0 + c, TK)) = pack8(x + c);
       if (write_master) {
 #pragma unroll
-        for (int u = 0; u < 64; u += 4)
-          *reinterpret_cast<float4*>(Sg + k * TV + v0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
+        for (int u = 0; u < 32; u += 4)
+          *reinterpret_cast<float4*>(Sg + k * TV + c0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
       }
     }
     fence_proxy_async();
@@ -1110,14 +1102,14 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     if (fires) {
       for (int l = 1; l < L; ++l) {
         if ((n + 1) % p.firing[l] != 0) continue;
-        if (p.promotion == NGDN2_PROMOTION_MERGE) {
+        if (!learned) {
           promote_simt(p, b, h, l, Sg, sc, gsm);
           refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
           fence_proxy_async();
           __syncthreads();
         } else {
           promote_tc(p, lay, ws, h, l, tb, Sbf, Rec, Mt, &bar_ld, &bar_mma, ph_ld, ph_mma, egp,
-                     nrm, &abort_flag);
+                     red, &abort_flag);
         }
       }
       fence_before_sync();

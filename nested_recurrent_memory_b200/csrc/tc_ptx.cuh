@@ -170,6 +170,14 @@ __device__ __forceinline__ void tmem_regs_after_wait32(uint32_t* r) {
   asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) :: "memory");
 }
 
+// 32 consecutive columns, waited for, as floats.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  tmem_ld32_nowait(taddr, r);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  tmem_regs_after_wait32(r);
+}
+
 // 64 consecutive columns (two x32 loads, one wait) as floats.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
