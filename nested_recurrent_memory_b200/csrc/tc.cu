@@ -275,8 +275,8 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   __shared__ uint32_t tbase;
   __shared__ float mixs[3][kC];             // mix_l * scale per row
   __shared__ __align__(16) float rho[5][TK];  // G[16J + 7] for J = 0..3, then G[63]
-  __shared__ __align__(16) float rat[4][TK];  // e^(rho_J - rho_(J-1)) for J = 1..3; [0]: e^(G_63 - rho_3)
-  float* tot = rho[4];                        // G[31] carry; later overwritten by G[63]
+  // [0]: e^(G_63 - rho_3); [J]: e^(rho_J - rho_(J-1)), J = 1..3; [4 + I]: e^(rho_I)
+  __shared__ __align__(16) float rat[8][TK];
   float* Tt = reinterpret_cast<float*>(sm + P_TT);
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -293,21 +293,20 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     mixs[l][i] = (t0 + i < p.T) ? p.mix.at(b, t0 + i, h, l) * p.scale : 0.f;
   }
 
-  // Phase A mapping: lanes are rows (32 * rh + lane), each warp owns four
-  // 8-column chunks. 16-byte stores of 8 consecutive rows then fill one
-  // contiguous 128-byte core matrix, so shared stores are conflict-free and
-  // global stores coalesce.
-  const int rh = warp & 1, cw = warp >> 1;
-  const int r = 32 * rh + lane, t = t0 + r;
+  // Phase A mapping: warp w owns rows 8w .. 8w+7; lane = 8 * c4 + r8 holds
+  // row 8w + r8 and the 8-column chunks c4, c4 + 4, c4 + 8, c4 + 12. A warp
+  // load then touches 8 rows x 64 contiguous bytes, and the 16-byte shared
+  // stores of 8 consecutive lanes fill one contiguous 128-byte core matrix.
+  const int c4 = lane >> 3, r8 = lane & 7;
+  const int r = 8 * warp + r8, t = t0 + r;
   const bool valid = t < p.T;
 
-  // A1. G = cumsum of g along the chunk (naive.py:329): a warp scan over
-  //     lanes for each of this thread's 32 columns, plus the carry from rows
-  //     0..31 into rows 32..63.
+  // A1. G = cumsum of g along the chunk (naive.py:329): a scan over the 8
+  //     rows of each warp, then the carries of the row blocks above.
   float G[4][8];
 #pragma unroll
   for (int ci = 0; ci < 4; ++ci) {
-    const int d0 = 8 * (cw + 4 * ci);
+    const int d0 = 8 * (c4 + 4 * ci);
     if (valid) load8(p.g, b, t, h, d0, G[ci]);
     else {
 #pragma unroll
@@ -315,42 +314,52 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     }
   }
 #pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
+  for (int off = 1; off < 8; off <<= 1) {
 #pragma unroll
     for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float y = __shfl_up_sync(0xffffffffu, G[ci][u], off);
-        if (lane >= off) G[ci][u] += y;
+        const float y = __shfl_up_sync(0xffffffffu, G[ci][u], off, 8);
+        if (r8 >= off) G[ci][u] += y;
       }
   }
-  if (rh == 0 && lane == 31) {
+  float* carry = reinterpret_cast<float*>(sm + P_R);  // [8][128], before R is built
+  if (r8 == 7) {
 #pragma unroll
     for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
-      for (int u = 0; u < 8; ++u) tot[8 * (cw + 4 * ci) + u] = G[ci][u];
+      for (int u = 0; u < 8; ++u) carry[warp * TK + 8 * (c4 + 4 * ci) + u] = G[ci][u];
   }
   __syncthreads();
-  if (rh == 1) {
+  if (tid < TK) {
+    float run = 0.f;
 #pragma unroll
-    for (int ci = 0; ci < 4; ++ci)
-#pragma unroll
-      for (int u = 0; u < 8; ++u) G[ci][u] += tot[8 * (cw + 4 * ci) + u];
+    for (int w = 0; w < 8; ++w) {
+      const float c = carry[w * TK + tid];
+      carry[w * TK + tid] = run;
+      run += c;
+    }
   }
-  __syncthreads();  // the carry row is reused for G[63] below
-  // Reference points rho_J = G[16J + 7] (rows 7, 23, 39, 55) and G[63].
-  if (lane == 7 || lane == 23 || (rh == 1 && lane == 31)) {
-    const int slot = lane == 31 ? 4 : 2 * rh + (lane == 23);
+  __syncthreads();
+#pragma unroll
+  for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+    for (int u = 0; u < 8; ++u) G[ci][u] += carry[warp * TK + 8 * (c4 + 4 * ci) + u];
+  // Reference points rho_I = G[16I + 7] (row 7 of even warps) and G[63].
+  if (r8 == 7 && ((warp & 1) == 0 || warp == 7)) {
+    const int slot = warp == 7 ? 4 : warp >> 1;
 #pragma unroll
     for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
-      for (int u = 0; u < 8; ++u) rho[slot][8 * (cw + 4 * ci) + u] = G[ci][u];
+      for (int u = 0; u < 8; ++u) rho[slot][8 * (c4 + 4 * ci) + u] = G[ci][u];
   }
   __syncthreads();
   if (tid < TK) {
     rat[0][tid] = __expf(rho[4][tid] - rho[3][tid]);
 #pragma unroll
     for (int J = 1; J < 4; ++J) rat[J][tid] = __expf(rho[J][tid] - rho[J - 1][tid]);
+#pragma unroll
+    for (int I2 = 0; I2 < 4; ++I2) rat[4 + I2][tid] = __expf(rho[I2][tid]);
   }
   __syncthreads();
   const uint32_t tb = tbase;
@@ -371,7 +380,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   // Raw 16-byte chunks of q_0, k, b, v, w, q_1, q_2 for one column chunk;
   // the next chunk's loads are issued before the current one is used.
   auto fetch = [&](int ci, uint4* raw) {
-    const int d0 = 8 * (cw + 4 * ci);
+    const int d0 = 8 * (c4 + 4 * ci);
     if (valid) {
       raw[0] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, 0, d0), p.q.sd);
       raw[1] = raw8_at(p.k.p, p.k.dt, p.k.off(b, t, h, d0), p.k.sd);
@@ -391,7 +400,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
 #pragma unroll
   for (int ci = 0; ci < 4; ++ci) {
     if (ci < 3) fetch(ci + 1, nxt);
-    const int d0 = 8 * (cw + 4 * ci);
+    const int d0 = 8 * (c4 + 4 * ci);
     float qq[8], kk[8], bb[8], o1[8], o2[8], rr[8];
     unpack8(cur[0], p.q.dt, qq);
     unpack8(cur[1], p.k.dt, kk);
@@ -404,11 +413,12 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       rr[4] = a1.x; rr[5] = a1.y; rr[6] = a1.z; rr[7] = a1.w;
     }
     // Q_I, BK_I rows (MMA1 B operand)
+    float eq[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const float e = __expf(g[u] - rr[u]);
-      o1[u] = qq[u] * e;
-      o2[u] = bb[u] * kk[u] * e;
+      eq[u] = __expf(g[u] - rr[u]);
+      o1[u] = qq[u] * eq[u];
+      o2[u] = bb[u] * kk[u] * eq[u];
     }
     bf16* tile = QB + I * (32 * 128);
     *reinterpret_cast<uint4*>(tile + kmajor_off(r & 15, d0, 128)) = pack8(o1);
@@ -431,15 +441,19 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       for (int u = 0; u < 8; ++u) o1[u] = kk[u] * ech[u];
       *reinterpret_cast<uint4*>(KG + kgroup_elems(J) + kmajor_off(r, d0, 128)) = pack8(o1);
     }
-    // e^G: level-0 read query and the k*b*e^G half of R; w*v half of R
+    // e^G = e^(G - rho_I) e^(rho_I): level-0 read query and the k*b*e^G half
+    // of R; w*v half of R
     {
       float vv[8], ww[8];
       unpack8(cur[3], p.v.dt, vv);
       unpack8(cur[4], p.w.dt, ww);
       const float m0 = mixs[0][r];
+      const float4* ep = reinterpret_cast<const float4*>(&rat[4 + I][d0]);
+      const float4 e0 = ep[0], e1 = ep[1];
+      const float er[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float e = __expf(g[u]);
+        const float e = eq[u] * er[u];
         o1[u] = m0 * qq[u] * e;
         o2[u] = kk[u] * bb[u] * e;
         ww[u] *= vv[u];
