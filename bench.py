@@ -201,6 +201,34 @@ def run_reference(args, w):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# multi-GPU plumbing (one process per GPU; no data-path collective)
+# ---------------------------------------------------------------------------
+
+def shard(world, rank, w):
+    """Weak scaling: every rank runs the configuration's per-GPU batch on its
+    own seeded rows of a global batch of ``world * B`` sequences; (b, h)
+    states are independent, so no rank needs another's data."""
+    return {"seed": 1000 + rank, "rows": (rank * w["B"], (rank + 1) * w["B"]),
+            "global_batch": world * w["B"]}
+
+
+def max_over_ranks(value, world, device="cpu"):
+    """Max of a per-rank scalar over the process group (any backend)."""
+    if world <= 1:
+        return float(value)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_tokens_per_s(w, world, ms_per_step):
+    """Whole-job tokens/s: all ranks' tokens over the slowest rank's time."""
+    return world * w["B"] * w["T"] / (ms_per_step / 1e3)
+
+
 def config_dict(args, w):
     return {
         "workload": (f"{args.config}: B={w['B']} per GPU, T={w['T']}, H={w['H']}, "
@@ -237,8 +265,9 @@ def run_ours(args, w):
             dist.barrier()
         torch.cuda.synchronize()
 
+    plan = shard(world, rank, w)
     inp = config_inputs(w["B"], w["T"], w["H"], w["K"], w["V"], w["L"], w["m"], w["firing"],
-                        dtype=w["dtype"], seed=1000 + rank, device=dev, gen_device=dev)
+                        dtype=w["dtype"], seed=plan["seed"], device=dev, gen_device=dev)
     L = inp.pop("L")
     call = FwdCall(**inp, L=L, path=args.path)
     launches_per_step = call.num_launches
@@ -259,14 +288,10 @@ def run_ours(args, w):
     end.record()
     barrier()
     clk = clocks.stop()
-    ms = start.elapsed_time(end)
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(start.elapsed_time(end), world, dev)
     ms_step = ms_max / args.steps
     tokens_per_step = w["B"] * w["T"] * world
-    value = tokens_per_step / (ms_step / 1e3)
+    value = job_tokens_per_s(w, world, ms_step)
 
     # Per-stage timing on the launching stream (stage 1 = prep, 2 = scan).
     stage_ms = {1: 0.0, 2: 0.0}
@@ -312,10 +337,8 @@ def run_ours(args, w):
             e2e_step()
         e1.record()
         barrier()
-        te = torch.tensor([e0.elapsed_time(e1)], device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": tokens_per_step / (float(te.item()) / args.steps / 1e3), "unit": "tokens/s",
+        te = max_over_ranks(e0.elapsed_time(e1), world, dev)
+        e2e = {"value": job_tokens_per_s(w, world, te / args.steps), "unit": "tokens/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
 
     peaks, peak_src = load_peaks()

@@ -137,3 +137,17 @@ def test_status_word_stays_clear():
     call.launch()
     torch.cuda.synchronize()
     assert int(status.item()) == 0
+
+
+def test_fp32_decay_with_bf16_inputs():
+    """The layer hands over g in fp32 (nested_gdn2.py:142-148) next to bf16
+    q/k/v/b/w; the tensor-core path reads each tensor in its own dtype."""
+    inp = config_inputs(1, 320, 2, 128, 128, 3, 32, (1, 2, 4), dtype=torch.bfloat16, seed=12,
+                        gate_proj_std=128 ** -0.5)
+    inp.pop("L")
+    inp["g"] = torch.nn.functional.logsigmoid(
+        torch.randn(1, 320, 2, 128, generator=torch.Generator().manual_seed(13)) + 1.0)
+    o, s = _run(inp, 3)
+    ro, rs = _oracle(inp, 3)
+    assert rel_err(_np(o), ro) < LOWP_REL
+    assert rel_err(_np(s), rs) < LOWP_REL
