@@ -300,6 +300,36 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   const int c4 = lane >> 3, r8 = lane & 7;
   const int r = 8 * warp + r8, t = t0 + r;
   const bool valid = t < p.T;
+  bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
+  bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
+
+  // The upper-level queries q_1, q_2 need no decay: their loads go out
+  // first, next to those of g, and they are written while G is formed.
+  uint4 qup[2][4];
+#pragma unroll
+  for (int l = 1; l < 3; ++l)
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci)
+      qup[l - 1][ci] = (valid && l < p.L)
+                           ? raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, l, 8 * (c4 + 4 * ci)), p.q.sd)
+                           : make_uint4(0, 0, 0, 0);
+
+  // Raw 16-byte chunks of q_0, k, b, v, w for one column chunk; each
+  // chunk's loads are issued one chunk ahead of their use.
+  auto fetch = [&](int ci, uint4* raw) {
+    const int d0 = 8 * (c4 + 4 * ci);
+    if (valid) {
+      raw[0] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, 0, d0), p.q.sd);
+      raw[1] = raw8_at(p.k.p, p.k.dt, p.k.off(b, t, h, d0), p.k.sd);
+      raw[2] = raw8_at(p.b.p, p.b.dt, p.b.off(b, t, h, d0), p.b.sd);
+      raw[3] = raw8_at(p.v.p, p.v.dt, p.v.off(b, t, h, d0), p.v.sd);
+      raw[4] = raw8_at(p.w.p, p.w.dt, p.w.off(b, t, h, d0), p.w.sd);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 5; ++i) raw[i] = make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 cur[5], nxt[5];
 
   // A1. G = cumsum of g along the chunk (naive.py:329): a scan over the 8
   //     rows of each warp, then the carries of the row blocks above.
@@ -331,6 +361,22 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       for (int u = 0; u < 8; ++u) carry[warp * TK + 8 * (c4 + 4 * ci) + u] = G[ci][u];
   }
   __syncthreads();
+  // Upper-level read queries mix_l * scale * q_l to the record (mixs is
+  // visible after the barrier above); then the first column chunk's loads.
+#pragma unroll
+  for (int l = 1; l < 3; ++l) {
+    if (l >= p.L) continue;
+    const float ml = mixs[l][r];
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci) {
+      float qq[8];
+      unpack8(qup[l - 1][ci], p.q.dt, qq);
+      scale8(qq, ml);
+      *reinterpret_cast<uint4*>(Qg + l * (kC * 128) + kmajor_off(r, 8 * (c4 + 4 * ci), 128)) =
+          pack8(qq);
+    }
+  }
+  fetch(0, cur);
   if (tid < TK) {
     float run = 0.f;
 #pragma unroll
@@ -374,29 +420,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   bf16* KG = reinterpret_cast<bf16*>(sm + P_KG);
   bf16* QB = reinterpret_cast<bf16*>(sm + P_QB);
   bf16* Rs = reinterpret_cast<bf16*>(sm + P_R);
-  bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
-  bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
   const int I = r >> 4;
-  // Raw 16-byte chunks of q_0, k, b, v, w, q_1, q_2 for one column chunk;
-  // the next chunk's loads are issued before the current one is used.
-  auto fetch = [&](int ci, uint4* raw) {
-    const int d0 = 8 * (c4 + 4 * ci);
-    if (valid) {
-      raw[0] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, 0, d0), p.q.sd);
-      raw[1] = raw8_at(p.k.p, p.k.dt, p.k.off(b, t, h, d0), p.k.sd);
-      raw[2] = raw8_at(p.b.p, p.b.dt, p.b.off(b, t, h, d0), p.b.sd);
-      raw[3] = raw8_at(p.v.p, p.v.dt, p.v.off(b, t, h, d0), p.v.sd);
-      raw[4] = raw8_at(p.w.p, p.w.dt, p.w.off(b, t, h, d0), p.w.sd);
-#pragma unroll
-      for (int l = 1; l < 3; ++l)
-        if (l < p.L) raw[4 + l] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, l, d0), p.q.sd);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 7; ++i) raw[i] = make_uint4(0, 0, 0, 0);
-    }
-  };
-  uint4 cur[7], nxt[7];
-  fetch(0, cur);
 #pragma unroll
   for (int ci = 0; ci < 4; ++ci) {
     if (ci < 3) fetch(ci + 1, nxt);
@@ -472,17 +496,9 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       for (int u = 0; u < 8; ++u) o1[u] = kk[u] * ech[u] * rj[u];
     }
     *reinterpret_cast<uint4*>(Ktg + mnmajor_off(r, d0, 64)) = pack8(o1);
-    // upper-level read queries mix_l * scale * q_l
-#pragma unroll
-    for (int l = 1; l < 3; ++l) {
-      if (l >= p.L) continue;
-      unpack8(cur[4 + l], p.q.dt, qq);
-      scale8(qq, mixs[l][r]);
-      *reinterpret_cast<uint4*>(Qg + l * (kC * 128) + kmajor_off(r, d0, 128)) = pack8(qq);
-    }
     if (ci < 3) {
 #pragma unroll
-      for (int i = 0; i < 7; ++i) cur[i] = nxt[i];
+      for (int i = 0; i < 5; ++i) cur[i] = nxt[i];
     }
   }
   if (tid < TK) reinterpret_cast<float*>(rec + lay.rec.eg)[tid] = __expf(rho[4][tid]);
