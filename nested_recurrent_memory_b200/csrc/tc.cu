@@ -184,6 +184,18 @@ __device__ __forceinline__ uint4 pack8(const float* x) {
   return r;
 }
 
+// Pack 8 floats as 8 fp16 (16 bytes).
+__device__ __forceinline__ uint4 pack8h(const float* x) {
+  uint4 r;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 hh = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&hh);
+  }
+  return r;
+}
+
 }  // namespace
 }  // namespace ngdn2
 
@@ -989,7 +1001,9 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   fence_after_sync();
   const uint32_t tb = tbase;
   const uint32_t tS0 = tb;        // S0 [K lanes x V cols], fp32
-  const uint32_t tD = tb + 128;   // lanes +0: W.S0 (M=64); lanes +16: output (M=64)
+  // Chunk accumulator, one M = 128 tile: lanes 0..63 W.S0, lanes 64..127
+  // the output rows.
+  const uint32_t tD = tb + 128;
 
   // S0 into TMEM, bf16 copies of every level into shared memory.
   {
@@ -1006,9 +1020,13 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   __syncthreads();
   fence_after_sync();
 
-  const uint32_t id_read = idesc_f16(64, 128, true, false, true);    // [64 x K] . [K x V]
-  const uint32_t id_state = idesc_f16(128, 128, true, true, true);   // K_tail^T [K x 64] . [64 x V]
+  const uint32_t id_m128 = idesc_f16(128, 128, true, false, true);  // [128 x K] . [K x V]
+  const uint32_t id_state = idesc_f16(128, 128, true, true, true);  // K_tail^T [K x 64] . [64 x V]
   uint32_t ph_ld = 0, ph_mma = 0;
+  // Chunks left until each level's next firing (naive.py:394-415 fires level
+  // l after chunk n when (n + 1) % f_l == 0).
+  // (this family has L <= 3).
+  int left1 = L > 1 ? p.firing[1] : 0, left2 = L > 2 ? p.firing[2] : 0;
   if (tid == 0 && p.NT > 0) {
     mbar_arrive_expect_tx(&bar_ld, load_bytes);
     bulk_g2s(Rec, rec0, load_bytes, &bar_ld);
@@ -1017,23 +1035,32 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     const char* recg = rec0 + int64_t(n) * lay.rec.size;
     if (!mbar_wait(&bar_ld, ph_ld)) abort_flag = 1;
     ph_ld ^= 1;
+    uint32_t fire_mask = 0;
+    if (L > 1 && --left1 == 0) {
+      fire_mask |= 2u;
+      left1 = p.firing[1];
+    }
+    if (L > 2 && --left2 == 0) {
+      fire_mask |= 4u;
+      left2 = p.firing[2];
+    }
+    const bool fires = fire_mask != 0;
 
-    // MMA1: W.S0 and the multi-level read (naive.py:376, 379, 382-385).
+    // MMA1: [W; Q_0] . S0 as one M = 128 tile (W and Q_0 are adjacent in the
+    // record): W.S0 in lanes 0..63 and the level-0 read in lanes 64..127,
+    // both from the state entering the chunk (naive.py:376, 379).
     if (tid == 0) {
       fence_after_sync();
-      mma_tile(tD, smem_u32(Rec + lay.rec.W), smem_u32(Sbf), TK, id_read, false);
-      for (int l = 0; l < L; ++l)
-        mma_tile(tD + (16u << 16), smem_u32(Rec + lay.rec.Q + l * TILE_QK),
-                 smem_u32(Sbf + l * TK * TV), TK, id_read, l > 0);
+      mma_tile(tD, smem_u32(Rec + lay.rec.W), smem_u32(Sbf), TK, id_m128, false);
       mma_commit(&bar_mma);
     }
     __syncwarp();
 
     // U rows for epilogue 1, fetched while MMA1 runs.
     uint4 urow[4];
-    if (lane < 16) {
+    if (quarter < 2) {
       const uint4* Ug = reinterpret_cast<const uint4*>(recg + lay.rec.U) +
-                        ((16 * quarter + lane) * TV + c0) / 8;
+                        ((32 * quarter + lane) * TV + c0) / 8;
 #pragma unroll
       for (int c = 0; c < 4; ++c) urow[c] = __ldg(Ug + c);
     }
@@ -1054,19 +1081,17 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     fence_after_sync();
 
     // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376).
-    {
-      const int i = 16 * quarter + lane;
+    if (quarter < 2) {
+      const int i = 32 * quarter + lane;
       float x[32];
       tmem_ld32(taddr(tD, 32 * quarter, c0), x);
-      if (lane < 16) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float uu[8];
-          unpack8(urow[c], NGDN2_BF16, uu);
+      for (int c = 0; c < 4; ++c) {
+        float uu[8];
+        unpack8(urow[c], NGDN2_BF16, uu);
 #pragma unroll
-          for (int t = 0; t < 8; ++t) uu[t] -= x[8 * c + t];
-          *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, c0 + 8 * c, kC)) = pack8(uu);
-        }
+        for (int t = 0; t < 8; ++t) uu[t] -= x[8 * c + t];
+        *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, c0 + 8 * c, kC)) = pack8(uu);
       }
     }
     fence_proxy_async();
@@ -1074,19 +1099,24 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     __syncthreads();
     if (abort_flag) break;
 
-    // MMA2: o += (mix0 scale A_qk) v_new; S0 += K_tail^T v_new (naive.py:379, 392).
+    // MMA2: S0 += K_tail^T v_new (naive.py:392); then the rest of the output
+    // into lanes 64..127: the upper-level reads (naive.py:382-385) and
+    // (mix0 scale A_qk) v_new (naive.py:379). Each of those A operands is the
+    // lower half of an M = 128 tile whose upper half (the 64 rows stored
+    // before it) only adds to the spent W.S0 lanes.
     if (tid == 0) {
       fence_after_sync();
-      mma_tile(tD + (16u << 16), smem_u32(Rec + lay.rec.A), smem_u32(Vn), kC, id_read, true);
       mma_tile(tS0, smem_u32(Rec + lay.rec.Kt), smem_u32(Vn), kC, id_state, true);
+      for (int l = 1; l < L; ++l)
+        mma_tile(tD, smem_u32(Rec + lay.rec.Q + (l - 1) * TILE_QK), smem_u32(Sbf + l * TK * TV), TK,
+                 id_m128, true);
+      mma_tile(tD, smem_u32(Rec + lay.rec.A - TILE_A), smem_u32(Vn), kC, id_m128, true);
       mma_commit(&bar_mma);
     }
     __syncwarp();
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
-    bool fires = false;
-    for (int l = 1; l < L; ++l) fires |= ((n + 1) % p.firing[l]) == 0;
     // The next record streams in during the epilogue, unless a promotion
     // needs the record buffer as scratch first.
     if (tid == 0 && n + 1 < p.NT && !fires) {
@@ -1094,19 +1124,26 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       bulk_g2s(Rec, recg + lay.rec.size, load_bytes, &bar_ld);
     }
     const bool write_master = (fires && !learned) || n + 1 == p.NT;
+    const bool stage16 = p.dtype == NGDN2_BF16 || p.dtype == NGDN2_F16;
 
-    // E2: output rows (lanes 16..31) and the new S0 (all lanes).
+    // E2: output rows (lanes 64..127) and the new S0 (all lanes). 16-bit
+    // outputs go through shared memory (the spent v_new tile, rows of 256
+    // bytes with 16-byte chunks XOR-swizzled by row) so that the global
+    // stores are whole rows.
     {
-      const int i = 16 * quarter + lane - 16, t = n * kC + i;
       float x[32];
-      tmem_ld32(taddr(tD, 32 * quarter, c0), x);
-      if (lane >= 16 && t < p.T) {
-        const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + c0;
-        if (p.dtype == NGDN2_BF16) {
-          bf16* og = reinterpret_cast<bf16*>(p.o) + o;
+      if (quarter >= 2) {
+        const int i = 32 * (quarter - 2) + lane, t = n * kC + i;
+        tmem_ld32(taddr(tD, 32 * quarter, c0), x);
+        if (stage16) {
+          uint4* row = reinterpret_cast<uint4*>(Vn) + i * 16;
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) *reinterpret_cast<uint4*>(og + c) = pack8(x + c);
-        } else {
+          for (int c = 0; c < 4; ++c) {
+            const int ch = (c0 >> 3) + c;
+            row[ch ^ (i & 15)] = p.dtype == NGDN2_BF16 ? pack8(x + 8 * c) : pack8h(x + 8 * c);
+          }
+        } else if (t < p.T) {
+          const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + c0;
 #pragma unroll
           for (int u = 0; u < 32; ++u) store_elem(p.o, o + u, x[u], p.dtype);
         }
@@ -1122,6 +1159,17 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
           *reinterpret_cast<float4*>(Sg + k * TV + c0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
       }
     }
+    if (stage16) {
+      __syncthreads();
+      // 64 rows x 16 chunks of 16 bytes: each warp stores two whole rows per step.
+      for (int e = tid; e < kC * 16; e += kScanThreads) {
+        const int i = e >> 4, ch = e & 15, t = n * kC + i;
+        if (t < p.T) {
+          const uint4 v = reinterpret_cast<const uint4*>(Vn)[i * 16 + (ch ^ (i & 15))];
+          *(reinterpret_cast<uint4*>(p.o) + (((int64_t(b) * p.T + t) * p.H + h) * TV) / 8 + ch) = v;
+        }
+      }
+    }
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
@@ -1131,7 +1179,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     // Promotions at this chunk's firings, bottom-up (naive.py:394-415).
     if (fires) {
       for (int l = 1; l < L; ++l) {
-        if ((n + 1) % p.firing[l] != 0) continue;
+        if (!(fire_mask >> l & 1u)) continue;
         if (!learned) {
           promote_simt(p, b, h, l, Sg, sc, gsm);
           refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
