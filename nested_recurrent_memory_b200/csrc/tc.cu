@@ -958,7 +958,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
 __global__ void __launch_bounds__(kScanThreads, 1)
 scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ uint64_t bar_ld, bar_mma;
+  __shared__ uint64_t bar_ld, bar_ld2, bar_mma;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   __shared__ float egp[128];
@@ -984,6 +984,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   if (warp == 0) tmem_alloc(&tbase, kScanCols);
   if (tid == 0) {
     mbar_init(&bar_ld, 1);
+    mbar_init(&bar_ld2, 1);
     mbar_init(&bar_mma, 1);
     fence_mbar_init();
     abort_flag = 0;
@@ -1027,9 +1028,49 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   // l after chunk n when (n + 1) % f_l == 0).
   // (this family has L <= 3).
   int left1 = L > 1 ? p.firing[1] : 0, left2 = L > 2 ? p.firing[2] : 0;
+  // A record arrives in two parts: [W, Q_0] (read by MMA1) on bar_ld and
+  // the rest (read by MMA2) on bar_ld2, so each part of the next record can
+  // stream in as soon as its MMA has finished with the current one.
+  const uint32_t part_a = static_cast<uint32_t>(lay.rec.Q + TILE_QK);
+  auto load_part = [&](const char* src, bool a) {
+    const uint32_t lo = a ? 0u : part_a, hi = a ? part_a : load_bytes;
+    uint64_t* bar = a ? &bar_ld : &bar_ld2;
+    mbar_arrive_expect_tx(bar, hi - lo);
+    bulk_g2s(Rec + lo, src + lo, hi - lo, bar);
+  };
+  uint32_t ph_ld2 = 0;
   if (tid == 0 && p.NT > 0) {
-    mbar_arrive_expect_tx(&bar_ld, load_bytes);
-    bulk_g2s(Rec, rec0, load_bytes, &bar_ld);
+    load_part(rec0, true);
+    load_part(rec0, false);
+  }
+  // U rows (lanes of quarters 0 and 1) and e^(G_last) of a chunk, read from
+  // its record in global memory one chunk ahead of use.
+  uint4 urow[4];
+  float eg = 0.f;
+  auto fetch_u = [&](int nn) {
+    const char* rg = rec0 + int64_t(nn) * lay.rec.size;
+    if (quarter < 2) {
+      const uint4* Ug = reinterpret_cast<const uint4*>(rg + lay.rec.U) +
+                        ((32 * quarter + lane) * TV + c0) / 8;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) urow[c] = __ldg(Ug + c);
+    }
+    eg = __ldg(reinterpret_cast<const float*>(rg + lay.rec.eg) + 32 * quarter + lane);
+  };
+  // S0 decayed by the first chunk's e^(G_last) (naive.py:392, first term);
+  // each later chunk's decay is applied where the previous epilogue reads S0.
+  if (p.NT > 0) {
+    fetch_u(0);
+    const uint32_t ta = taddr(tS0, 32 * quarter, c0);
+    float x[32];
+    tmem_ld32(ta, x);
+#pragma unroll
+    for (int t = 0; t < 32; ++t) x[t] *= eg;
+    tmem_st32(ta, x);
+    tmem_wait_st();
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
   }
   for (int n = 0; n < p.NT; ++n) {
     const char* recg = rec0 + int64_t(n) * lay.rec.size;
@@ -1055,30 +1096,12 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       mma_commit(&bar_mma);
     }
     __syncwarp();
-
-    // U rows for epilogue 1, fetched while MMA1 runs.
-    uint4 urow[4];
-    if (quarter < 2) {
-      const uint4* Ug = reinterpret_cast<const uint4*>(recg + lay.rec.U) +
-                        ((32 * quarter + lane) * TV + c0) / 8;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) urow[c] = __ldg(Ug + c);
-    }
-    // Decay S0 in TMEM by e^(G_last) while MMA1 runs (naive.py:392, first term).
-    {
-      const int k = 32 * quarter + lane;
-      const float e = reinterpret_cast<const float*>(recg + lay.rec.eg)[k];
-      const uint32_t ta = taddr(tS0, 32 * quarter, c0);
-      float x[32];
-      tmem_ld32(ta, x);
-#pragma unroll
-      for (int t = 0; t < 32; ++t) x[t] *= e;
-      tmem_st32(ta, x);
-      tmem_wait_st();
-    }
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
+    // W and Q_0 are spent: the next record's first part streams in (unless
+    // a promotion needs the buffer as scratch first).
+    if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, true);
 
     // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376).
     if (quarter < 2) {
@@ -1094,6 +1117,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
         *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, c0 + 8 * c, kC)) = pack8(uu);
       }
     }
+    if (n + 1 < p.NT) fetch_u(n + 1);
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
@@ -1105,6 +1129,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     // lower half of an M = 128 tile whose upper half (the 64 rows stored
     // before it) only adds to the spent W.S0 lanes.
     if (tid == 0) {
+      if (!mbar_wait(&bar_ld2, ph_ld2)) abort_flag = 1;
       fence_after_sync();
       mma_tile(tS0, smem_u32(Rec + lay.rec.Kt), smem_u32(Vn), kC, id_state, true);
       for (int l = 1; l < L; ++l)
@@ -1113,16 +1138,13 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       mma_tile(tD, smem_u32(Rec + lay.rec.A - TILE_A), smem_u32(Vn), kC, id_m128, true);
       mma_commit(&bar_mma);
     }
+    ph_ld2 ^= 1;
     __syncwarp();
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
-    // The next record streams in during the epilogue, unless a promotion
-    // needs the record buffer as scratch first.
-    if (tid == 0 && n + 1 < p.NT && !fires) {
-      mbar_arrive_expect_tx(&bar_ld, load_bytes);
-      bulk_g2s(Rec, recg + lay.rec.size, load_bytes, &bar_ld);
-    }
+    // The rest of the next record streams in during the epilogue.
+    if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, false);
     const bool write_master = (fires && !learned) || n + 1 == p.NT;
     const bool stage16 = p.dtype == NGDN2_BF16 || p.dtype == NGDN2_F16;
 
@@ -1148,8 +1170,11 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
           for (int u = 0; u < 32; ++u) store_elem(p.o, o + u, x[u], p.dtype);
         }
       }
+      // The new S0: bf16 copy (and fp32 master), then S0 in TMEM decayed
+      // by the next chunk's e^(G_last).
       const int k = 32 * quarter + lane;
-      tmem_ld32(taddr(tS0, 32 * quarter, c0), x);
+      const uint32_t ta = taddr(tS0, 32 * quarter, c0);
+      tmem_ld32(ta, x);
 #pragma unroll
       for (int c = 0; c < 32; c += 8)
         *reinterpret_cast<uint4*>(Sbf + mnmajor_off(k, c0 + c, TK)) = pack8(x + c);
@@ -1157,6 +1182,12 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
 #pragma unroll
         for (int u = 0; u < 32; u += 4)
           *reinterpret_cast<float4*>(Sg + k * TV + c0 + u) = make_float4(x[u], x[u + 1], x[u + 2], x[u + 3]);
+      }
+      if (n + 1 < p.NT) {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) x[t] *= eg;
+        tmem_st32(ta, x);
+        tmem_wait_st();
       }
     }
     if (stage16) {
@@ -1195,8 +1226,8 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       fence_after_sync();
       if (abort_flag) break;
       if (tid == 0 && n + 1 < p.NT) {
-        mbar_arrive_expect_tx(&bar_ld, load_bytes);
-        bulk_g2s(Rec, recg + lay.rec.size, load_bytes, &bar_ld);
+        load_part(recg + lay.rec.size, true);
+        load_part(recg + lay.rec.size, false);
       }
     }
   }
