@@ -106,6 +106,29 @@ __device__ __forceinline__ float fast_sigmoid(float x) {
 __device__ __forceinline__ float fast_softplus(float x) {
   return x > 20.f ? x : __logf(1.f + __expf(x));
 }
+// softplus(x) = max(x, 0) + log1p(e^-|x|) with one hardware exponential and
+// log1p on [0, 1] as z * q(z), q of degree 7: a least-squares fit on 4000
+// Chebyshev nodes (max abs error 1.4e-7 evaluated in fp32 Horner form).
+__device__ __forceinline__ float softplus_poly(float x) {
+  const float z = __expf(-fabsf(x));
+  float q = -0.0064523066f;
+  q = fmaf(q, z, 0.03608331f);
+  q = fmaf(q, z, -0.09532055f);
+  q = fmaf(q, z, 0.16764624f);
+  q = fmaf(q, z, -0.24073002f);
+  q = fmaf(q, z, 0.33179808f);
+  q = fmaf(q, z, -0.49987403f);
+  q = fmaf(q, z, 0.9999964f);
+  return fmaxf(x, 0.f) + q * z;
+}
+// sigmoid(x) = (1 + tanh(x / 2)) / 2 with the hardware tanh (absolute error
+// about 2.5e-4): used for the write gate, whose values sit near 1/2 and
+// only scale a bf16 operand.
+__device__ __forceinline__ float sigmoid_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return fmaf(0.5f, t, 0.5f);
+}
 
 // 8 consecutive elements starting at element offset ``o`` (element stride
 // ``sd``), as fp32. Uses one 16-byte load when the data are contiguous and
@@ -700,6 +723,24 @@ __device__ __forceinline__ void refresh_copy(bf16* dst, const float* src) {
   }
 }
 
+// First operands of a learned promotion of level l: the query bank (K-major,
+// padded to 64 or 128 rows) and [W_w | W_g], into the promotion scratch X.
+// Issued by one thread; completion arrives on ``bar_ld``.
+__device__ __forceinline__ void promote_tc_first_loads(const FwdParams& p, const TcLayout& lay,
+                                                       const char* ws, int h, int l, uint8_t* X,
+                                                       uint64_t* bar_ld) {
+  const int mp = pad_pairs(p.nq[l - 1]);
+  const char* pt = ws + lay.ptc_off + (int64_t(l - 1) * p.H + h) * PT_SIZE;
+  mbar_arrive_expect_tx(bar_ld, uint32_t(mp * 256 + 65536));
+  bulk_g2s(X + 65536, pt + PT_QB, uint32_t(mp * 256), bar_ld);
+  bulk_g2s(X, pt + PT_W2B, 65536u, bar_ld);
+}
+
+// Gate partials of a 64-pair promotion, fp16, at this offset of the scratch
+// (after the 64-row bank): [64 pairs][64 column pairs] 32-bit words with the
+// column-pair index XOR-swizzled by row.
+constexpr int kGpartOff = 65536 + 16384;
+
 // Learned promotion of level l - 1 into level l on the tensor cores
 // (probe.py:69-102 with _gates :34-66, then update_fwd.py:120-123):
 //   P1  V'  = Q_bank . S_{l-1}
@@ -717,7 +758,7 @@ __device__ __forceinline__ void refresh_copy(bf16* dst, const float* src) {
 __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* ws, int h, int l,
                            uint32_t tb, bf16* Sbf, uint8_t* X, float* Mt, uint64_t* bar_ld,
                            uint64_t* bar_mma, uint32_t& ph_ld, uint32_t& ph_mma, float* egp,
-                           float* red, int* abort_flag) {
+                           float* red, int* abort_flag, bool loaded) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, c0 = 32 * (warp >> 2);
   const int nq = p.nq[l - 1], mp = pad_pairs(nq);
@@ -733,12 +774,8 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   const uint32_t id_half = idesc_f16(64, 128, true, false, false);
   const uint32_t id_upd = idesc_f16(128, 128, true, true, true);
 
-  // Query bank and [W_w | W_g] in.
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_ld, uint32_t(mp * 256 + 65536));
-    bulk_g2s(XQ, pt + PT_QB, uint32_t(mp * 256), bar_ld);
-    bulk_g2s(XW, pt + PT_W2B, 65536u, bar_ld);
-  }
+  // Query bank and [W_w | W_g] in (issued by the caller when ``loaded``).
+  if (tid == 0 && !loaded) promote_tc_first_loads(p, lay, ws, h, l, X, bar_ld);
   if (!mbar_wait(bar_ld, ph_ld)) *abort_flag = 1;
   ph_ld ^= 1;
   // P1
@@ -779,35 +816,60 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
   ph_mma ^= 1;
   fence_after_sync();
+  // With 64 pairs [W_w | W_g] is spent now: [W_k^T | W_b] streams in while
+  // the gates are formed (their partials live past the bank).
+  if (split && tid == 0) {
+    mbar_arrive_expect_tx(bar_ld, 65536u);
+    bulk_g2s(XW, pt + PT_W2A, 65536u, bar_ld);
+  }
   // v * w back into TMEM; -softplus(g_logit - 4) per pair into shared memory
   // (columns XOR-swizzled by row so both the row writes and the column sums
   // are free of bank conflicts).
   float* gpart = reinterpret_cast<float*>(X);
+  uint32_t* gpart16 = reinterpret_cast<uint32_t*>(X + kGpartOff);
   {
     float a[32], vp[32];
     if (split) {
+      // Lane l < 16 holds the w logits of pair 16q + l, lane l + 16 its g
+      // logits. The two lanes swap halves so that each forms 16 of both
+      // gates (no divergence): the low lane takes columns 0..15, the high
+      // lane 16..31; the high lane hands its w gates back for v * w.
       tmem_ld32(taddr(tG, 32 * quarter, c0), a);
+      const bool hi = lane >= 16;
+      const int gr = 16 * quarter + (lane & 15), cb = c0 + (hi ? 16 : 0);
+      float sw[16];
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        float gg[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float mine_w = hi ? 0.f : a[j + e], mine_g = hi ? a[16 + j + e] : 0.f;
+          const float got = __shfl_xor_sync(0xffffffffu, hi ? a[j + e] : a[16 + j + e], 16);
+          const float wl = hi ? got : mine_w, gl = hi ? mine_g : got;
+          sw[j + e] = sigmoid_tanh(wl + kWLogitInit);
+          gg[e] = -softplus_poly(gl + kGLogitInit);
+        }
+        const __half2 g2 = __floats2half2_rn(gg[0], gg[1]);
+        gpart16[gr * 64 + (((cb + j) >> 1) ^ (gr & 31))] = *reinterpret_cast<const uint32_t*>(&g2);
+      }
       tmem_ld32(taddr(tV, 32 * quarter, c0), vp);
-      if (lane < 16) {
 #pragma unroll
-        for (int u = 0; u < 32; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
-      } else {
-        const int gr = 16 * quarter + lane - 16;
-#pragma unroll
-        for (int u = 0; u < 32; ++u)
-          gpart[gr * 128 + ((c0 + u) ^ (gr & 31))] = -fast_softplus(a[u] + kGLogitInit);
+      for (int j = 0; j < 16; ++j) {
+        const float back = __shfl_xor_sync(0xffffffffu, sw[j], 16);
+        vp[j] *= sw[j];
+        vp[16 + j] *= back;
       }
       tmem_st32(taddr(tV, 32 * quarter, c0), vp);  // lanes 16..31 of tV are unused
     } else {
       tmem_ld32(taddr(tV, 32 * quarter, c0), vp);
       tmem_ld32(taddr(tG, 32 * quarter, c0), a);
 #pragma unroll
-      for (int u = 0; u < 32; ++u) vp[u] *= fast_sigmoid(a[u] + kWLogitInit);
+      for (int u = 0; u < 32; ++u) vp[u] *= sigmoid_tanh(a[u] + kWLogitInit);
       tmem_st32(taddr(tV, 32 * quarter, c0), vp);
       tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), a);
 #pragma unroll
       for (int u = 0; u < 32; ++u)
-        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -fast_softplus(a[u] + kGLogitInit);
+        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -softplus_poly(a[u] + kGLogitInit);
     }
   }
   tmem_wait_st();
@@ -816,7 +878,13 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
     // g = mean over the real pairs, four threads per column.
     const int k = tid & 127, qq = tid >> 7, r0 = qq * (nq >> 2), r1 = r0 + (nq >> 2);
     float s = 0.f;
-    for (int r = r0; r < r1; ++r) s += gpart[r * 128 + (k ^ (r & 31))];
+    if (split) {
+      const __half* g16 = reinterpret_cast<const __half*>(gpart16);
+      for (int r = r0; r < r1; ++r)
+        s += __half2float(g16[2 * (r * 64 + ((k >> 1) ^ (r & 31))) + (k & 1)]);
+    } else {
+      for (int r = r0; r < r1; ++r) s += gpart[r * 128 + (k ^ (r & 31))];
+    }
     red[qq * 128 + k] = s;
   }
   __syncthreads();
@@ -824,8 +892,8 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
     egp[tid] = expf((red[tid] + red[128 + tid] + red[256 + tid] + red[384 + tid]) / float(nq));
   fence_proxy_async();
   __syncthreads();
-  // [W_k^T | W_b] in over the gate scratch.
-  if (tid == 0) {
+  // [W_k^T | W_b] in over the gate scratch (128 pairs).
+  if (tid == 0 && !split) {
     mbar_arrive_expect_tx(bar_ld, 65536u);
     bulk_g2s(XW, pt + PT_W2A, 65536u, bar_ld);
   }
@@ -847,9 +915,9 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   ph_mma ^= 1;
   fence_after_sync();
   // keys = u / max(|u|, 1e-12) (probe.py:100): row norms across the four parts.
-  float u[32];
-  tmem_ld32(taddr(tG, 32 * quarter, c0), u);
   {
+    float u[32];
+    tmem_ld32(taddr(tG, 32 * quarter, c0), u);
     float ss = 0.f;
 #pragma unroll
     for (int t = 0; t < 32; ++t) ss = fmaf(u[t], u[t], ss);
@@ -863,21 +931,36 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
         row >= 0 ? __fdividef(1.f, fmaxf(sqrtf(red[row] + red[128 + row] + red[256 + row] +
                                                red[384 + row]), 1e-12f))
                  : 0.f;
-    float bl[32];
     if (split) {
-      // lanes 16..31 hold the b logits of row (lane - 16): they form
-      // sigmoid(b - 4) * e^g and hand it to the u lane.
+      // Lane l < 16 holds u of pair 16q + l, lane l + 16 its b logits. The
+      // two swap halves (the low lane keeps columns 0..15, the high lane
+      // takes 16..31) and each writes 16 columns of keys and k * b * e^g.
+      const bool hi = lane >= 16;
+      const int pr = 16 * quarter + (lane & 15), cb = c0 + (hi ? 16 : 0);
+      const float iv = __shfl_sync(0xffffffffu, inv, lane & 15);
+      float x0[16], x1[16];
+      tmem_ld16(taddr(tG, 32 * quarter, c0), x0);
+      tmem_ld16(taddr(tG, 32 * quarter, c0 + 16), x1);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const float sb = lane >= 16 ? fast_sigmoid(u[t] + kBLogitInit) * egp[c0 + t] : 0.f;
-        bl[t] = __shfl_down_sync(0xffffffffu, sb, 16);
+      for (int c = 0; c < 16; c += 8) {
+        float kk[8], kb[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int j = c + t;
+          const float got = __shfl_xor_sync(0xffffffffu, hi ? x0[j] : x1[j], 16);
+          const float uu = hi ? got : x0[j], bb = hi ? x1[j] : got;
+          kk[t] = uu * iv;
+          kb[t] = kk[t] * (fast_sigmoid(bb + kBLogitInit) * egp[cb + j]);
+        }
+        *reinterpret_cast<uint4*>(keysT + mnmajor_off(pr, cb + c, mp)) = pack8(kk);
+        *reinterpret_cast<uint4*>(kbg + kmajor_off(pr, cb + c, TK)) = pack8(kb);
       }
     } else {
+      float u[32], bl[32];
+      tmem_ld32(taddr(tG, 32 * quarter, c0), u);
       tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), bl);
 #pragma unroll
       for (int t = 0; t < 32; ++t) bl[t] = fast_sigmoid(bl[t] + kBLogitInit) * egp[c0 + t];
-    }
-    if (row >= 0) {
 #pragma unroll
       for (int c = 0; c < 32; c += 8) {
         float kk[8], kb[8];
@@ -1047,7 +1130,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   // its record in global memory one chunk ahead of use.
   uint4 urow[4];
   float eg = 0.f;
-  auto fetch_u = [&](int nn) {
+  auto fetch_rows = [&](int nn) {
     const char* rg = rec0 + int64_t(nn) * lay.rec.size;
     if (quarter < 2) {
       const uint4* Ug = reinterpret_cast<const uint4*>(rg + lay.rec.U) +
@@ -1055,12 +1138,16 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) urow[c] = __ldg(Ug + c);
     }
+  };
+  auto fetch_eg = [&](int nn) {
+    const char* rg = rec0 + int64_t(nn) * lay.rec.size;
     eg = __ldg(reinterpret_cast<const float*>(rg + lay.rec.eg) + 32 * quarter + lane);
   };
   // S0 decayed by the first chunk's e^(G_last) (naive.py:392, first term);
   // each later chunk's decay is applied where the previous epilogue reads S0.
   if (p.NT > 0) {
-    fetch_u(0);
+    fetch_rows(0);
+    fetch_eg(0);
     const uint32_t ta = taddr(tS0, 32 * quarter, c0);
     float x[32];
     tmem_ld32(ta, x);
@@ -1099,9 +1186,6 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
-    // W and Q_0 are spent: the next record's first part streams in (unless
-    // a promotion needs the buffer as scratch first).
-    if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, true);
 
     // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376).
     if (quarter < 2) {
@@ -1117,11 +1201,20 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
         *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, c0 + 8 * c, kC)) = pack8(uu);
       }
     }
-    if (n + 1 < p.NT) fetch_u(n + 1);
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
     if (abort_flag) break;
+    // W and Q_0 are spent: the next record's first part streams in (unless
+    // a promotion needs the buffer as scratch first). It is issued only after
+    // this barrier, which every thread reaches after its wait on bar_ld: a
+    // phase completing early could otherwise alias the parity a slow thread
+    // still waits for. The next chunk's U rows and e^(G_last) load during
+    // MMA2 (U rows wait for the end of a promotion: they would hold
+    // registers across it).
+    if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, true);
+    if (n + 1 < p.NT) fetch_eg(n + 1);
+    if (n + 1 < p.NT && !fires) fetch_rows(n + 1);
 
     // MMA2: S0 += K_tail^T v_new (naive.py:392); then the rest of the output
     // into lanes 64..127: the upper-level reads (naive.py:382-385) and
@@ -1143,8 +1236,14 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
-    // The rest of the next record streams in during the epilogue.
+    // The rest of the next record streams in during the epilogue; at a
+    // firing the first learned promotion's operands do instead.
+    // (Only when the bank stays clear of the v_new tile that the output
+    // rows are staged in.)
+    const int first = fires ? __ffs(fire_mask) - 1 : 0;
+    const bool early = fires && learned && 65536 + pad_pairs(p.nq[first - 1]) * 256 <= load_bytes;
     if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, false);
+    if (tid == 0 && early) promote_tc_first_loads(p, lay, ws, h, first, Rec, &bar_ld);
     const bool write_master = (fires && !learned) || n + 1 == p.NT;
     const bool stage16 = p.dtype == NGDN2_BF16 || p.dtype == NGDN2_F16;
 
@@ -1218,7 +1317,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
           __syncthreads();
         } else {
           promote_tc(p, lay, ws, h, l, tb, Sbf, Rec, Mt, &bar_ld, &bar_mma, ph_ld, ph_mma, egp,
-                     red, &abort_flag);
+                     red, &abort_flag, early && l == first);
         }
       }
       fence_before_sync();
@@ -1229,6 +1328,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
         load_part(recg + lay.rec.size, true);
         load_part(recg + lay.rec.size, false);
       }
+      if (n + 1 < p.NT) fetch_rows(n + 1);
     }
   }
   if (abort_flag && tid == 0) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
