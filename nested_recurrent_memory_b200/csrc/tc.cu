@@ -286,7 +286,7 @@ constexpr int P_AF = 0;                  // fp32 [64][65] strictly lower A_kk
 constexpr int XS = 68;                   // row stride (floats) of the inverse: float4 rows
 constexpr int P_XF = P_AF + 16640;       // fp32 [64][XS] (I + A_kk)^-1
 constexpr int P_XB = P_XF + 64 * XS * 4; // bf16 [64 x 64] K-major: staged A_qk, then the inverse
-constexpr int P_TT = P_XB + 8192;        // fp32 [3][16][16] block products of the inverse
+constexpr int P_TT = P_XB + 8192;        // fp32 block products of the inverse (<= [32][36])
 constexpr int P_R = 73728;               // bf16 [64 x 256] MN-major [w*v | k*b*e^G]
 constexpr int kPrepSmem = P_R + 32768;   // 106496
 
@@ -590,8 +590,11 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     for (int e = tid; e < TILE_A / 16; e += kPrepThreads) dst[e] = src[e];
   }
 
-  // D. (I + A_kk)^-1 in fp32: 16x16 diagonal blocks by forward substitution,
-  //    then X_IJ = -X_II sum_{K=J}^{I-1} A_IK X_KJ block row by block row.
+  // D. (I + A_kk)^-1 in fp32 by 2x2 block recursion (for unit lower
+  //    triangular [[L11, 0], [L21, L22]], X21 = -X22 L21 X11): 16x16
+  //    diagonal blocks by forward substitution, then the 16-row off-diagonal
+  //    blocks of both 32x32 halves, then the 32-row block of the whole. Only
+  //    the lower triangle of Xf is ever read; blocks above it hold garbage.
   float* Xf = reinterpret_cast<float*>(sm + P_XF);
   if (tid < 64) {
     const int o = 16 * (tid >> 4), c = tid & 15;
@@ -607,40 +610,48 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     for (int rr = 0; rr < 16; ++rr) Xf[(o + rr) * XS + o + c] = x[rr];
   }
   __syncthreads();
-  // Off-diagonal block rows; each thread owns 4 consecutive columns of one
-  // row of one block (float4 operands of X and T).
-  for (int I2 = 1; I2 < 4; ++I2) {
-    const bool active = tid < I2 * 64;
-    const int J = tid >> 6, rr = (tid >> 2) & 15, c0 = (tid & 3) * 4;
-    if (active) {
+  auto fma4 = [](float a, const float4& x, float4& acc) {
+    acc.x = fmaf(a, x.x, acc.x);
+    acc.y = fmaf(a, x.y, acc.y);
+    acc.z = fmaf(a, x.z, acc.z);
+    acc.w = fmaf(a, x.w, acc.w);
+  };
+  // 32-level: in half h (rows/cols 32h..), T = L21 X11 then X21 = -X22 T,
+  // 16x16 each; a thread owns 4 columns of one row (128 threads).
+  {
+    const int hh = tid >> 6, rr = (tid >> 2) & 15, cq = (tid & 3) * 4;
+    const int r0 = 32 * hh + 16, k0 = 32 * hh;
+    if (tid < 128) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int K2 = J; K2 < I2; ++K2) {
 #pragma unroll
-        for (int m = 0; m < 16; ++m) {
-          const float a = Af[(16 * I2 + rr) * 65 + 16 * K2 + m];
-          const float4 x = *reinterpret_cast<const float4*>(&Xf[(16 * K2 + m) * XS + 16 * J + c0]);
-          acc.x = fmaf(a, x.x, acc.x);
-          acc.y = fmaf(a, x.y, acc.y);
-          acc.z = fmaf(a, x.z, acc.z);
-          acc.w = fmaf(a, x.w, acc.w);
-        }
-      }
-      *reinterpret_cast<float4*>(&Tt[(J << 8) + rr * 16 + c0]) = acc;
+      for (int m = 0; m < 16; ++m)
+        fma4(Af[(r0 + rr) * 65 + k0 + m], *reinterpret_cast<const float4*>(&Xf[(k0 + m) * XS + k0 + cq]), acc);
+      *reinterpret_cast<float4*>(&Tt[hh * 256 + rr * 16 + cq]) = acc;
     }
     __syncthreads();
-    if (active) {
+    if (tid < 128) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int m = 0; m <= rr; ++m) {
-        const float a = Xf[(16 * I2 + rr) * XS + 16 * I2 + m];
-        const float4 tv = *reinterpret_cast<const float4*>(&Tt[(J << 8) + m * 16 + c0]);
-        acc.x = fmaf(a, tv.x, acc.x);
-        acc.y = fmaf(a, tv.y, acc.y);
-        acc.z = fmaf(a, tv.z, acc.z);
-        acc.w = fmaf(a, tv.w, acc.w);
-      }
-      *reinterpret_cast<float4*>(&Xf[(16 * I2 + rr) * XS + 16 * J + c0]) =
-          make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
+      for (int m = 0; m <= rr; ++m)
+        fma4(Xf[(r0 + rr) * XS + r0 + m], *reinterpret_cast<const float4*>(&Tt[hh * 256 + m * 16 + cq]), acc);
+      *reinterpret_cast<float4*>(&Xf[(r0 + rr) * XS + k0 + cq]) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     }
+    __syncthreads();
+  }
+  // 64-level: T = A[32.., 0..31] X_A (X_A lower triangular, so k >= column),
+  // then X[32.., 0..31] = -X_B T (X_B lower triangular); 32x32 each, a
+  // thread owns 4 columns of one row (256 threads).
+  {
+    const int rr = tid >> 3, cq = (tid & 7) * 4;
+    constexpr int TS = 36;  // row stride (floats) of T
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = cq; k < 32; ++k)
+      fma4(Af[(32 + rr) * 65 + k], *reinterpret_cast<const float4*>(&Xf[k * XS + cq]), acc);
+    *reinterpret_cast<float4*>(&Tt[rr * TS + cq]) = acc;
+    __syncthreads();
+    acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int m = 0; m <= rr; ++m)
+      fma4(Xf[(32 + rr) * XS + 32 + m], *reinterpret_cast<const float4*>(&Tt[m * TS + cq]), acc);
+    *reinterpret_cast<float4*>(&Xf[(32 + rr) * XS + cq]) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     __syncthreads();
   }
   for (int it = tid; it < kC * 8; it += kPrepThreads) {
