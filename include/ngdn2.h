@@ -16,6 +16,9 @@
  *                        (and the forward of chunk_nested_gdn2, chunk.py:722-766,
  *                        whose Function.forward calls it, chunk.py:571-648)
  *   ngdn2_update_state   nested_gdn2/ops/update_fwd.py:131-204  update_state
+ *   ngdn2_step           nested_gdn2/ops/naive.py:42-134  naive_step_nested_gdn2
+ *                        (the one-token decode step the layer runs past the
+ *                        chunked prefix, nested_gdn2.py:218-224)
  *
  * Layouts are the reference's (chunk.py:184-217): per-token tensors
  * [B, T, H, ...], states [B, H, L, K, V] float32, parameters
@@ -145,10 +148,50 @@ typedef struct ngdn2_update_args {
   float* final_state;                           /* [B, H, K, V] out */
 } ngdn2_update_args;
 
+/* Arguments of ngdn2_step: one token of every batch row (naive.py:42-134).
+ * Per-token inputs carry no T dimension. */
+typedef struct ngdn2_step_args {
+  int32_t abi_version;
+  int32_t B, H, K, V, L;
+  int32_t chunk_size;   /* tokens per chunk for the firing schedule (default 64) */
+  int32_t promotion;    /* NGDN2_PROMOTION_* */
+  int32_t dtype;        /* element type of o (the reference returns q's dtype) */
+  int32_t param_dtype;
+  float scale;
+  int32_t n_max;
+  int32_t n_queries[NGDN2_MAX_LEVELS];
+  int32_t firing[NGDN2_MAX_LEVELS];
+
+  const void* q;   int32_t q_dtype;   int64_t q_stride[4];   /* [B, H, L, K] */
+  const void* k;   int32_t k_dtype;   int64_t k_stride[3];   /* [B, H, K] */
+  const void* v;   int32_t v_dtype;   int64_t v_stride[3];   /* [B, H, V] */
+  const void* g;   int32_t g_dtype;   int64_t g_stride[3];   /* [B, H, K] */
+  const void* b;   int32_t b_dtype;   int64_t b_stride[3];   /* [B, H, K] */
+  const void* w;   int32_t w_dtype;   int64_t w_stride[3];   /* [B, H, V] */
+  const void* mix; int32_t mix_dtype; int64_t mix_stride[3]; /* [B, H, L] */
+
+  const void* query_banks;
+  const void* key_projections;
+  const void* b_projections;
+  const void* w_projections;
+  const void* g_projections;
+
+  const int64_t* positions;     /* [B] device positions of this token, or NULL */
+  int64_t position;             /* the position of every row when positions is NULL */
+  const float* state_in;        /* [B, H, L, K, V] contiguous */
+  float* state_out;             /* [B, H, L, K, V] contiguous; may equal state_in */
+  void* o;                      /* [B, H, V] contiguous, element type dtype */
+
+  void* workspace;              /* >= ngdn2_step_workspace_size */
+  size_t workspace_bytes;
+  int32_t* status;
+} ngdn2_step_args;
+
 NGDN2_API int ngdn2_abi_version(void);
-/* sizeof the two argument structs, so bindings can check their layout. */
+/* sizeof the argument structs, so bindings can check their layout. */
 NGDN2_API size_t ngdn2_sizeof_fwd_args(void);
 NGDN2_API size_t ngdn2_sizeof_update_args(void);
+NGDN2_API size_t ngdn2_sizeof_step_args(void);
 NGDN2_API const char* ngdn2_error_string(int code);
 
 /* Validates *args and returns the workspace ngdn2_fwd needs, in bytes. */
@@ -171,6 +214,16 @@ NGDN2_API int ngdn2_fwd_num_launches(const ngdn2_fwd_args* args);
 
 /* The promotion write scan on its own. */
 NGDN2_API int ngdn2_update_state(const ngdn2_update_args* args, void* stream);
+
+/* Validates *args and returns the workspace ngdn2_step needs, in bytes
+ * (fp32 parameter copies and promotion scratch). */
+NGDN2_API int ngdn2_step_workspace_size(const ngdn2_step_args* args, size_t* bytes);
+
+/* One decode token (naive.py:42-134): level 0 writes, every level is read
+ * and mixed into o, then each level whose firing this token completes
+ * promotes, bottom-up, per batch row (rows may sit at different positions).
+ * Reads state_in, writes state_out (in place when they are equal). */
+NGDN2_API int ngdn2_step(const ngdn2_step_args* args, void* stream);
 
 /* Capacity of the fixed scratch buffer behind ngdn2_fwd_noalloc. */
 #define NGDN2_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)

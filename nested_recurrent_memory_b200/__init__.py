@@ -1,7 +1,8 @@
 """B200-native nested Gated DeltaNet (nested GDN-2) forward hot path.
 
 A drop-in for the reference's ``nested_gdn2.ops`` forward ops
-(``chunk_nested_gdn2``, ``chunk_nested_gdn2_fwd``, ``update_state``),
+(``chunk_nested_gdn2``, ``chunk_nested_gdn2_fwd``, ``update_state``, and the
+one-token decode step ``naive_step_nested_gdn2`` as ``step_nested_gdn2``),
 computed by hand-written sm_100a CUDA kernels behind the C ABI in
 ``include/ngdn2.h``.
 """
@@ -14,6 +15,7 @@ from .ops import (  # noqa: F401
     last_path,
     n_firings,
     n_groups,
+    step_nested_gdn2,
     update_state,
 )
 

@@ -1,7 +1,7 @@
 """ctypes binding of ``libngdn2.so`` (the C ABI declared in include/ngdn2.h).
 
-The structs below mirror ``ngdn2_fwd_args`` and ``ngdn2_update_args`` field
-for field; ``check_layout()`` compares their sizes with the library's own
+The structs below mirror ``ngdn2_fwd_args``, ``ngdn2_update_args`` and
+``ngdn2_step_args`` field for field; ``check_layout()`` compares their sizes with the library's own
 ``sizeof``. Loading fails loudly: there is no fallback implementation.
 """
 
@@ -64,11 +64,28 @@ class UpdateArgs(ctypes.Structure):
     ]
 
 
+class StepArgs(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", c_i32),
+        ("B", c_i32), ("H", c_i32), ("K", c_i32), ("V", c_i32), ("L", c_i32),
+        ("chunk_size", c_i32), ("promotion", c_i32), ("dtype", c_i32), ("param_dtype", c_i32),
+        ("scale", ctypes.c_float), ("n_max", c_i32),
+        ("n_queries", c_i32 * MAX_LEVELS), ("firing", c_i32 * MAX_LEVELS),
+        *_tok("q", 4), *_tok("k", 3), *_tok("v", 3), *_tok("g", 3), *_tok("b", 3),
+        *_tok("w", 3), *_tok("mix", 3),
+        ("query_banks", c_ptr), ("key_projections", c_ptr), ("b_projections", c_ptr),
+        ("w_projections", c_ptr), ("g_projections", c_ptr),
+        ("positions", c_ptr), ("position", c_i64),
+        ("state_in", c_ptr), ("state_out", c_ptr), ("o", c_ptr),
+        ("workspace", c_ptr), ("workspace_bytes", ctypes.c_size_t), ("status", c_ptr),
+    ]
+
+
 EXPORTS = (
     "ngdn2_abi_version", "ngdn2_sizeof_fwd_args", "ngdn2_sizeof_update_args",
     "ngdn2_error_string", "ngdn2_fwd_workspace_size", "ngdn2_fwd_select_path",
     "ngdn2_fwd", "ngdn2_fwd_stage", "ngdn2_fwd_num_launches", "ngdn2_update_state",
-    "ngdn2_fwd_noalloc",
+    "ngdn2_fwd_noalloc", "ngdn2_sizeof_step_args", "ngdn2_step_workspace_size", "ngdn2_step",
 )
 
 _LIB = None
@@ -104,6 +121,11 @@ def load(path: str | os.PathLike | None = None):
     lib.ngdn2_update_state.restype = ctypes.c_int
     lib.ngdn2_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), c_ptr]
     lib.ngdn2_fwd_noalloc.restype = ctypes.c_int
+    lib.ngdn2_sizeof_step_args.restype = ctypes.c_size_t
+    lib.ngdn2_step_workspace_size.argtypes = [ctypes.POINTER(StepArgs), ctypes.POINTER(ctypes.c_size_t)]
+    lib.ngdn2_step_workspace_size.restype = ctypes.c_int
+    lib.ngdn2_step.argtypes = [ctypes.POINTER(StepArgs), c_ptr]
+    lib.ngdn2_step.restype = ctypes.c_int
     if path is None:
         _LIB = lib
     return lib
@@ -117,6 +139,8 @@ def check_layout(lib=None) -> None:
         raise RuntimeError("ngdn2_fwd_args layout mismatch")
     if lib.ngdn2_sizeof_update_args() != ctypes.sizeof(UpdateArgs):
         raise RuntimeError("ngdn2_update_args layout mismatch")
+    if lib.ngdn2_sizeof_step_args() != ctypes.sizeof(StepArgs):
+        raise RuntimeError("ngdn2_step_args layout mismatch")
 
 
 def error_string(code: int) -> str:

@@ -6,6 +6,8 @@ messages as the reference (awehrs/nested_recurrent_memory):
 * ``chunk_nested_gdn2``      -- nested_gdn2/ops/chunk.py:722-766
 * ``chunk_nested_gdn2_fwd``  -- nested_gdn2/ops/chunk.py:159-304
 * ``update_state``           -- nested_gdn2/ops/update_fwd.py:131-204
+* ``step_nested_gdn2``       -- nested_gdn2/ops/naive.py:42-134 (naive_step_nested_gdn2,
+  the one-token decode step; same signature)
 * ``n_groups``, ``n_firings`` -- nested_gdn2/ops/chunk.py:26-36
 
 The work is done by hand-written sm_100a CUDA kernels behind the C ABI of
@@ -27,6 +29,7 @@ __all__ = [
     "chunk_nested_gdn2",
     "chunk_nested_gdn2_fwd",
     "update_state",
+    "step_nested_gdn2",
     "n_groups",
     "n_firings",
     "fwd_workspace_bytes",
@@ -326,3 +329,85 @@ def update_state(keys, values, g, b, w, n_groups, initial_state=None, block_v=16
     rc = _lib.load().ngdn2_update_state(ctypes.byref(a), ctypes.c_void_p(stream))
     _raise_for(rc, "ngdn2_update_state", N=N, block_v=block_v, V=V, NF=NF, NG=n_groups)
     return states, final
+
+
+def step_nested_gdn2(q, k, v, g, b, w, mix_weights, state, position, query_banks,
+                     key_projections, b_projections, w_projections, g_projections,
+                     n_queries_per_level, firing_intervals, L, scale=None, chunk_size=64,
+                     promotion="learned", *, out_state=None, workspace=None):
+    """One decode token for every batch row (naive.py:42-134,
+    ``naive_step_nested_gdn2``): level 0 writes, every level is read and
+    mixed, then each level whose firing this token completes promotes,
+    bottom-up. Level 0 writes before the read, levels above after, so a
+    firing is first visible at the next token.
+
+    Args as the reference: q [B, H, L, K]; k, g, b [B, H, K]; v, w [B, H, V];
+    mix_weights [B, H, L]; state [B, H, L, K, V] float32; position an int or a
+    [B] integer tensor (rows at different positions fire on different
+    tokens); the rest as for ``chunk_nested_gdn2``. ``out_state`` may be
+    ``state`` itself to update in place.
+
+    Returns ``(o, state)``: o [B, H, V] in q's dtype, the new state float32.
+    """
+    if promotion not in _lib.PROMOTION:
+        raise KeyError(promotion)  # PROBES[promotion] in the reference
+    B, H, _, K = q.shape
+    V = v.shape[-1]
+    if scale is None:
+        scale = K ** -0.5
+    firing = [int(x) for x in firing_intervals]
+    nq = [int(x) for x in n_queries_per_level]
+    for lvl in range(1, L):
+        n = K if promotion == "merge" else nq[lvl - 1]
+        if n < 16 or n & (n - 1):
+            raise ValueError(f"pairs per firing must be a power of two >= 16, got {n}")
+    _require_cuda(q, k, v, g, b, w, mix_weights, state)
+    params, n_max = [], 1
+    if L > 1:
+        pdt = query_banks.dtype
+        params = [t.to(q.device, pdt).contiguous() for t in
+                  (query_banks, key_projections, b_projections, w_projections, g_projections)]
+        _require_cuda(*params)
+        n_max = query_banks.shape[2]
+    state_in = state.to(torch.float32).contiguous()
+    new = torch.empty_like(state_in) if out_state is None else out_state
+    o = torch.empty(B, H, V, dtype=q.dtype, device=q.device)
+    a = _lib.StepArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.B, a.H, a.K, a.V, a.L = B, H, K, V, L
+    a.chunk_size = int(chunk_size)
+    a.promotion = _lib.PROMOTION[promotion]
+    a.dtype = _code(o)
+    a.param_dtype = _code(params[0]) if params else _lib.F32
+    a.scale = float(scale)
+    a.n_max = n_max
+    for i, n in enumerate(nq):
+        a.n_queries[i] = n
+    for i, f in enumerate(firing):
+        a.firing[i] = f
+    _fill_tok(a, "q", q, 4)
+    for name, t in (("k", k), ("v", v), ("g", g), ("b", b), ("w", w), ("mix", mix_weights)):
+        _fill_tok(a, name, t, 3)
+    if params:
+        (a.query_banks, a.key_projections, a.b_projections, a.w_projections,
+         a.g_projections) = (p.data_ptr() for p in params)
+    pos = None
+    if torch.is_tensor(position):
+        pos = position.to(q.device, torch.int64).contiguous()
+        a.positions = pos.data_ptr()
+    else:
+        a.position = int(position)
+    a.state_in = state_in.data_ptr()
+    a.state_out = new.data_ptr()
+    a.o = o.data_ptr()
+    lib = _lib.load()
+    need = ctypes.c_size_t(0)
+    _raise_for(lib.ngdn2_step_workspace_size(ctypes.byref(a), ctypes.byref(need)), "ngdn2_step")
+    if need.value and (workspace is None or workspace.numel() < need.value):
+        workspace = torch.empty(need.value, dtype=torch.uint8, device=q.device)
+    if need.value:
+        a.workspace = workspace.data_ptr()
+        a.workspace_bytes = workspace.numel()
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    _raise_for(lib.ngdn2_step(ctypes.byref(a), ctypes.c_void_p(stream)), "ngdn2_step")
+    return o, new

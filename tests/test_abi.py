@@ -127,3 +127,47 @@ def test_update_validation_codes_follow_the_reference_order(lib, over, code):
 def test_error_strings(lib):
     assert _lib.error_string(_lib.ERR_CHUNK_SIZE) == "chunk_size must be 64"
     assert "unit-stride" in _lib.error_string(_lib.ERR_UNIT_STRIDE)
+
+
+def _fake_step(**over):
+    a = _lib.StepArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.B, a.H, a.K, a.V, a.L = 2, 2, 64, 64, 3
+    a.chunk_size = 64
+    a.scale = 0.125
+    a.n_max = 16
+    for i in range(2):
+        a.n_queries[i] = 16
+    for i, f in enumerate((1, 2, 4)):
+        a.firing[i] = f
+    for name in ("q", "k", "v", "g", "b", "w", "mix", "query_banks", "key_projections",
+                 "b_projections", "w_projections", "g_projections", "state_in", "state_out", "o"):
+        setattr(a, name, 0x1000)
+    for k, v in over.items():
+        if k == "n_queries":
+            for i, x in enumerate(v):
+                a.n_queries[i] = x
+        else:
+            setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize(("over", "code"), [
+    (dict(n_queries=(24, 16)), _lib.ERR_N_POW2),
+    (dict(state_out=None), -9),
+    (dict(chunk_size=0), -7),
+    (dict(abi_version=5), -13),
+])
+def test_step_validation_codes(lib, over, code):
+    n = ctypes.c_size_t(0)
+    assert lib.ngdn2_step_workspace_size(ctypes.byref(_fake_step(**over)), ctypes.byref(n)) == code
+    assert lib.ngdn2_step(ctypes.byref(_fake_step(**over)), None) == code
+
+
+def test_step_needs_its_workspace_for_promotions(lib):
+    n = ctypes.c_size_t(0)
+    assert lib.ngdn2_step_workspace_size(ctypes.byref(_fake_step()), ctypes.byref(n)) == 0
+    assert n.value > 0
+    assert lib.ngdn2_step(ctypes.byref(_fake_step()), None) == -10
+    one = _fake_step(L=1)
+    assert lib.ngdn2_step_workspace_size(ctypes.byref(one), ctypes.byref(n)) == 0 and n.value == 0
