@@ -53,6 +53,9 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling runs on a smaller case)")
+    ap.add_argument("--decode", action="store_true",
+                    help="time the one-token decode step (step_nested_gdn2) on the config's "
+                         "B, H, K, V, L instead of the chunked forward; prints its own line")
     return ap.parse_args()
 
 
@@ -396,12 +399,78 @@ def run_ours(args, w):
         dist.destroy_process_group()
 
 
+def run_decode(args, w):
+    """One step = one token for every batch row through ``step_nested_gdn2``,
+    in place on a resident state, positions advancing from 0 (so the upper
+    levels fire on schedule), replayed from a CUDA graph. Single GPU;
+    tokens/s = B / step time."""
+    import torch
+
+    from nested_recurrent_memory_b200 import step_nested_gdn2
+    from nested_recurrent_memory_b200.synthetic import config_inputs
+
+    dev = torch.device("cuda", 0)
+    B, H, K, V, L = w["B"], w["H"], w["K"], w["V"], w["L"]
+    steps = max(args.steps, 256)
+    inp = config_inputs(B, steps, H, K, V, L, w["m"], w["firing"], dtype=w["dtype"],
+                        device=dev, gen_device=dev)
+    inp.pop("L")
+    per_token = ("q", "k", "v", "g", "b", "w", "mix_weights")
+    wts = {n: inp[n] for n in inp if n not in per_token}
+    state = torch.zeros(B, H, L, K, V, dtype=torch.float32, device=dev)
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+
+    def step(t):
+        step_nested_gdn2(**{n: inp[n][:, t] for n in per_token}, state=state, position=t,
+                         **wts, L=L, out_state=state, workspace=ws)
+
+    for t in range(args.warmup):
+        step(t)
+    torch.cuda.synchronize()
+    # The steps are captured once into a CUDA graph and replayed, so the
+    # timing is the GPU's, not the Python launch loop's.
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for t in range(steps):
+                step(t)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    state.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    state.zero_()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del graph
+    peaks, _ = load_peaks()
+    nbytes = B * H * (L + 1) * K * V * 4  # state read (all levels) + level-0 write, in place
+    print(json.dumps({
+        "metric": "nested-GDN decode step tokens/s (one token per row, in-place state)",
+        "value": B / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": str(w["dtype"]).replace("torch.", ""), "data": "synthetic",
+        "config": {"workload": f"{args.config} decode: B={B}, H={H}, K=V={K}, L={L}, "
+                               f"firing {'/'.join(map(str, w['firing']))} chunks, positions 0..{steps - 1}"},
+        "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                     "alg_bytes_per_step": nbytes},
+    }), flush=True)
+
+
 def main():
     args = parse_args()
     w = workload(args.config)
     if args.batch is not None:
         w["B"] = args.batch
-    if args.impl == "reference":
+    if args.decode:
+        run_decode(args, w)
+    elif args.impl == "reference":
         run_reference(args, w)
     else:
         run_ours(args, w)
