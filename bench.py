@@ -53,6 +53,9 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling runs on a smaller case)")
+    ap.add_argument("--model", action="store_true",
+                    help="time the full-model forward harness (BASELINE config 4: 12-layer "
+                         "NestedGDN-2 LM, B=32 sharded over the GPUs, T=4096); prints its own line")
     ap.add_argument("--decode", action="store_true",
                     help="time the one-token decode step (step_nested_gdn2) on the config's "
                          "B, H, K, V, L instead of the chunked forward; prints its own line")
@@ -463,8 +466,74 @@ def run_decode(args, w):
     }), flush=True)
 
 
+def run_model(args):
+    """random-init 12-layer NestedGDN-2 LM forward in bf16,
+    batch-sharded (32 sequences over the ranks), T=4096, token ids uniform
+    over the vocabulary. One step = one forward of the rank's batch plus an
+    NCCL all-reduce of the mean logit (the config's data-parallel collective).
+    Dense layers run as torch GEMMs, the token mixer as this package's op."""
+    import torch
+    import torch.distributed as dist
+
+    from nested_recurrent_memory_b200.model import ModelConfig, NestedGDN2ForCausalLM
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    B_total, T = 32, 4096
+    B = args.batch or max(1, B_total // world)
+    torch.manual_seed(0)
+    cfg = ModelConfig()
+    model = NestedGDN2ForCausalLM(cfg).to(dev, torch.bfloat16)
+    ids = torch.randint(0, cfg.vocab_size, (B, T), device=dev,
+                        generator=torch.Generator(device=dev).manual_seed(100 + rank))
+    red = torch.zeros(1, device=dev)
+
+    def step():
+        with torch.no_grad():
+            logits = model(ids)
+        red.copy_(logits[:, -1].float().mean().reshape(1))
+        if world > 1:
+            dist.all_reduce(red)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+    if rank == 0:
+        print(json.dumps({
+            "metric": "nested-GDN LM forward tokens/s (BASELINE config 4)",
+            "value": B * T * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic token ids, random-init weights N(0, 0.02)",
+            "config": {"workload": f"config4: 12 layers, d 1024, 8x128 heads, L 3 (1/4/16), m 64, "
+                                   f"SwiGLU 2816, vocab 32000; B={B} per GPU, T={T}",
+                       "parallelism": f"data parallel over {world} GPU(s), NCCL all-reduce per step"},
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
+    if args.model:
+        run_model(args)
+        return
     w = workload(args.config)
     if args.batch is not None:
         w["B"] = args.batch
