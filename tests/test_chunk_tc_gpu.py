@@ -174,3 +174,15 @@ def test_full_occupancy_no_wait_timeouts():
     ro, rs = _oracle(sub, 3)
     assert rel_err(_np(o[:1, :, :2]), ro) < LOWP_REL
     assert rel_err(_np(s[:1, :2]), rs) < LOWP_REL
+
+
+@pytest.mark.parametrize("promotion", ["learned", "merge"])
+def test_128_pairs_per_firing(promotion):
+    """n_queries = 128 (the M = 128 promotion tiles, no half-lane split)."""
+    inp = config_inputs(1, 512, 2, 128, 128, 3, 128, (1, 2, 4), dtype=torch.bfloat16, seed=15,
+                        gate_proj_std=128 ** -0.5)
+    inp.pop("L")
+    o, s = _run(inp, 3, promotion=promotion)
+    ro, rs = _oracle(inp, 3, promotion)
+    assert rel_err(_np(o), ro) < LOWP_REL
+    assert rel_err(_np(s), rs) < LOWP_REL
