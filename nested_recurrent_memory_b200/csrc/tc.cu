@@ -26,6 +26,10 @@
 // fla's GDN-2, chunk.py:236-248), reads and mix naive.py:382-390, promotion
 // naive.py:394-415 with probe.py:34-136.
 
+#include <cuda.h>
+#include <string.h>
+#include <cudaTypedefs.h>
+
 #include "promote_simt.cuh"
 #include "tc_api.cuh"
 #include "tc_ptx.cuh"
@@ -44,16 +48,19 @@ constexpr int TV = 128;         // value dim
 constexpr int TILE_QK = kC * TK * 2;   // bytes of a [64 x 128] bf16 tile
 constexpr int TILE_A = kC * kC * 2;    // bytes of a [64 x 64] bf16 tile
 
-// Byte offsets inside one chunk record of the tensor-core family.
+// Byte offsets inside one chunk record of the tensor-core family. The
+// upper levels' read queries are not in it: the scan loads them from q
+// itself with the tensor memory accelerator and applies mix * scale.
 struct TcRecord {
-  int64_t W, Q, A, Kt, U, eg, load_bytes, size;
+  int64_t W, Q, Kt, A, U, eg, load_bytes, size;
   __host__ __device__ static TcRecord make(int L) {
+    (void)L;
     TcRecord r;
     r.W = 0;                                  // [64 x K] K-major A operand
-    r.Q = r.W + TILE_QK;                      // L x [64 x K] K-major A operands
-    r.A = r.Q + int64_t(L) * TILE_QK;         // [64 x 64] K-major A operand
-    r.Kt = r.A + TILE_A;                      // [64 tok x K] MN-major A operand (K_tail^T)
-    r.load_bytes = r.Kt + TILE_QK;            // the part the scan copies to smem
+    r.Q = r.W + TILE_QK;                      // [64 x K] level-0 read queries, K-major
+    r.Kt = r.Q + TILE_QK;                     // [64 tok x K] MN-major A operand (K_tail^T)
+    r.A = r.Kt + TILE_QK;                     // [64 x 64] K-major A operand
+    r.load_bytes = r.A + TILE_A;              // the part the scan copies to smem
     r.U = r.load_bytes;                       // [64 x V] row-major bf16
     r.eg = r.U + kC * TV * 2;                 // [K] fp32 e^(G_last)
     r.size = (r.eg + TK * 4 + 127) & ~int64_t(127);
@@ -308,7 +315,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tbase;
-  __shared__ float mixs[3][kC];             // mix_l * scale per row
+  __shared__ float mixs[1][kC];             // mix_0 * scale per row
   __shared__ __align__(16) float rho[5][TK];  // G[16J + 7] for J = 0..3, then G[63]
   // [0]: e^(G_63 - rho_3); [J]: e^(rho_J - rho_(J-1)), J = 1..3; [4 + I]: e^(rho_I)
   __shared__ __align__(16) float rat[8][TK];
@@ -323,10 +330,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
-  if (tid < kC * p.L) {
-    const int l = tid / kC, i = tid % kC;
-    mixs[l][i] = (t0 + i < p.T) ? p.mix.at(b, t0 + i, h, l) * p.scale : 0.f;
-  }
+  if (tid < kC) mixs[0][tid] = (t0 + tid < p.T) ? p.mix.at(b, t0 + tid, h, 0) * p.scale : 0.f;
 
   // Phase A mapping: warp w owns rows 8w .. 8w+7; lane = 8 * c4 + r8 holds
   // row 8w + r8 and the 8-column chunks c4, c4 + 4, c4 + 8, c4 + 12. A warp
@@ -337,17 +341,6 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   const bool valid = t < p.T;
   bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
   bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
-
-  // The upper-level queries q_1, q_2 need no decay: their loads go out
-  // first, next to those of g, and they are written while G is formed.
-  uint4 qup[2][4];
-#pragma unroll
-  for (int l = 1; l < 3; ++l)
-#pragma unroll
-    for (int ci = 0; ci < 4; ++ci)
-      qup[l - 1][ci] = (valid && l < p.L)
-                           ? raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, l, 8 * (c4 + 4 * ci)), p.q.sd)
-                           : make_uint4(0, 0, 0, 0);
 
   // Raw 16-byte chunks of q_0, k, b, v, w for one column chunk; each
   // chunk's loads are issued one chunk ahead of their use.
@@ -396,21 +389,7 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       for (int u = 0; u < 8; ++u) carry[warp * TK + 8 * (c4 + 4 * ci) + u] = G[ci][u];
   }
   __syncthreads();
-  // Upper-level read queries mix_l * scale * q_l to the record (mixs is
-  // visible after the barrier above); then the first column chunk's loads.
-#pragma unroll
-  for (int l = 1; l < 3; ++l) {
-    if (l >= p.L) continue;
-    const float ml = mixs[l][r];
-#pragma unroll
-    for (int ci = 0; ci < 4; ++ci) {
-      float qq[8];
-      unpack8(qup[l - 1][ci], p.q.dt, qq);
-      scale8(qq, ml);
-      *reinterpret_cast<uint4*>(Qg + l * (kC * 128) + kmajor_off(r, 8 * (c4 + 4 * ci), 128)) =
-          pack8(qq);
-    }
-  }
+  // The first column chunk's loads.
   fetch(0, cur);
   if (tid < TK) {
     float run = 0.f;
@@ -718,9 +697,12 @@ constexpr int TILE_S = TK * TV * 2;     // bf16 state copy
 // for weights / gate partials / keys, and a 32 KB slot for the pairs.
 constexpr int kPromoScratch = 98304;
 
+// Shared memory of the scan: L bf16 state copies, then the record, the
+// upper levels' query tiles (L - 1), the v_new tile and the CUDA-core
+// promotion's GEMM staging; promotions reuse everything after the states.
 __host__ __device__ inline int64_t scan_tc_smem(int L, const TcRecord& rec) {
-  const int64_t tail = rec.load_bytes + TILE_QK + kGemmSmemFloats * 4;
-  return int64_t(L) * TILE_S + (tail > kPromoScratch ? tail : kPromoScratch);
+  const int64_t tail = rec.load_bytes + int64_t(L - 1) * TILE_QK + TILE_QK + kGemmSmemFloats * 4;
+  return int64_t(L) * TILE_S + (tail > kPromoScratch ? tail : kPromoScratch) + 1024;
 }
 
 // fp32 master [K][V] -> bf16 MN-major B operand copy [Kd = K][N = V].
@@ -1049,10 +1031,17 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   fence_after_sync();
 }
 
+// qmap views q as 4-D [64 channels, (b, t) tokens, 2 channel halves,
+// (head, level) pairs] with 128-byte swizzle: one (64, 64, 2, 1) box is a
+// [64 tokens x 128] K-major MMA operand in the swizzled layout (sw128_off).
+// hl = h * L + l when hl_mode == 0, l * H + h when 1. With hl_mode == 2 (q
+// laid out otherwise) there is no map: the scaling warps read their rows
+// from q themselves.
 __global__ void __launch_bounds__(kScanThreads, 1)
-scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
-  extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ uint64_t bar_ld, bar_ld2, bar_mma;
+scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUtensorMap qmap,
+               int hl_mode) {
+  extern __shared__ __align__(1024) uint8_t sm_raw[];
+  __shared__ uint64_t bar_ld, bar_ld2, bar_mma, bar_q;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   __shared__ float egp[128];
@@ -1063,9 +1052,13 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   const int quarter = warp & 3, c0 = 32 * (warp >> 2);
   const int64_t bh = int64_t(b) * p.H + h;
   const uint32_t load_bytes = static_cast<uint32_t>(lay.rec.load_bytes);
+  // The swizzled query tiles need 1024-byte alignment (the launch adds the
+  // slack).
+  uint8_t* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
   bf16* Sbf = reinterpret_cast<bf16*>(sm);
   uint8_t* Rec = sm + int64_t(L) * TILE_S;
-  bf16* Vn = reinterpret_cast<bf16*>(Rec + lay.rec.load_bytes);
+  uint8_t* QT = Rec + lay.rec.load_bytes;  // upper-level query tiles (sw128_off)
+  bf16* Vn = reinterpret_cast<bf16*>(QT + int64_t(L - 1) * TILE_QK);
   float* gsm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Vn) + TILE_QK);
   float* Sg = p.fin + bh * L * TK * TV;
   float* sc = p.scan + bh * p.ss.size;
@@ -1080,6 +1073,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     mbar_init(&bar_ld, 1);
     mbar_init(&bar_ld2, 1);
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_q, 1);
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -1132,11 +1126,39 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     mbar_arrive_expect_tx(bar, hi - lo);
     bulk_g2s(Rec + lo, src + lo, hi - lo, bar);
   };
-  uint32_t ph_ld2 = 0;
+  uint32_t ph_ld2 = 0, ph_q = 0;
+  // The upper levels' raw query tiles of chunk nn (read by MMA2 after the
+  // warps idle in E1 scale their rows by mix_l * scale; naive.py:382-385).
+  const bool q_tma = hl_mode != 2;
+  // Query tiles that need a pass before MMA2 reads them (fp16 to bf16, or
+  // plain loads); bf16 tiles from the map are read as they land.
+  const bool q_conv = !q_tma || p.q.dt != NGDN2_BF16;
+  auto load_q = [&](int nn) {
+    if (L < 2 || !q_tma) return;
+    mbar_arrive_expect_tx(&bar_q, uint32_t(L - 1) * TILE_QK);
+    const int row = b * p.T + nn * kC;
+    for (int l = 1; l < L; ++l)
+      tma_load_4d(QT + (l - 1) * TILE_QK, &qmap, 0, row, 0, hl_mode ? l * p.H + h : h * L + l,
+                  &bar_q);
+  };
   if (tid == 0 && p.NT > 0) {
     load_part(rec0, true);
     load_part(rec0, false);
+    load_q(0);
   }
+  // mix_l * scale of the upper levels for the output row this thread
+  // assembles in E2 (threads of lane quarters 2 and 3), one chunk ahead.
+  const int jq = (warp >> 2) * 64 + (warp & 1) * 32 + lane;  // 0..255 among them
+  float mixr[2] = {0.f, 0.f};
+  bool qrow = false;
+  auto fetch_mix = [&](int nn) {
+    if (quarter < 2) return;
+    const int t = nn * kC + (jq & 63);
+    qrow = t < p.T;
+#pragma unroll
+    for (int l = 1; l < 3; ++l)
+      if (l < L) mixr[l - 1] = qrow ? p.mix.at(b, t, h, l) * p.scale : 0.f;
+  };
   // U rows (lanes of quarters 0 and 1) and e^(G_last) of a chunk, read from
   // its record in global memory one chunk ahead of use.
   uint4 urow[4];
@@ -1159,6 +1181,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   if (p.NT > 0) {
     fetch_rows(0);
     fetch_eg(0);
+    fetch_mix(0);
     const uint32_t ta = taddr(tS0, 32 * quarter, c0);
     float x[32];
     tmem_ld32(ta, x);
@@ -1198,7 +1221,9 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     ph_mma ^= 1;
     fence_after_sync();
 
-    // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376).
+    // E1: v_new = U - W.S0 -> bf16 B operand (naive.py:376). Meanwhile, for
+    // fp16 q or q without a tensor map, the other warps turn the upper
+    // levels' query tiles into bf16 (the state operand's type).
     if (quarter < 2) {
       const int i = 32 * quarter + lane;
       float x[32];
@@ -1210,6 +1235,26 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
 #pragma unroll
         for (int t = 0; t < 8; ++t) uu[t] -= x[8 * c + t];
         *reinterpret_cast<uint4*>(Vn + mnmajor_off(i, c0 + 8 * c, kC)) = pack8(uu);
+      }
+    } else if (L > 1 && q_conv) {
+      if (q_tma && !mbar_wait(&bar_q, ph_q)) abort_flag = 1;
+      const int r = jq & 63, g4 = jq >> 6;
+#pragma unroll
+      for (int l = 1; l < 3; ++l) {
+        if (l >= L) break;
+        bf16* tile = reinterpret_cast<bf16*>(QT + (l - 1) * TILE_QK);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4* q8 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(tile) +
+                                               sw128_off(r, 8 * (g4 + 4 * u)));
+          float f[8];
+          const uint4 raw = q_tma ? *q8
+                            : qrow ? raw8_at(p.q.p, p.q.dt,
+                                             p.q.off(b, n * kC + r, h, l, 8 * (g4 + 4 * u)), p.q.sd)
+                                   : make_uint4(0, 0, 0, 0);
+          unpack8(raw, p.q.dt, f);
+          *q8 = pack8(f);
+        }
       }
     }
     fence_proxy_async();
@@ -1227,22 +1272,25 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     if (n + 1 < p.NT) fetch_eg(n + 1);
     if (n + 1 < p.NT && !fires) fetch_rows(n + 1);
 
-    // MMA2: S0 += K_tail^T v_new (naive.py:392); then the rest of the output
-    // into lanes 64..127: the upper-level reads (naive.py:382-385) and
-    // (mix0 scale A_qk) v_new (naive.py:379). Each of those A operands is the
-    // lower half of an M = 128 tile whose upper half (the 64 rows stored
-    // before it) only adds to the spent W.S0 lanes.
+    // MMA2: S0 += K_tail^T v_new (naive.py:392); (mix0 scale A_qk) v_new
+    // into the output lanes 64..127 (naive.py:379); the upper-level reads
+    // q_l . S_l (naive.py:382-385) into lanes 64..127 of their own
+    // accumulators, weighted by mix_l * scale per row in E2. Each of those A
+    // operands is the lower half of an M = 128 tile whose upper half (the 64
+    // rows stored before it) only lands in lanes that are never read.
     if (tid == 0) {
       if (!mbar_wait(&bar_ld2, ph_ld2)) abort_flag = 1;
+      if (L > 1 && !q_conv && !mbar_wait(&bar_q, ph_q)) abort_flag = 1;
       fence_after_sync();
       mma_tile(tS0, smem_u32(Rec + lay.rec.Kt), smem_u32(Vn), kC, id_state, true);
-      for (int l = 1; l < L; ++l)
-        mma_tile(tD, smem_u32(Rec + lay.rec.Q + (l - 1) * TILE_QK), smem_u32(Sbf + l * TK * TV), TK,
-                 id_m128, true);
       mma_tile(tD, smem_u32(Rec + lay.rec.A - TILE_A), smem_u32(Vn), kC, id_m128, true);
+      for (int l = 1; l < L; ++l)
+        mma_tile_sw128_lo(tD + 128 * l, smem_u32(QT + (l - 1) * TILE_QK),
+                          smem_u32(Sbf + l * TK * TV), id_m128, false);
       mma_commit(&bar_mma);
     }
     ph_ld2 ^= 1;
+    ph_q ^= 1;
     __syncwarp();
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
@@ -1252,8 +1300,12 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     // (Only when the bank stays clear of the v_new tile that the output
     // rows are staged in.)
     const int first = fires ? __ffs(fire_mask) - 1 : 0;
-    const bool early = fires && learned && 65536 + pad_pairs(p.nq[first - 1]) * 256 <= load_bytes;
-    if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, false);
+    const bool early = fires && learned &&
+                       65536 + pad_pairs(p.nq[first - 1]) * 256 <= load_bytes + (L - 1) * TILE_QK;
+    if (tid == 0 && n + 1 < p.NT && !fires) {
+      load_part(recg + lay.rec.size, false);
+      load_q(n + 1);
+    }
     if (tid == 0 && early) promote_tc_first_loads(p, lay, ws, h, first, Rec, &bar_ld);
     const bool write_master = (fires && !learned) || n + 1 == p.NT;
     const bool stage16 = p.dtype == NGDN2_BF16 || p.dtype == NGDN2_F16;
@@ -1265,19 +1317,41 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     {
       float x[32];
       if (quarter >= 2) {
+        // In halves of 16 columns: output = level-0 part + sum_l mix_l scale
+        // (q_l . S_l).
         const int i = 32 * (quarter - 2) + lane, t = n * kC + i;
-        tmem_ld32(taddr(tD, 32 * quarter, c0), x);
-        if (stage16) {
-          uint4* row = reinterpret_cast<uint4*>(Vn) + i * 16;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int ch = (c0 >> 3) + c;
-            row[ch ^ (i & 15)] = p.dtype == NGDN2_BF16 ? pack8(x + 8 * c) : pack8h(x + 8 * c);
+        for (int hh = 0; hh < 2; ++hh) {
+          float xo[16];
+          uint32_t y[2][16];
+          tmem_ld16_nowait(taddr(tD, 32 * quarter, c0 + 16 * hh),
+                           reinterpret_cast<uint32_t*>(xo));
+          // (Both level accumulators are loaded whatever L is: the columns
+          // are allocated; only the levels present are added.)
+          tmem_ld16_nowait(taddr(tD + 128, 32 * quarter, c0 + 16 * hh), y[0]);
+          tmem_ld16_nowait(taddr(tD + 256, 32 * quarter, c0 + 16 * hh), y[1]);
+          tmem_wait_ld();
+          tmem_regs_after_wait16(reinterpret_cast<uint32_t*>(xo));
+#pragma unroll
+          for (int l = 1; l < 3; ++l) {
+            tmem_regs_after_wait16(y[l - 1]);
+            if (l >= L) break;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              xo[j] = fmaf(mixr[l - 1], __uint_as_float(y[l - 1][j]), xo[j]);
           }
-        } else if (t < p.T) {
-          const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + c0;
+          if (stage16) {
+            uint4* row = reinterpret_cast<uint4*>(Vn) + i * 16;
 #pragma unroll
-          for (int u = 0; u < 32; ++u) store_elem(p.o, o + u, x[u], p.dtype);
+            for (int c = 0; c < 2; ++c) {
+              const int ch = (c0 >> 3) + 2 * hh + c;
+              row[ch ^ (i & 15)] = p.dtype == NGDN2_BF16 ? pack8(xo + 8 * c) : pack8h(xo + 8 * c);
+            }
+          } else if (t < p.T) {
+            const int64_t o = ((int64_t(b) * p.T + t) * p.H + h) * TV + c0 + 16 * hh;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) store_elem(p.o, o + u, xo[u], p.dtype);
+          }
         }
       }
       // The new S0: bf16 copy (and fp32 master), then S0 in TMEM decayed
@@ -1300,6 +1374,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
         tmem_wait_st();
       }
     }
+    if (n + 1 < p.NT) fetch_mix(n + 1);
     if (stage16) {
       __syncthreads();
       // 64 rows x 16 chunks of 16 bytes: each warp stores two whole rows per step.
@@ -1338,6 +1413,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       if (tid == 0 && n + 1 < p.NT) {
         load_part(recg + lay.rec.size, true);
         load_part(recg + lay.rec.size, false);
+        load_q(n + 1);
       }
       if (n + 1 < p.NT) fetch_rows(n + 1);
     }
@@ -1364,12 +1440,53 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
 
 static bool is16(int dt) { return dt == NGDN2_BF16 || dt == NGDN2_F16; }
 
+// How the scan's tensor map walks q's (head, level) pairs: 0 when the level
+// index is the contiguous one (hl = h * L + l), 1 when the head is (hl =
+// l * H + h), -1 when q's layout has no such single stride.
+// The map needs 16-byte aligned q and token stride, (b, t) rows in one
+// stride and one of the two (head, level) layouts; 2 otherwise.
+static int q_hl_mode(const FwdParams& p) {
+  const auto& q = p.q;
+  if (q.sd != 1 || q.sb != int64_t(p.T) * q.st || q.st % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(q.p) & 15) != 0)
+    return 2;
+  if (q.sl == TK && q.sh == int64_t(p.L) * TK) return 0;
+  if (q.sh == TK && q.sl == int64_t(p.H) * TK) return 1;
+  return 2;
+}
+
 bool tc_supports(const ngdn2_fwd_args* a) {
   if (a->K != TK || a->V != TV || a->L < 1 || a->L > 3) return false;
   if (!is16(a->q_dtype) || !is16(a->k_dtype) || !is16(a->v_dtype) || !is16(a->b_dtype) ||
       !is16(a->w_dtype) || !is16(a->dtype))
     return false;
   return true;
+}
+
+// Tensor map of q for the scan (see scan_tc_kernel): 4-D view whose
+// (64, 64, 2, 1) box is one chunk's [64 x 128] operand, 128-byte swizzled.
+static bool make_q_map(const FwdParams& p, CUtensorMap* m) {
+  static PFN_cuTensorMapEncodeTiled encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+  }
+  // Both (head, level) layouts step from one pair to the next by K elements.
+  const cuuint64_t dims[4] = {64, cuuint64_t(p.B) * p.T, TK / 64, cuuint64_t(p.H) * p.L};
+  const cuuint64_t strides[3] = {cuuint64_t(p.q.st) * 2, 128, cuuint64_t(TK) * 2};
+  const cuuint32_t box[4] = {64, kC, TK / 64, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = encode(
+      m, p.q.dt == NGDN2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+      4, const_cast<void*>(p.q.p), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 size_t tc_workspace_bytes(const FwdParams& p) { return size_t(tc_layout(p).total); }
@@ -1403,7 +1520,11 @@ cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t 
     const int smem = int(scan_tc_smem(p.L, lay.rec));
     err = cudaFuncSetAttribute(scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
-    scan_tc_kernel<<<dim3(p.H, p.B), kScanThreads, smem, stream>>>(p, lay, ws);
+    CUtensorMap qmap;
+    memset(&qmap, 0, sizeof(qmap));
+    const int hl_mode = p.L > 1 ? q_hl_mode(p) : 2;
+    if (hl_mode != 2 && !make_q_map(p, &qmap)) return cudaErrorInvalidValue;
+    scan_tc_kernel<<<dim3(p.H, p.B), kScanThreads, smem, stream>>>(p, lay, ws, qmap, hl_mode);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
   }
   return cudaSuccess;

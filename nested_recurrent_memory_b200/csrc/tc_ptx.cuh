@@ -56,6 +56,29 @@ __device__ __forceinline__ uint64_t desc_tile(uint32_t saddr, int Kd, int kk) {
   return desc_noswz(saddr + kk * 256, 128, Kd * 16);
 }
 
+// 128-byte-swizzled K-major layout (what a TMA copy with SWIZZLE_128B
+// writes): rows of 64 bf16 = 128 bytes, 8-row atoms of 1024 bytes (1024-byte
+// aligned) whose 16-byte chunks are XOR-permuted by the row within the atom,
+// atoms stacked along M; a K extent of 128 is two such [M x 64] blocks.
+// sw128_off gives the byte offset of element (r, k) in an M = 64 tile
+// (blocks 8 KB apart).
+__device__ __forceinline__ int sw128_off(int r, int k) {
+  return (k >> 6) * 8192 + (r >> 3) * 1024 + (r & 7) * 128 + ((((k & 63) >> 3) ^ (r & 7)) << 4) +
+         (k & 7) * 2;
+}
+
+// Descriptor of a 128-byte-swizzled K-major operand: 8-row groups SBO bytes
+// apart; the leading offset is unused for this layout (encoded as 1).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2) << 61;  // layout: 128-byte swizzle
+  return d;
+}
+
 // Instruction descriptor, kind::f16 with fp32 accumulate.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a_mn, bool b_mn) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
@@ -80,6 +103,17 @@ __device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_saddr, uint
   for (int kk = 0; kk < Kd / 16; ++kk)
     mma_f16(d_tmem, desc_tile(a_saddr, Kd, kk), desc_tile(b_saddr, Kd, kk), idesc,
             (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// C[128 x N] (+)= A[128 x 128] . B[128 x N] where A's rows 64..127 are the
+// M = 64, 128-byte-swizzled tile at a_tile (sw128_off) and rows 0..63 are
+// whatever the 8 KB before each of its two K blocks holds; B as mma_tile.
+__device__ __forceinline__ void mma_tile_sw128_lo(uint32_t d_tmem, uint32_t a_tile,
+                                                  uint32_t b_saddr, uint32_t idesc,
+                                                  bool accumulate) {
+  for (int kk = 0; kk < 8; ++kk)
+    mma_f16(d_tmem, desc_sw128(a_tile + (kk >> 2) * 8192 + (kk & 3) * 32 - 8192, 1024),
+            desc_tile(b_saddr, 128, kk), idesc, (accumulate || kk > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -133,6 +167,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 16 columns; no wait (pair with tmem_wait_ld and
+// tmem_regs_after_wait16). Warp-collective.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_regs_after_wait16(uint32_t* r) {
+  asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+               "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+               "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])::"memory");
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
@@ -246,6 +298,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Tiled tensor-map load (no multicast) of one 4-D box into shared memory,
+// completing its bytes on ``bar``. The tensor map lives in kernel parameter
+// space (__grid_constant__); the innermost coordinate is always 0 here.
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0, int c1, int c2,
+                                            int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar))
       : "memory");
 }
 

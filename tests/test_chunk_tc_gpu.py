@@ -186,3 +186,25 @@ def test_128_pairs_per_firing(promotion):
     ro, rs = _oracle(inp, 3, promotion)
     assert rel_err(_np(o), ro) < LOWP_REL
     assert rel_err(_np(s), rs) < LOWP_REL
+
+
+def test_query_layouts_agree_bitwise():
+    """q in each layout the scan reads it from: [B, T, H, L, K] contiguous and
+    the layer's [B, T, L, H, K] transposed view (both through the tensor map),
+    and a view cut from a longer sequence (its batch stride is not T tokens:
+    plain loads). Same values, so the same bits out."""
+    inp = config_inputs(2, 192, 2, 128, 128, 3, 64, (1, 2, 4), dtype=torch.bfloat16, seed=11)
+    inp.pop("L")
+    d = _dev(inp)
+    q = d["q"]
+    longer = torch.zeros(2, 200, *q.shape[2:], dtype=q.dtype, device="cuda")
+    longer[:, :192] = q
+    outs = []
+    for qq in (q, q.transpose(2, 3).contiguous().transpose(2, 3), longer[:, :192]):
+        call = FwdCall(**dict(d, q=qq), L=3, path="tc")
+        outs.append(call.launch())
+        assert call.path == "tc"
+    torch.cuda.synchronize()
+    assert outs[1][0].data_ptr() != outs[0][0].data_ptr()
+    for o, s in outs[1:]:
+        assert torch.equal(o, outs[0][0]) and torch.equal(s, outs[0][1])
