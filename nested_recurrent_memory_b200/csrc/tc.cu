@@ -1041,7 +1041,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUtensorMap qmap,
                int hl_mode) {
   extern __shared__ __align__(1024) uint8_t sm_raw[];
-  __shared__ uint64_t bar_ld, bar_ld2, bar_mma, bar_q;
+  __shared__ uint64_t bar_ld, bar_ld2, bar_mma, bar_q, bar_lvl;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   __shared__ float egp[128];
@@ -1074,6 +1074,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     mbar_init(&bar_ld2, 1);
     mbar_init(&bar_mma, 1);
     mbar_init(&bar_q, 1);
+    mbar_init(&bar_lvl, 1);
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -1126,7 +1127,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     mbar_arrive_expect_tx(bar, hi - lo);
     bulk_g2s(Rec + lo, src + lo, hi - lo, bar);
   };
-  uint32_t ph_ld2 = 0, ph_q = 0;
+  uint32_t ph_ld2 = 0, ph_q = 0, ph_lvl = 0;
   // The upper levels' raw query tiles of chunk nn (read by MMA2 after the
   // warps idle in E1 scale their rows by mix_l * scale; naive.py:382-385).
   const bool q_tma = hl_mode != 2;
@@ -1216,6 +1217,21 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
       mma_tile(tD, smem_u32(Rec + lay.rec.W), smem_u32(Sbf), TK, id_m128, false);
       mma_commit(&bar_mma);
     }
+    // The upper-level reads q_l . S_l (naive.py:382-385) need neither v_new
+    // nor S0: with bf16 query tiles from the map they are issued here, by a
+    // thread of a warp that E1 leaves idle, so the tensor pipe runs them
+    // during E1. Each lands in lanes 64..127 of its own accumulator (the
+    // lower half of an M = 128 tile whose upper half, the 64 rows stored
+    // before the tile, lands in lanes that are never read) and is weighted
+    // by mix_l * scale per row in E2.
+    if (tid == 64 && L > 1 && !q_conv) {
+      if (!mbar_wait(&bar_q, ph_q)) abort_flag = 1;
+      fence_after_sync();
+      for (int l = 1; l < L; ++l)
+        mma_tile_sw128_lo(tD + 128 * l, smem_u32(QT + (l - 1) * TILE_QK),
+                          smem_u32(Sbf + l * TK * TV), id_m128, false);
+      mma_commit(&bar_lvl);
+    }
     __syncwarp();
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
@@ -1273,20 +1289,18 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     if (n + 1 < p.NT && !fires) fetch_rows(n + 1);
 
     // MMA2: S0 += K_tail^T v_new (naive.py:392); (mix0 scale A_qk) v_new
-    // into the output lanes 64..127 (naive.py:379); the upper-level reads
-    // q_l . S_l (naive.py:382-385) into lanes 64..127 of their own
-    // accumulators, weighted by mix_l * scale per row in E2. Each of those A
-    // operands is the lower half of an M = 128 tile whose upper half (the 64
-    // rows stored before it) only lands in lanes that are never read.
+    // into the output lanes 64..127 (naive.py:379), as the lower half of an
+    // M = 128 tile like the reads; and the upper-level reads here when their
+    // tiles needed the conversion pass.
     if (tid == 0) {
       if (!mbar_wait(&bar_ld2, ph_ld2)) abort_flag = 1;
-      if (L > 1 && !q_conv && !mbar_wait(&bar_q, ph_q)) abort_flag = 1;
       fence_after_sync();
       mma_tile(tS0, smem_u32(Rec + lay.rec.Kt), smem_u32(Vn), kC, id_state, true);
       mma_tile(tD, smem_u32(Rec + lay.rec.A - TILE_A), smem_u32(Vn), kC, id_m128, true);
-      for (int l = 1; l < L; ++l)
-        mma_tile_sw128_lo(tD + 128 * l, smem_u32(QT + (l - 1) * TILE_QK),
-                          smem_u32(Sbf + l * TK * TV), id_m128, false);
+      if (q_conv)
+        for (int l = 1; l < L; ++l)
+          mma_tile_sw128_lo(tD + 128 * l, smem_u32(QT + (l - 1) * TILE_QK),
+                            smem_u32(Sbf + l * TK * TV), id_m128, false);
       mma_commit(&bar_mma);
     }
     ph_ld2 ^= 1;
@@ -1294,6 +1308,10 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     __syncwarp();
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
+    if (L > 1 && !q_conv) {
+      if (!mbar_wait(&bar_lvl, ph_lvl)) abort_flag = 1;
+      ph_lvl ^= 1;
+    }
     fence_after_sync();
     // The rest of the next record streams in during the epilogue; at a
     // firing the first learned promotion's operands do instead.

@@ -301,6 +301,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Hint: bring [src, src + bytes) into L2 (16-byte aligned, multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Tiled tensor-map load (no multicast) of one 4-D box into shared memory,
 // completing its bytes on ``bar``. The tensor map lives in kernel parameter
 // space (__grid_constant__); the innermost coordinate is always 0 here.
