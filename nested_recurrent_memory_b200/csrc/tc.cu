@@ -61,7 +61,7 @@ struct TcRecord {
     r.Kt = r.Q + TILE_QK;                     // [64 tok x K] MN-major A operand (K_tail^T)
     r.A = r.Kt + TILE_QK;                     // [64 x 64] K-major A operand
     r.load_bytes = r.A + TILE_A;              // the part the scan copies to smem
-    r.U = r.load_bytes;                       // [64 x V] row-major bf16
+    r.U = r.load_bytes;                       // [V/8][64 rows][8] bf16 (16-byte pieces)
     r.eg = r.U + kC * TV * 2;                 // [K] fp32 e^(G_last)
     r.size = (r.eg + TK * 4 + 127) & ~int64_t(127);
     return r;
@@ -666,8 +666,10 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       if (lane < 16) {
         const int d0 = 16 * c16;
         if (ch == 0) {
-          *reinterpret_cast<uint4*>(Ug + i * 128 + d0) = pack8(v);
-          *reinterpret_cast<uint4*>(Ug + i * 128 + d0 + 8) = pack8(v + 8);
+          // 8-column pieces, rows consecutive within a piece: the scan's
+          // lane-per-row loads of one piece are then contiguous.
+          *reinterpret_cast<uint4*>(Ug + (d0 / 8) * (kC * 8) + i * 8) = pack8(v);
+          *reinterpret_cast<uint4*>(Ug + (d0 / 8 + 1) * (kC * 8) + i * 8) = pack8(v + 8);
         } else {
           *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0, 128)) = pack8(v);
           *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0 + 8, 128)) = pack8(v + 8);
@@ -1150,15 +1152,34 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
   // mix_l * scale of the upper levels for the output row this thread
   // assembles in E2 (threads of lane quarters 2 and 3), one chunk ahead.
   const int jq = (warp >> 2) * 64 + (warp & 1) * 32 + lane;  // 0..255 among them
+  // The raw bits are loaded at the top of the chunk before and converted
+  // after that chunk's E2, so the load latency hides behind a whole chunk.
   float mixr[2] = {0.f, 0.f};
-  bool qrow = false;
+  uint32_t mixraw[2] = {0u, 0u};
   auto fetch_mix = [&](int nn) {
     if (quarter < 2) return;
     const int t = nn * kC + (jq & 63);
-    qrow = t < p.T;
 #pragma unroll
-    for (int l = 1; l < 3; ++l)
-      if (l < L) mixr[l - 1] = qrow ? p.mix.at(b, t, h, l) * p.scale : 0.f;
+    for (int l = 1; l < 3; ++l) {
+      if (l >= L) break;
+      mixraw[l - 1] = 0u;
+      if (t < p.T) {
+        const int64_t o = p.mix.off(b, t, h, l);
+        mixraw[l - 1] = p.mix.dt == NGDN2_F32
+                            ? __ldg(reinterpret_cast<const unsigned int*>(p.mix.p) + o)
+                            : uint32_t(__ldg(reinterpret_cast<const unsigned short*>(p.mix.p) + o));
+      }
+    }
+  };
+  auto take_mix = [&]() {
+#pragma unroll
+    for (int l = 0; l < 2; ++l) {
+      const uint32_t r = mixraw[l];
+      const float m = p.mix.dt == NGDN2_F32    ? __uint_as_float(r)
+                      : p.mix.dt == NGDN2_BF16 ? __uint_as_float(r << 16)
+                                               : __half2float(__ushort_as_half(uint16_t(r)));
+      mixr[l] = m * p.scale;
+    }
   };
   // U rows (lanes of quarters 0 and 1) and e^(G_last) of a chunk, read from
   // its record in global memory one chunk ahead of use.
@@ -1167,10 +1188,12 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
   auto fetch_rows = [&](int nn) {
     const char* rg = rec0 + int64_t(nn) * lay.rec.size;
     if (quarter < 2) {
-      const uint4* Ug = reinterpret_cast<const uint4*>(rg + lay.rec.U) +
-                        ((32 * quarter + lane) * TV + c0) / 8;
+      // Piece c0/8 + c of row 32 * quarter + lane: a warp's load is 512
+      // contiguous bytes.
+      const uint4* Ug = reinterpret_cast<const uint4*>(rg + lay.rec.U) + (c0 / 8) * kC +
+                        32 * quarter + lane;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) urow[c] = __ldg(Ug + c);
+      for (int c = 0; c < 4; ++c) urow[c] = __ldg(Ug + c * kC);
     }
   };
   auto fetch_eg = [&](int nn) {
@@ -1183,6 +1206,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     fetch_rows(0);
     fetch_eg(0);
     fetch_mix(0);
+    take_mix();
     const uint32_t ta = taddr(tS0, 32 * quarter, c0);
     float x[32];
     tmem_ld32(ta, x);
@@ -1198,6 +1222,12 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     const char* recg = rec0 + int64_t(n) * lay.rec.size;
     if (!mbar_wait(&bar_ld, ph_ld)) abort_flag = 1;
     ph_ld ^= 1;
+    // e^(G_last) of the next chunk (for the decay in this chunk's E2) and
+    // its mix weights.
+    if (n + 1 < p.NT) {
+      fetch_eg(n + 1);
+      fetch_mix(n + 1);
+    }
     uint32_t fire_mask = 0;
     if (L > 1 && --left1 == 0) {
       fire_mask |= 2u;
@@ -1265,7 +1295,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
                                                sw128_off(r, 8 * (g4 + 4 * u)));
           float f[8];
           const uint4 raw = q_tma ? *q8
-                            : qrow ? raw8_at(p.q.p, p.q.dt,
+                            : n * kC + r < p.T ? raw8_at(p.q.p, p.q.dt,
                                              p.q.off(b, n * kC + r, h, l, 8 * (g4 + 4 * u)), p.q.sd)
                                    : make_uint4(0, 0, 0, 0);
           unpack8(raw, p.q.dt, f);
@@ -1285,7 +1315,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     // MMA2 (U rows wait for the end of a promotion: they would hold
     // registers across it).
     if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, true);
-    if (n + 1 < p.NT) fetch_eg(n + 1);
+
     if (n + 1 < p.NT && !fires) fetch_rows(n + 1);
 
     // MMA2: S0 += K_tail^T v_new (naive.py:392); (mix0 scale A_qk) v_new
@@ -1320,11 +1350,11 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     const int first = fires ? __ffs(fire_mask) - 1 : 0;
     const bool early = fires && learned &&
                        65536 + pad_pairs(p.nq[first - 1]) * 256 <= load_bytes + (L - 1) * TILE_QK;
-    if (tid == 0 && n + 1 < p.NT && !fires) {
-      load_part(recg + lay.rec.size, false);
-      load_q(n + 1);
-    }
-    if (tid == 0 && early) promote_tc_first_loads(p, lay, ws, h, first, Rec, &bar_ld);
+    // (Issued by lanes of three warps of lane quarters 0 and 1, whose share
+    // of E2 is the shortest; warp 0's thread 0 issues the MMAs.)
+    if (tid == 32 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, false);
+    if (tid == 128 && n + 1 < p.NT && !fires) load_q(n + 1);
+    if (tid == 160 && early) promote_tc_first_loads(p, lay, ws, h, first, Rec, &bar_ld);
     const bool write_master = (fires && !learned) || n + 1 == p.NT;
     const bool stage16 = p.dtype == NGDN2_BF16 || p.dtype == NGDN2_F16;
 
@@ -1392,7 +1422,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
         tmem_wait_st();
       }
     }
-    if (n + 1 < p.NT) fetch_mix(n + 1);
+    take_mix();
     if (stage16) {
       __syncthreads();
       // 64 rows x 16 chunks of 16 bytes: each warp stores two whole rows per step.
