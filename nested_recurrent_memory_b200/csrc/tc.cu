@@ -1311,12 +1311,10 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     // a promotion needs the buffer as scratch first). It is issued only after
     // this barrier, which every thread reaches after its wait on bar_ld: a
     // phase completing early could otherwise alias the parity a slow thread
-    // still waits for. The next chunk's U rows and e^(G_last) load during
-    // MMA2 (U rows wait for the end of a promotion: they would hold
-    // registers across it).
-    if (tid == 0 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, true);
-
-    if (n + 1 < p.NT && !fires) fetch_rows(n + 1);
+    // still waits for. (Issued by warp 1: thread 0 goes on to MMA2.) The
+    // next chunk's U rows load during MMA2 (at a firing they wait for the
+    // end of the promotions: they would hold registers across them).
+    if (tid == 32 && n + 1 < p.NT && !fires) load_part(recg + lay.rec.size, true);
 
     // MMA2: S0 += K_tail^T v_new (naive.py:392); (mix0 scale A_qk) v_new
     // into the output lanes 64..127 (naive.py:379), as the lower half of an
@@ -1333,6 +1331,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
                             smem_u32(Sbf + l * TK * TV), id_m128, false);
       mma_commit(&bar_mma);
     }
+    if (n + 1 < p.NT && !fires) fetch_rows(n + 1);
     ph_ld2 ^= 1;
     ph_q ^= 1;
     __syncwarp();
