@@ -113,20 +113,11 @@ __device__ __forceinline__ float fast_sigmoid(float x) {
 __device__ __forceinline__ float fast_softplus(float x) {
   return x > 20.f ? x : __logf(1.f + __expf(x));
 }
-// softplus(x) = max(x, 0) + log1p(e^-|x|) with one hardware exponential and
-// log1p on [0, 1] as z * q(z), q of degree 7: a least-squares fit on 4000
-// Chebyshev nodes (max abs error 1.4e-7 evaluated in fp32 Horner form).
-__device__ __forceinline__ float softplus_poly(float x) {
-  const float z = __expf(-fabsf(x));
-  float q = -0.0064523066f;
-  q = fmaf(q, z, 0.03608331f);
-  q = fmaf(q, z, -0.09532055f);
-  q = fmaf(q, z, 0.16764624f);
-  q = fmaf(q, z, -0.24073002f);
-  q = fmaf(q, z, 0.33179808f);
-  q = fmaf(q, z, -0.49987403f);
-  q = fmaf(q, z, 0.9999964f);
-  return fmaxf(x, 0.f) + q * z;
+// softplus(x) = max(x, 0) + log(1 + e^-|x|) with the hardware exponential
+// and logarithm (absolute error about 1e-7; the decay gate's values are
+// rounded to fp16 partials right after).
+__device__ __forceinline__ float softplus_fast(float x) {
+  return fmaxf(x, 0.f) + __logf(1.f + __expf(-fabsf(x)));
 }
 // sigmoid(x) = (1 + tanh(x / 2)) / 2 with the hardware tanh (absolute error
 // about 2.5e-4): used for the write gate, whose values sit near 1/2 and
@@ -842,7 +833,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
           const float got = __shfl_xor_sync(0xffffffffu, hi ? a[j + e] : a[16 + j + e], 16);
           const float wl = hi ? got : mine_w, gl = hi ? mine_g : got;
           sw[j + e] = sigmoid_tanh(wl + kWLogitInit);
-          gg[e] = -softplus_poly(gl + kGLogitInit);
+          gg[e] = -softplus_fast(gl + kGLogitInit);
         }
         const __half2 g2 = __floats2half2_rn(gg[0], gg[1]);
         gpart16[gr * 64 + (((cb + j) >> 1) ^ (gr & 31))] = *reinterpret_cast<const uint32_t*>(&g2);
@@ -864,7 +855,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
       tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), a);
 #pragma unroll
       for (int u = 0; u < 32; ++u)
-        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -softplus_poly(a[u] + kGLogitInit);
+        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -softplus_fast(a[u] + kGLogitInit);
     }
   }
   tmem_wait_st();
@@ -1238,6 +1229,11 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
       left2 = p.firing[2];
     }
     const bool fires = fire_mask != 0;
+    // The fp32 masters that this chunk's learned promotions read (at P3)
+    // are asked into L2 now, a chunk's work ahead of use.
+    if (tid == 96 && fires && learned)
+      for (int l = 1; l < L; ++l)
+        if (fire_mask >> l & 1u) bulk_prefetch_l2(Mt + int64_t(l - 1) * TK * TV, TK * TV * 4);
 
     // MMA1: [W; Q_0] . S0 as one M = 128 tile (W and Q_0 are adjacent in the
     // record): W.S0 in lanes 0..63 and the level-0 read in lanes 64..127,
