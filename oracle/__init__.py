@@ -9,6 +9,10 @@ timed CPU restatement of the reference algorithm).
 (``nested_gdn2/ops/naive.py``) and its promotion probes
 (``nested_gdn2/ops/probe.py``). Parity of this restatement is pinned against
 golden vectors produced by the reference itself (``tests/golden/``).
+``naive_torch`` is a differentiable torch restatement of the chunkwise oracle
+(imported as ``oracle.naive_torch``); the backward's parity tests take
+autograd through it, and its gradients are pinned to golden gradients taken
+by autograd through the reference's oracle (``tests/golden/bwd_*.npz``).
 """
 
 from .naive_np import (  # noqa: F401
