@@ -187,11 +187,41 @@ typedef struct ngdn2_step_args {
   int32_t* status;
 } ngdn2_step_args;
 
+/* Arguments of ngdn2_bwd: the gradients of sum(o * d_o) + sum(final * d_final)
+ * with respect to every differentiable input of the forward
+ * (ChunkNestedGDN2Function.backward, chunk.py:650-719, whose gradient
+ * composition is chunk_nested_gdn2_bwd, chunk.py:368-564). Computed on CUDA
+ * cores in fp32 from a re-run of the forward. Gradient outputs are fp32 and
+ * contiguous in the shape of their input. */
+typedef struct ngdn2_bwd_args {
+  int32_t abi_version;
+  ngdn2_fwd_args fwd;   /* the forward's arguments; its o, final_state,
+                           workspace and path are not used */
+  const void* d_o; int32_t d_o_dtype; int64_t d_o_stride[4];  /* [B, T, H, V] */
+  const float* d_final;        /* [B, H, L, K, V] contiguous, or NULL for zeros */
+  float* dq;                   /* [B, T, H, L, K] */
+  float* dk;                   /* [B, T, H, K] */
+  float* dv;                   /* [B, T, H, V] */
+  float* dg;                   /* [B, T, H, K] */
+  float* db;                   /* [B, T, H, K] */
+  float* dw;                   /* [B, T, H, V] */
+  float* dmix;                 /* [B, T, H, L] */
+  float* dquery_banks;         /* [L-1, H, n_max, K], or NULL to skip */
+  float* dkey_projections;     /* [L-1, H, K, V], or NULL */
+  float* db_projections;       /* [L-1, H, V, K], or NULL */
+  float* dw_projections;       /* [L-1, H, V, V], or NULL */
+  float* dg_projections;       /* [L-1, H, V, K], or NULL */
+  float* dinitial_state;       /* [B, H, L, K, V], or NULL */
+  void* workspace;             /* >= ngdn2_bwd_workspace_size */
+  size_t workspace_bytes;
+} ngdn2_bwd_args;
+
 NGDN2_API int ngdn2_abi_version(void);
 /* sizeof the argument structs, so bindings can check their layout. */
 NGDN2_API size_t ngdn2_sizeof_fwd_args(void);
 NGDN2_API size_t ngdn2_sizeof_update_args(void);
 NGDN2_API size_t ngdn2_sizeof_step_args(void);
+NGDN2_API size_t ngdn2_sizeof_bwd_args(void);
 NGDN2_API const char* ngdn2_error_string(int code);
 
 /* Validates *args and returns the workspace ngdn2_fwd needs, in bytes. */
@@ -211,6 +241,18 @@ NGDN2_API int ngdn2_fwd_stage(const ngdn2_fwd_args* args, int stage, void* strea
 
 /* Number of kernel launches ngdn2_fwd makes for these arguments. */
 NGDN2_API int ngdn2_fwd_num_launches(const ngdn2_fwd_args* args);
+
+/* Validates *args and returns the workspace ngdn2_bwd needs, in bytes
+ * (the forward's records and checkpoints, the per-chunk state gradients and
+ * the backward's scratch: about (3 NT + 1) K V + 4 NT 64 (K + V) floats per
+ * (batch row, head)). */
+NGDN2_API int ngdn2_bwd_workspace_size(const ngdn2_bwd_args* args, size_t* bytes);
+
+/* The backward. Replaces chunk.py:650-719 (ChunkNestedGDN2Function.backward). */
+NGDN2_API int ngdn2_bwd(const ngdn2_bwd_args* args, void* stream);
+
+/* Number of kernel launches ngdn2_bwd makes (copies excluded). */
+NGDN2_API int ngdn2_bwd_num_launches(const ngdn2_bwd_args* args);
 
 /* The promotion write scan on its own. */
 NGDN2_API int ngdn2_update_state(const ngdn2_update_args* args, void* stream);

@@ -1,15 +1,16 @@
-"""B200-native nested Gated DeltaNet (nested GDN-2) forward hot path.
+"""B200-native nested Gated DeltaNet (nested GDN-2) hot path.
 
-A drop-in for the reference's ``nested_gdn2.ops`` forward ops
-(``chunk_nested_gdn2``, ``chunk_nested_gdn2_fwd``, ``update_state``, and the
-one-token decode step ``naive_step_nested_gdn2`` as ``step_nested_gdn2``),
-computed by hand-written sm_100a CUDA kernels behind the C ABI in
-``include/ngdn2.h``.
+A drop-in for the reference's ``nested_gdn2.ops`` ops (``chunk_nested_gdn2``
+with its backward, ``chunk_nested_gdn2_fwd``, ``chunk_nested_gdn2_bwd``,
+``update_state``, and the one-token decode step ``naive_step_nested_gdn2`` as
+``step_nested_gdn2``), computed by hand-written sm_100a CUDA kernels behind
+the C ABI in ``include/ngdn2.h``.
 """
 
 from .ops import (  # noqa: F401
     FwdCall,
     chunk_nested_gdn2,
+    chunk_nested_gdn2_bwd,
     chunk_nested_gdn2_fwd,
     fwd_workspace_bytes,
     last_path,

@@ -1,7 +1,7 @@
 """ctypes binding of ``libngdn2.so`` (the C ABI declared in include/ngdn2.h).
 
-The structs below mirror ``ngdn2_fwd_args``, ``ngdn2_update_args`` and
-``ngdn2_step_args`` field for field; ``check_layout()`` compares their sizes with the library's own
+The structs below mirror ``ngdn2_fwd_args``, ``ngdn2_update_args``,
+``ngdn2_step_args`` and ``ngdn2_bwd_args`` field for field; ``check_layout()`` compares their sizes with the library's own
 ``sizeof``. Loading fails loudly: there is no fallback implementation.
 """
 
@@ -81,11 +81,23 @@ class StepArgs(ctypes.Structure):
     ]
 
 
+class BwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", c_i32), ("fwd", FwdArgs), *_tok("d_o", 4), ("d_final", c_ptr),
+        ("dq", c_ptr), ("dk", c_ptr), ("dv", c_ptr), ("dg", c_ptr), ("db", c_ptr),
+        ("dw", c_ptr), ("dmix", c_ptr),
+        ("dquery_banks", c_ptr), ("dkey_projections", c_ptr), ("db_projections", c_ptr),
+        ("dw_projections", c_ptr), ("dg_projections", c_ptr), ("dinitial_state", c_ptr),
+        ("workspace", c_ptr), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 EXPORTS = (
     "ngdn2_abi_version", "ngdn2_sizeof_fwd_args", "ngdn2_sizeof_update_args",
     "ngdn2_error_string", "ngdn2_fwd_workspace_size", "ngdn2_fwd_select_path",
     "ngdn2_fwd", "ngdn2_fwd_stage", "ngdn2_fwd_num_launches", "ngdn2_update_state",
     "ngdn2_fwd_noalloc", "ngdn2_sizeof_step_args", "ngdn2_step_workspace_size", "ngdn2_step",
+    "ngdn2_sizeof_bwd_args", "ngdn2_bwd_workspace_size", "ngdn2_bwd", "ngdn2_bwd_num_launches",
 )
 
 _LIB = None
@@ -126,6 +138,13 @@ def load(path: str | os.PathLike | None = None):
     lib.ngdn2_step_workspace_size.restype = ctypes.c_int
     lib.ngdn2_step.argtypes = [ctypes.POINTER(StepArgs), c_ptr]
     lib.ngdn2_step.restype = ctypes.c_int
+    lib.ngdn2_sizeof_bwd_args.restype = ctypes.c_size_t
+    lib.ngdn2_bwd_workspace_size.argtypes = [ctypes.POINTER(BwdArgs), ctypes.POINTER(ctypes.c_size_t)]
+    lib.ngdn2_bwd_workspace_size.restype = ctypes.c_int
+    lib.ngdn2_bwd.argtypes = [ctypes.POINTER(BwdArgs), c_ptr]
+    lib.ngdn2_bwd.restype = ctypes.c_int
+    lib.ngdn2_bwd_num_launches.argtypes = [ctypes.POINTER(BwdArgs)]
+    lib.ngdn2_bwd_num_launches.restype = ctypes.c_int
     if path is None:
         _LIB = lib
     return lib
@@ -141,6 +160,8 @@ def check_layout(lib=None) -> None:
         raise RuntimeError("ngdn2_update_args layout mismatch")
     if lib.ngdn2_sizeof_step_args() != ctypes.sizeof(StepArgs):
         raise RuntimeError("ngdn2_step_args layout mismatch")
+    if lib.ngdn2_sizeof_bwd_args() != ctypes.sizeof(BwdArgs):
+        raise RuntimeError("ngdn2_bwd_args layout mismatch")
 
 
 def error_string(code: int) -> str:

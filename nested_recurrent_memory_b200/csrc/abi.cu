@@ -9,6 +9,10 @@ namespace ngdn2 {
 cudaError_t launch_fwd_simt(const FwdParams& p, int stage, cudaStream_t stream);
 int num_launches_simt(const FwdParams& p);
 cudaError_t launch_update_simt(const UpdParams& u, cudaStream_t stream);
+int64_t bwd_workspace_floats(const FwdParams& f);
+int num_launches_bwd(const FwdParams& f);
+struct BwdParams;
+cudaError_t launch_bwd_abi(const ngdn2_bwd_args* a, const FwdParams& f, cudaStream_t stream);
 }  // namespace ngdn2
 
 #include "tc_api.cuh"
@@ -21,7 +25,7 @@ bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
 bool dtype_ok(int d) { return d == NGDN2_F32 || d == NGDN2_BF16 || d == NGDN2_F16; }
 bool dim_ok(int d) { return d >= 16 && d <= 128 && d % 16 == 0; }
 
-int validate_fwd(const ngdn2_fwd_args* a) {
+int validate_fwd(const ngdn2_fwd_args* a, bool outputs = true) {
   if (!a) return NGDN2_ERR_NULL;
   if (a->abi_version != NGDN2_ABI_VERSION) return NGDN2_ERR_ABI;
   if (a->chunk_size != NGDN2_CHUNK) return NGDN2_ERR_CHUNK_SIZE;
@@ -45,8 +49,9 @@ int validate_fwd(const ngdn2_fwd_args* a) {
     if (a->promotion == NGDN2_PROMOTION_LEARNED && (n > a->n_max || n > 128))
       return NGDN2_ERR_SHAPE;
   }
-  if (!a->q || !a->k || !a->v || !a->g || !a->b || !a->w || !a->mix || !a->o || !a->final_state)
+  if (!a->q || !a->k || !a->v || !a->g || !a->b || !a->w || !a->mix)
     return NGDN2_ERR_NULL;
+  if (outputs && (!a->o || !a->final_state)) return NGDN2_ERR_NULL;
   if (a->L > 1 && (!a->query_banks || !a->key_projections || !a->b_projections ||
                    !a->w_projections || !a->g_projections))
     return NGDN2_ERR_NULL;
@@ -185,6 +190,50 @@ int ngdn2_fwd_stage(const ngdn2_fwd_args* a, int stage, void* stream) {
     p.scan = p.chunks + int64_t(p.B) * p.H * p.NT * p.rec.size;
     err = launch_fwd_simt(p, stage, st);
   }
+  return err == cudaSuccess ? NGDN2_OK : NGDN2_ERR_CUDA;
+}
+
+size_t ngdn2_sizeof_bwd_args(void) { return sizeof(ngdn2_bwd_args); }
+
+// The backward's own checks on top of the forward's (its o, final_state,
+// workspace and path are not used).
+static int validate_bwd(const ngdn2_bwd_args* a) {
+  if (!a) return NGDN2_ERR_NULL;
+  if (a->abi_version != NGDN2_ABI_VERSION) return NGDN2_ERR_ABI;
+  const int rc = validate_fwd(&a->fwd, false);
+  if (rc != NGDN2_OK) return rc;
+  if (!dtype_ok(a->d_o_dtype)) return NGDN2_ERR_DTYPE;
+  if (!a->d_o || !a->dq || !a->dk || !a->dv || !a->dg || !a->db || !a->dw || !a->dmix)
+    return NGDN2_ERR_NULL;
+  return NGDN2_OK;
+}
+
+int ngdn2_bwd_workspace_size(const ngdn2_bwd_args* a, size_t* bytes) {
+  const int rc = validate_bwd(a);
+  if (rc != NGDN2_OK) return rc;
+  if (!bytes) return NGDN2_ERR_NULL;
+  FwdParams p;
+  fill_params(&a->fwd, &p);
+  *bytes = size_t(bwd_workspace_floats(p)) * sizeof(float);
+  return NGDN2_OK;
+}
+
+int ngdn2_bwd_num_launches(const ngdn2_bwd_args* a) {
+  const int rc = validate_bwd(a);
+  if (rc != NGDN2_OK) return rc;
+  FwdParams p;
+  fill_params(&a->fwd, &p);
+  return num_launches_bwd(p);
+}
+
+int ngdn2_bwd(const ngdn2_bwd_args* a, void* stream) {
+  const int rc = validate_bwd(a);
+  if (rc != NGDN2_OK) return rc;
+  FwdParams p;
+  fill_params(&a->fwd, &p);
+  const size_t need = size_t(bwd_workspace_floats(p)) * sizeof(float);
+  if (!a->workspace || a->workspace_bytes < need) return NGDN2_ERR_WORKSPACE;
+  const cudaError_t err = launch_bwd_abi(a, p, reinterpret_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? NGDN2_OK : NGDN2_ERR_CUDA;
 }
 

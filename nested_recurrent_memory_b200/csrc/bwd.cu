@@ -1,0 +1,747 @@
+// Backward of the chunkwise nested GDN-2 forward, on CUDA cores in fp32.
+//
+// The reference's backward (nested_gdn2/ops/chunk.py:368-564,
+// ChunkNestedGDN2Function.backward :650-719) is a composition: read-level
+// einsums, a probe replay through autograd, update_state's own backward
+// (update_bwd.py) and fla's level-0 chunk backward with the promotions'
+// gradient injected as dh_ext. Here the same gradient is computed by three
+// kernels over the forward's own per-chunk records:
+//
+//   1. the CUDA-core forward (prep + scan) re-run with checkpoints: the
+//      level-0 state entering every chunk, every upper level's state entering
+//      every group, and v_new of every chunk;
+//   2. bwd_scan -- one CTA per (b, h), chunks in reverse: the state gradient
+//      of every level flows back through each chunk's level-0 recurrence,
+//      the upper-level reads, and at each firing the promotion (update step
+//      then probe, top level first); parameter gradients accumulate across
+//      the batch with atomics. Per chunk it leaves dS (leaving the chunk) and
+//      dv_new for the local pass;
+//   3. bwd_local -- one CTA per (b, h, chunk), fully parallel: the gradients
+//      of q, k, v, g, b, w and the mix weights from the chunk's quantities,
+//      recomputed from the inputs where cheap.
+//
+// Notation per chunk (64 tokens; naive.py:329-392): G = cumsum(g),
+// T = strictly-lower (b*k) k^T decayed, A_qk = lower q~ k^T decayed
+// (q~ = scale q_0), [U | W] = (I + T)^-1 [w*v | k*b*e^G], v_new = U - W S,
+// r_0 = A_qk v_new + (q~ e^G) S, o = sum_l mix_l r_l,
+// S' = e^(G_last) S + Kt^T v_new with Kt = k e^(G_last - G).
+
+#include <string.h>
+
+#include "fwd_params.cuh"
+#include "promote_simt.cuh"
+
+namespace ngdn2 {
+
+// Per-(b, h) scratch of the promotion backward, fp32, offsets in floats.
+struct PromoBwdScratch {
+  int64_t vp, keys, nrm, bg, wg, zg, z, y, dkeys, dkb, dvp, sd, dsd, gv, dgv, size;
+  __host__ __device__ static PromoBwdScratch make(int K, int V, int NP) {
+    PromoBwdScratch s;
+    const int64_t mv = int64_t(NP) * V, mk = int64_t(NP) * K, kv = int64_t(K) * V;
+    s.vp = 0;                              // [m, V] values V'
+    s.keys = align_floats(s.vp + mv);      // [m, K] keys (u / |u|)
+    s.nrm = align_floats(s.keys + mk);     // [m] max(|u|, 1e-12)
+    s.bg = align_floats(s.nrm + NP);       // [m, K] erase gate b
+    s.wg = align_floats(s.bg + mk);        // [m, V] write gate w
+    s.zg = align_floats(s.wg + mv);        // [m, K] decay logits V' W_g - 4
+    s.z = align_floats(s.zg + mk);         // [m, V] keys . dS'
+    s.y = align_floats(s.z + mv);          // [m, V] (keys * b) . S_d
+    s.dkeys = align_floats(s.y + mv);      // [m, K]
+    s.dkb = align_floats(s.dkeys + mk);    // [m, K] d(keys * b)
+    s.dvp = align_floats(s.dkb + mk);      // [m, V] dV'
+    s.sd = align_floats(s.dvp + mv);       // [K, V] e^g S
+    s.dsd = align_floats(s.sd + kv);       // [K, V] d(e^g S)
+    s.gv = align_floats(s.dsd + kv);       // [K] g
+    s.dgv = align_floats(s.gv + K);        // [K] dg
+    s.size = align_floats(s.dgv + K);
+    return s;
+  }
+};
+
+// Per-chunk scratch of the local pass, fp32, offsets in floats.
+struct LocalScratch {
+  int64_t dqg, dkt, drw, dru, dkta, size;
+  __host__ __device__ static LocalScratch make(int K, int V) {
+    LocalScratch s;
+    s.dqg = 0;                                  // [64, K] d(q~ e^G), mix_0 folded
+    s.dkt = align_floats(s.dqg + kC * K);       // [64, K] dKt
+    s.drw = align_floats(s.dkt + kC * K);       // [64, K] dW, then dR_W
+    s.dru = align_floats(s.drw + kC * K);       // [64, V] dU, then dR_U
+    s.dkta = align_floats(s.dru + kC * V);      // [64, K] dk from the decayed blocks
+    s.size = align_floats(s.dkta + kC * K);
+    return s;
+  }
+};
+
+struct BwdParams {
+  FwdParams f;  // inputs, converted parameters, records and checkpoints
+  const void* d_o;
+  int d_o_dtype;
+  int64_t dos[4];        // [B, T, H, V] element strides
+  const float* d_final;  // [B, H, L, K, V] or null
+  float *dq, *dk, *dv, *dg, *db, *dw, *dmix;  // fp32 outputs, contiguous
+  float* dparams;        // fp32 [B] x layout f.pl, zeroed before the scan (null when L == 1)
+  float* dinit;          // [B, H, L, K, V] or null
+  float* dS;             // [B, H, L, K, V] running state gradient
+  float* dsn;            // [B, H, NT, K, V] dS0 leaving each chunk
+  float* dvn;            // [B, H, NT, 64, V] dv_new of each chunk
+  float* pscr;           // [B, H] x PromoBwdScratch
+  PromoBwdScratch ps;
+  float* lscr;           // [B, H, NT] x LocalScratch
+  LocalScratch ls;
+};
+
+__device__ __forceinline__ float d_o_at(const BwdParams& p, int b, int t, int h, int c) {
+  if (t >= p.f.T) return 0.f;
+  return load_elem(p.d_o, b * p.dos[0] + t * p.dos[1] + h * p.dos[2] + c * p.dos[3], p.d_o_dtype);
+}
+
+__device__ __forceinline__ const float* ck_level(const FwdParams& f, int64_t bh, int level, int j) {
+  const int64_t kv = int64_t(f.K) * f.V;
+  return level == 0 ? f.ck0 + (bh * (f.NT + 1) + j) * kv
+                    : f.ck_up + f.ck_up_off[level] + (bh * f.ck_up_n[level] + j) * kv;
+}
+
+// Backward of one firing of level l at chunk n: the update step
+// (naive.py:7-39) after the probe (probe.py:34-136), both recomputed from the
+// checkpoints. In: dS_l after the firing. Out: dS_l before it, dS_{l-1}
+// (the source, level l-1 after chunk n) increased by the probe's gradient,
+// and the parameter gradients added into p.dparams.
+__device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, float* gsm) {
+  const FwdParams& f = p.f;
+  const int K = f.K, V = f.V, tid = threadIdx.x, nth = blockDim.x;
+  const int64_t bh = int64_t(b) * f.H + h;
+  const bool merge = f.promotion == NGDN2_PROMOTION_MERGE;
+  const int m = merge ? K : f.nq[l - 1];
+  const float* X = l == 1 ? ck_level(f, bh, 0, n + 1)
+                          : ck_level(f, bh, l - 1, (n + 1) / f.firing[l - 1]);
+  const float* Sold = ck_level(f, bh, l, n / f.firing[l]);
+  float* dSl = p.dS + (bh * f.L + l) * K * V;
+  float* dSb = p.dS + (bh * f.L + l - 1) * K * V;
+  const int64_t pidx = int64_t(l - 1) * f.H + h;
+  const float* qb = f.params32 + f.pl.qb + pidx * f.n_max * K;
+  const float* kp = f.params32 + f.pl.kp + pidx * K * V;
+  const float* bp = f.params32 + f.pl.bp + pidx * V * K;
+  const float* wp = f.params32 + f.pl.wp + pidx * V * V;
+  const float* gp = f.params32 + f.pl.gp + pidx * V * K;
+  // This batch row's own copy of the parameter gradients (summed over rows
+  // in a fixed order afterwards, so the result is reproducible).
+  float* dpar = p.dparams + int64_t(b) * f.pl.size;
+  float* dqb = dpar + f.pl.qb + pidx * f.n_max * K;
+  float* dkp = dpar + f.pl.kp + pidx * K * V;
+  float* dbp = dpar + f.pl.bp + pidx * V * K;
+  float* dwp = dpar + f.pl.wp + pidx * V * V;
+  float* dgp = dpar + f.pl.gp + pidx * V * K;
+  float* sc = p.pscr + bh * p.ps.size;
+  float* Vp = sc + p.ps.vp;
+  float* Kk = sc + p.ps.keys;
+  float* Nr = sc + p.ps.nrm;
+  float* Bg = sc + p.ps.bg;
+  float* Wg = sc + p.ps.wg;
+  float* Zg = sc + p.ps.zg;
+  float* Z = sc + p.ps.z;
+  float* Y = sc + p.ps.y;
+  float* dKk = sc + p.ps.dkeys;
+  float* dKB = sc + p.ps.dkb;
+  float* dVp = sc + p.ps.dvp;
+  float* Sd = sc + p.ps.sd;
+  float* dSd = sc + p.ps.dsd;
+  float* gv = sc + p.ps.gv;
+  float* dgv = sc + p.ps.dgv;
+  const int warp = tid / 32, lane = tid % 32, nwarp = nth / 32;
+
+  // --- the probe, recomputed (as promote_simt) ---
+  const float* vals = X;  // merge: the values are the level below (probe.py:133-136)
+  if (!merge) {
+    block_gemm(m, V, K, [&](int r, int k) { return qb[r * K + k]; },
+               [&](int k, int c) { return X[k * V + c]; }, gsm,
+               [&](int r, int c, float a) { Vp[r * V + c] = a; });
+    vals = Vp;
+    block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+               [&](int v, int k) { return kp[k * V + v]; }, gsm,
+               [&](int r, int k, float a) { Kk[r * K + k] = a; });
+    for (int r = warp; r < m; r += nwarp) {
+      float s = 0.f;
+      for (int k = lane; k < K; k += 32) s = fmaf(Kk[r * K + k], Kk[r * K + k], s);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float nrm = sqrtf(s);
+      for (int k = lane; k < K; k += 32) Kk[r * K + k] /= fmaxf(nrm, 1e-12f);
+      if (lane == 0) Nr[r] = nrm;
+    }
+  }
+  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+             [&](int v, int k) { return bp[v * K + k]; }, gsm,
+             [&](int r, int k, float a) { Bg[r * K + k] = sigmoidf_(a + kBLogitInit); });
+  block_gemm(m, V, V, [&](int r, int v) { return vals[r * V + v]; },
+             [&](int v, int u) { return wp[v * V + u]; }, gsm,
+             [&](int r, int u, float a) { Wg[r * V + u] = sigmoidf_(a + kWLogitInit); });
+  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+             [&](int v, int k) { return gp[v * K + k]; }, gsm,
+             [&](int r, int k, float a) { Zg[r * K + k] = a + kGLogitInit; });
+  for (int k = tid; k < K; k += nth) {
+    float s = 0.f;
+    for (int r = 0; r < m; ++r) s += -softplusf_(Zg[r * K + k]);
+    gv[k] = s / float(m);
+  }
+  __syncthreads();
+  for (int e = tid; e < K * V; e += nth) Sd[e] = Sold[e] * expf(gv[e / V]);
+  __syncthreads();
+
+  // --- backward of S' = S_d - K^T (K*b) S_d + K^T (V' * w), S_d = e^g S ---
+  // Z = K dS', Y = (K*b) S_d  (merge: K = I)
+  if (!merge) {
+    block_gemm(m, V, K, [&](int r, int k) { return Kk[r * K + k]; },
+               [&](int k, int c) { return dSl[k * V + c]; }, gsm,
+               [&](int r, int c, float a) { Z[r * V + c] = a; });
+    block_gemm(m, V, K, [&](int r, int k) { return Kk[r * K + k] * Bg[r * K + k]; },
+               [&](int k, int c) { return Sd[k * V + c]; }, gsm,
+               [&](int r, int c, float a) { Y[r * V + c] = a; });
+    // dK = (V' * w - Y) dS'^T;  d(K*b) = -Z S_d^T
+    block_gemm(m, K, V, [&](int r, int c) { return vals[r * V + c] * Wg[r * V + c] - Y[r * V + c]; },
+               [&](int c, int k) { return dSl[k * V + c]; }, gsm,
+               [&](int r, int k, float a) { dKk[r * K + k] = a; });
+    block_gemm(m, K, V, [&](int r, int c) { return Z[r * V + c]; },
+               [&](int c, int k) { return Sd[k * V + c]; }, gsm,
+               [&](int r, int k, float a) { dKB[r * K + k] = -a; });
+    // dS_d = dS' - (K*b)^T Z
+    block_gemm(K, V, m, [&](int k, int r) { return Kk[r * K + k] * Bg[r * K + k]; },
+               [&](int r, int c) { return Z[r * V + c]; }, gsm,
+               [&](int k, int c, float a) { dSd[k * V + c] = dSl[k * V + c] - a; });
+  } else {
+    for (int e = tid; e < K * V; e += nth) {
+      const int k = e / V;
+      Z[e] = dSl[e];
+      dSd[e] = dSl[e] - Bg[k * K + k] * dSl[e];
+    }
+    __syncthreads();
+    // d(K*b) only matters on the diagonal (b is read there only)
+    for (int k = warp; k < K; k += nwarp) {
+      float s = 0.f;
+      for (int c = lane; c < V; c += 32) s = fmaf(Z[k * V + c], Sd[k * V + c], s);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) dKB[k * K + k] = -s;
+    }
+    __syncthreads();
+  }
+  // dg = sum_v dS_d * S_d;  dS (before the firing) = e^g dS_d
+  for (int k = warp; k < K; k += nwarp) {
+    float s = 0.f;
+    for (int c = lane; c < V; c += 32) s = fmaf(dSd[k * V + c], Sd[k * V + c], s);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) dgv[k] = s;
+  }
+  __syncthreads();
+  for (int e = tid; e < K * V; e += nth) dSl[e] = expf(gv[e / V]) * dSd[e];
+  // Gates: dV' = Z * w; dw -> d(w logit) = Z * V' * w (1 - w) (into Wg);
+  // db = d(K*b) * K -> d(b logit) = db * b (1 - b) (into Bg);
+  // dK += d(K*b) * b; d(g logit) = -(dg / m) sigmoid(z) (into Zg).
+  for (int e = tid; e < m * V; e += nth) {
+    const float w = Wg[e], z = Z[e];
+    dVp[e] = z * w;
+    Wg[e] = z * vals[e] * w * (1.f - w);
+  }
+  for (int e = tid; e < m * K; e += nth) {
+    const int r = e / K, k = e % K;
+    const float bb = Bg[e];
+    float db;
+    if (merge) {
+      db = (r == k) ? dKB[e] : 0.f;
+    } else {
+      db = dKB[e] * Kk[e];
+      dKk[e] += dKB[e] * bb;
+    }
+    Bg[e] = db * bb * (1.f - bb);
+    Zg[e] = -(dgv[k] / float(m)) * sigmoidf_(Zg[e]);
+  }
+  __syncthreads();
+  // dV' += d(g logit) W_g^T + d(w logit) W_w^T + d(b logit) W_b^T
+  block_gemm(m, V, 2 * K + V,
+             [&](int r, int j) {
+               return j < K ? Zg[r * K + j] : j < 2 * K ? Bg[r * K + j - K] : Wg[r * V + j - 2 * K];
+             },
+             [&](int j, int v) {
+               return j < K ? gp[v * K + j] : j < 2 * K ? bp[v * K + j - K] : wp[v * V + j - 2 * K];
+             },
+             gsm, [&](int r, int v, float a) { dVp[r * V + v] += a; });
+  // parameter gradients of the gates: V'^T d(logit)
+  block_gemm(V, 2 * K + V, m, [&](int v, int r) { return vals[r * V + v]; },
+             [&](int r, int j) {
+               return j < K ? Zg[r * K + j] : j < 2 * K ? Bg[r * K + j - K] : Wg[r * V + j - 2 * K];
+             },
+             gsm, [&](int v, int j, float a) {
+               if (j < K) dgp[v * K + j] += a;
+               else if (j < 2 * K) dbp[v * K + j - K] += a;
+               else dwp[v * V + j - 2 * K] += a;
+             });
+  if (merge) {
+    for (int e = tid; e < K * V; e += nth) dSb[e] += dVp[e];
+    __syncthreads();
+    return;
+  }
+  // keys = u / max(|u|, 1e-12) (probe.py:100): du = (dK - K (K . dK)) / |u|
+  for (int r = warp; r < m; r += nwarp) {
+    float s = 0.f;
+    for (int k = lane; k < K; k += 32) s = fmaf(Kk[r * K + k], dKk[r * K + k], s);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float nrm = Nr[r];
+    for (int k = lane; k < K; k += 32) {
+      const float d = dKk[r * K + k];
+      dKk[r * K + k] = nrm > 1e-12f ? (d - Kk[r * K + k] * s) / nrm : d / 1e-12f;
+    }
+  }
+  __syncthreads();
+  // dV' += du W_k; dW_k += du^T V'
+  block_gemm(m, V, K, [&](int r, int k) { return dKk[r * K + k]; },
+             [&](int k, int v) { return kp[k * V + v]; }, gsm,
+             [&](int r, int v, float a) { dVp[r * V + v] += a; });
+  block_gemm(K, V, m, [&](int k, int r) { return dKk[r * K + k]; },
+             [&](int r, int v) { return vals[r * V + v]; }, gsm,
+             [&](int k, int v, float a) { dkp[k * V + v] += a; });
+  // V' = Q_bank X: dQ_bank += dV' X^T; dX = Q_bank^T dV'
+  block_gemm(m, K, V, [&](int r, int v) { return dVp[r * V + v]; },
+             [&](int v, int k) { return X[k * V + v]; }, gsm,
+             [&](int r, int k, float a) { dqb[r * K + k] += a; });
+  block_gemm(K, V, m, [&](int k, int r) { return qb[r * K + k]; },
+             [&](int r, int v) { return dVp[r * V + v]; }, gsm,
+             [&](int k, int v, float a) { dSb[k * V + v] += a; });
+}
+
+// ---------------------------------------------------------------------------
+// bwd_scan: grid (H, B), 256 threads; chunks in reverse.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
+  __shared__ float gsm[kGemmSmemFloats];
+  const FwdParams& f = p.f;
+  const int h = blockIdx.x, b = blockIdx.y, K = f.K, V = f.V, L = f.L, tid = threadIdx.x;
+  const int64_t bh = int64_t(b) * f.H + h;
+  float* dS = p.dS + bh * L * K * V;
+  for (int64_t e = tid; e < int64_t(L) * K * V; e += blockDim.x)
+    dS[e] = p.d_final ? p.d_final[bh * L * K * V + e] : 0.f;
+  __syncthreads();
+  for (int n = f.NT - 1; n >= 0; --n) {
+    const float* rec = f.chunks + (bh * f.NT + n) * f.rec.size;
+    const float* Am = rec + f.rec.A;   // mix0 scale A_qk
+    const float* Q0 = rec + f.rec.Q;   // mix0 scale q e^G
+    const float* Wm = rec + f.rec.W;
+    const float* Kt = rec + f.rec.Kt;
+    const float* eg = rec + f.rec.eg;
+    const int t0 = n * kC;
+    // The firings after this chunk, top level first (naive.py:394-415 reversed).
+    for (int l = L - 1; l >= 1; --l)
+      if ((n + 1) % f.firing[l] == 0) promote_bwd(p, b, h, l, n, gsm);
+    // Upper-level reads (naive.py:382-385): dS_l += (mix_l scale q_l)^T dO.
+    for (int l = 1; l < L; ++l) {
+      const float* Ql = rec + f.rec.Q + int64_t(l) * kC * K;
+      float* dSl = dS + int64_t(l) * K * V;
+      block_gemm(K, V, kC, [&](int k, int i) { return Ql[i * K + k]; },
+                 [&](int i, int c) { return d_o_at(p, b, t0 + i, h, c); }, gsm,
+                 [&](int k, int c, float a) { dSl[k * V + c] += a; });
+    }
+    // Level 0: dv_new = (mix0 scale A_qk)^T dO + Kt dS0 (the S0 entering the
+    // next chunk, naive.py:392), kept for the local pass with dS0 itself.
+    float* dv = p.dvn + (bh * f.NT + n) * kC * V;
+    block_gemm(kC, V, kC + K,
+               [&](int i, int j) { return j < kC ? Am[j * kC + i] : Kt[i * K + j - kC]; },
+               [&](int j, int c) {
+                 return j < kC ? d_o_at(p, b, t0 + j, h, c) : dS[(j - kC) * V + c];
+               },
+               gsm, [&](int i, int c, float a) { dv[i * V + c] = a; });
+    float* dsn = p.dsn + (bh * f.NT + n) * K * V;
+    for (int e = tid; e < K * V; e += blockDim.x) dsn[e] = dS[e];
+    __syncthreads();
+    // dS0 <- e^(G_last) dS0 + (mix0 scale q e^G)^T dO - W^T dv_new
+    block_gemm(K, V, 2 * kC,
+               [&](int k, int i) { return i < kC ? Q0[i * K + k] : -Wm[(i - kC) * K + k]; },
+               [&](int i, int c) { return i < kC ? d_o_at(p, b, t0 + i, h, c) : dv[(i - kC) * V + c]; },
+               gsm, [&](int k, int c, float a) { dS[k * V + c] = eg[k] * dS[k * V + c] + a; });
+  }
+  if (p.dinit)
+    for (int64_t e = tid; e < int64_t(L) * K * V; e += blockDim.x) p.dinit[bh * L * K * V + e] = dS[e];
+}
+
+// ---------------------------------------------------------------------------
+// bwd_local: grid (NT, H, B), 256 threads; the level-0 chunk backward and
+// the upper-level read gradients of one chunk.
+// ---------------------------------------------------------------------------
+
+size_t bwd_local_smem(int K) {
+  return sizeof(float) * (5 * size_t(kC) * (K + 1) + 3 * kC * 65 + kC + K + kGemmSmemFloats);
+}
+
+__global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
+  extern __shared__ float sm[];
+  const FwdParams& f = p.f;
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int K = f.K, V = f.V, KP = K + 1, tid = threadIdx.x, nth = blockDim.x;
+  const int64_t bh = int64_t(b) * f.H + h;
+  const int t0 = n * kC;
+  float* Gs = sm;               // [64][K+1] G = cumsum g
+  float* Qs = Gs + kC * KP;     // [64][K+1] scale q_0
+  float* Ks = Qs + kC * KP;     // [64][K+1] k
+  float* Bs = Ks + kC * KP;     // [64][K+1] b
+  float* dGs = Bs + kC * KP;    // [64][K+1] dG
+  float* Ts = dGs + kC * KP;    // [64][65] T (strictly lower)
+  float* As = Ts + kC * 65;     // [64][65] A_qk, then dA_qk
+  float* Dt = As + kC * 65;     // [64][65] dT
+  float* mx = Dt + kC * 65;     // [64] mix_l of the rows
+  float* dGl = mx + kC;         // [K] dG_last
+  float* gsm = dGl + K;
+  const float* rec = f.chunks + (bh * f.NT + n) * f.rec.size;
+  const float* Um = rec + f.rec.U;
+  const float* Wm = rec + f.rec.W;
+  const float* S0 = ck_level(f, bh, 0, n);
+  const float* dSn = p.dsn + (bh * f.NT + n) * K * V;
+  const float* dvn = p.dvn + (bh * f.NT + n) * kC * V;
+  const float* vn = f.ck_vnew + (bh * f.NT + n) * kC * V;
+  float* scr = p.lscr + (bh * f.NT + n) * p.ls.size;
+  float* dQG = scr + p.ls.dqg;
+  float* dKt = scr + p.ls.dkt;
+  float* dRW = scr + p.ls.drw;
+  float* dRU = scr + p.ls.dru;
+  float* dKTA = scr + p.ls.dkta;
+  auto dO = [&](int i, int c) { return d_o_at(p, b, t0 + i, h, c); };
+  // fp32 output row of token i (rows past T are never written)
+  auto orow = [&](int i, int width) { return ((int64_t(b) * f.T + t0 + i) * f.H + h) * width; };
+
+  // Inputs of the chunk; tokens past T are zeros (naive.py:302-312).
+  for (int e = tid; e < kC * K; e += nth) {
+    const int i = e / K, d = e % K, t = t0 + i;
+    const bool ok = t < f.T;
+    Qs[i * KP + d] = ok ? f.q.at(b, t, h, 0, d) * f.scale : 0.f;
+    Ks[i * KP + d] = ok ? f.k.at(b, t, h, d) : 0.f;
+    Gs[i * KP + d] = ok ? f.g.at(b, t, h, d) : 0.f;
+    Bs[i * KP + d] = ok ? f.b.at(b, t, h, d) : 0.f;
+    dGs[i * KP + d] = 0.f;
+  }
+  for (int i = tid; i < kC; i += nth) mx[i] = t0 + i < f.T ? f.mix.at(b, t0 + i, h, 0) : 0.f;
+  for (int k = tid; k < K; k += nth) dGl[k] = 0.f;
+  __syncthreads();
+  if (tid < K) {
+    float acc = 0.f;
+    for (int i = 0; i < kC; ++i) {
+      acc += Gs[i * KP + tid];
+      Gs[i * KP + tid] = acc;
+    }
+  }
+  __syncthreads();
+  // T and A_qk with the reference's clamped decays (naive.py:335-344, 377-378).
+  for (int e = tid; e < kC * kC; e += nth) {
+    const int i = e / kC, j = e % kC;
+    float aq = 0.f, ak = 0.f;
+    if (j <= i) {
+      for (int d = 0; d < K; ++d) {
+        const float kd = Ks[j * KP + d] * expf(fminf(Gs[i * KP + d] - Gs[j * KP + d], 0.f));
+        aq = fmaf(Qs[i * KP + d], kd, aq);
+        ak = fmaf(Bs[i * KP + d] * Ks[i * KP + d], kd, ak);
+      }
+    }
+    As[i * 65 + j] = aq;
+    Ts[i * 65 + j] = j < i ? ak : 0.f;
+  }
+  __syncthreads();
+  // dmix_0 = sum_v dO r_0, r_0 = A_qk v_new + (q~ e^G) S0 (naive.py:377-390)
+  // (r_0 goes through the dR_U scratch, free until the solve below, and is
+  // reduced row by row in a fixed order.)
+  block_gemm(kC, V, kC + K,
+             [&](int i, int j) {
+               return j < kC ? As[i * 65 + j] : Qs[i * KP + j - kC] * expf(Gs[i * KP + j - kC]);
+             },
+             [&](int j, int c) { return j < kC ? vn[j * V + c] : S0[(j - kC) * V + c]; }, gsm,
+             [&](int i, int c, float a) { dRU[i * V + c] = a * dO(i, c); });
+  for (int i = tid; i < kC; i += nth) {
+    float s = 0.f;
+    for (int c = 0; c < V; ++c) s += dRU[i * V + c];
+    if (t0 + i < f.T) p.dmix[(int64_t(b) * f.T + t0 + i) * f.H * f.L + h * f.L] = s;
+  }
+  __syncthreads();
+  // dA_qk = (mix_0 dO) v_new^T on the causal triangle; d(q~ e^G) = (mix_0 dO) S0^T
+  block_gemm(kC, kC + K, V, [&](int i, int c) { return mx[i] * dO(i, c); },
+             [&](int c, int j) { return j < kC ? vn[j * V + c] : S0[(j - kC) * V + c]; }, gsm,
+             [&](int i, int j, float a) {
+               if (j < kC) As[i * 65 + j] = j <= i ? a : 0.f;
+               else dQG[i * K + j - kC] = a;
+             });
+  // dKt = v_new dS'^T; dW = -dv_new S0^T (the [W] half of dY); dU = dv_new
+  block_gemm(kC, K, V, [&](int i, int c) { return vn[i * V + c]; },
+             [&](int c, int k) { return dSn[k * V + c]; }, gsm,
+             [&](int i, int k, float a) { dKt[i * K + k] = a; });
+  block_gemm(kC, K, V, [&](int i, int c) { return dvn[i * V + c]; },
+             [&](int c, int k) { return S0[k * V + c]; }, gsm,
+             [&](int i, int k, float a) { dRW[i * K + k] = -a; });
+  for (int e = tid; e < kC * V; e += nth) dRU[e] = dvn[e];
+  // dG_last from S' = e^(G_last) S0: sum_v S0 dS' e^(G_last)
+  for (int k = tid; k < K; k += nth) {
+    float s = 0.f;
+    for (int c = 0; c < V; ++c) s = fmaf(S0[k * V + c], dSn[k * V + c], s);
+    dGl[k] = s * expf(Gs[(kC - 1) * KP + k]);
+  }
+  __syncthreads();
+  // dR = (I + T)^-T dY: back substitution, one column of [dU | dW] per thread.
+  for (int c = tid; c < V + K; c += nth) {
+    float* col = c < V ? dRU + c : dRW + (c - V);
+    const int ld = c < V ? V : K;
+    float x[kC];
+#pragma unroll
+    for (int i = kC - 1; i >= 0; --i) {
+      float r = col[i * ld];
+#pragma unroll
+      for (int j = i + 1; j < kC; ++j) r = fmaf(-Ts[j * 65 + i], x[j], r);
+      x[i] = r;
+    }
+#pragma unroll
+    for (int i = 0; i < kC; ++i) col[i * ld] = x[i];
+  }
+  __syncthreads();
+  // dT = -dR [U | W]^T on the strict lower triangle
+  block_gemm(kC, kC, V + K,
+             [&](int i, int c) { return c < V ? dRU[i * V + c] : dRW[i * K + c - V]; },
+             [&](int c, int j) { return c < V ? Um[j * V + c] : Wm[j * K + c - V]; }, gsm,
+             [&](int i, int j, float a) { Dt[i * 65 + j] = j < i ? -a : 0.f; });
+  // dv = dR_U w, dw = dR_U v (R_V = w * v, naive.py:346)
+  for (int e = tid; e < kC * V; e += nth) {
+    const int i = e / V, c = e % V, t = t0 + i;
+    if (t < f.T) {
+      const float d = dRU[e];
+      p.dv[orow(i, V) + c] = d * f.w.at(b, t, h, c);
+      p.dw[orow(i, V) + c] = d * f.v.at(b, t, h, c);
+    }
+  }
+  // Column pass over the decayed blocks: for key j, sums over the rows i.
+  for (int e = tid; e < kC * K; e += nth) {
+    const int j = e / K, d = e % K;
+    const float gj = Gs[j * KP + d];
+    float acc = 0.f, accg = 0.f;
+    for (int i = j; i < kC; ++i) {
+      const float x = Gs[i * KP + d] - gj;
+      const float ex = expf(fminf(x, 0.f));
+      const float term = (i > j ? Dt[i * 65 + j] * Bs[i * KP + d] * Ks[i * KP + d] : 0.f) +
+                         As[i * 65 + j] * Qs[i * KP + d];
+      acc = fmaf(term, ex, acc);
+      if (x <= 0.f) accg = fmaf(term, ex, accg);
+    }
+    dKTA[j * K + d] = acc;
+    dGs[j * KP + d] = -Ks[j * KP + d] * accg;
+  }
+  __syncthreads();
+  // Row pass and assembly of every gradient of the token row.
+  for (int e = tid; e < kC * K; e += nth) {
+    const int i = e / K, d = e % K, t = t0 + i;
+    const float gi = Gs[i * KP + d];
+    float dbk = 0.f, dqs = 0.f, gbk = 0.f, gqs = 0.f;
+    for (int j = 0; j <= i; ++j) {
+      const float x = gi - Gs[j * KP + d];
+      const float kx = Ks[j * KP + d] * expf(fminf(x, 0.f));
+      const float tt = j < i ? Dt[i * 65 + j] : 0.f, aa = As[i * 65 + j];
+      dbk = fmaf(tt, kx, dbk);
+      dqs = fmaf(aa, kx, dqs);
+      if (x <= 0.f) {
+        gbk = fmaf(tt, kx, gbk);
+        gqs = fmaf(aa, kx, gqs);
+      }
+    }
+    const float q = Qs[i * KP + d], k = Ks[i * KP + d], bb = Bs[i * KP + d];
+    const float eG = expf(gi), eT = expf(Gs[(kC - 1) * KP + d] - gi);
+    const float rw = dRW[i * K + d], qg = dQG[i * K + d], kt = dKt[i * K + d];
+    float dG = dGs[i * KP + d] + bb * k * gbk + q * gqs + rw * k * bb * eG + qg * q * eG -
+               kt * k * eT;
+    dGs[i * KP + d] = dG;
+    if (t < f.T) {
+      p.dq[(int64_t(b) * f.T + t) * f.H * f.L * K + (int64_t(h) * f.L) * K + d] =
+          f.scale * (dqs + qg * eG);
+      p.db[orow(i, K) + d] = rw * k * eG + dbk * k;
+      p.dk[orow(i, K) + d] = rw * bb * eG + dbk * bb + kt * eT + dKTA[i * K + d];
+    }
+  }
+  __syncthreads();
+  // g: dG_last (with the Kt part, sum_i dKt k e^(G_last - G)) joins the last
+  // row, then reverse cumsum (G = cumsum g).
+  if (tid < K) {
+    float acc = dGl[tid];
+    const float gl = Gs[(kC - 1) * KP + tid];
+    for (int i = 0; i < kC; ++i)
+      acc += dKt[i * K + tid] * Ks[i * KP + tid] * expf(gl - Gs[i * KP + tid]);
+    for (int i = kC - 1; i >= 0; --i) {
+      acc += dGs[i * KP + tid];
+      if (t0 + i < f.T) p.dg[orow(i, K) + tid] = acc;
+    }
+  }
+  // Upper-level reads (naive.py:382-385): dq_l = mix_l scale dO S_l^T,
+  // dmix_l = scale sum_v dO (q_l S_l), S_l the state entering the chunk.
+  for (int l = 1; l < f.L; ++l) {
+    const float* Sl = ck_level(f, bh, l, n / f.firing[l]);
+    __syncthreads();
+    for (int i = tid; i < kC; i += nth) mx[i] = t0 + i < f.T ? f.mix.at(b, t0 + i, h, l) : 0.f;
+    __syncthreads();
+    block_gemm(kC, K, V, [&](int i, int c) { return dO(i, c); },
+               [&](int c, int k) { return Sl[k * V + c]; }, gsm,
+               [&](int i, int k, float a) {
+                 if (t0 + i < f.T)
+                   p.dq[(int64_t(b) * f.T + t0 + i) * f.H * f.L * K + (int64_t(h) * f.L + l) * K + k] =
+                       f.scale * mx[i] * a;
+               });
+    block_gemm(kC, V, K,
+               [&](int i, int k) { return t0 + i < f.T ? f.q.at(b, t0 + i, h, l, k) : 0.f; },
+               [&](int k, int c) { return Sl[k * V + c]; }, gsm,
+               [&](int i, int c, float a) { dRU[i * V + c] = a * dO(i, c); });
+    for (int i = tid; i < kC; i += nth) {
+      float s2 = 0.f;
+      for (int c = 0; c < V; ++c) s2 += dRU[i * V + c];
+      if (t0 + i < f.T) p.dmix[(int64_t(b) * f.T + t0 + i) * f.H * f.L + h * f.L + l] = f.scale * s2;
+    }
+  }
+}
+
+}  // namespace ngdn2
+
+namespace ngdn2 {
+
+cudaError_t launch_fwd_simt(const FwdParams& p, int stage, cudaStream_t stream);
+
+// Workspace of the backward, in floats, region by region.
+struct BwdLayout {
+  int64_t params32, chunks, scan, fin, ck0, ck_up, ck_vnew, dparams, dS, dsn, dvn, pscr, lscr,
+      size;
+  int64_t ck_up_off[NGDN2_MAX_LEVELS];
+  int ck_up_n[NGDN2_MAX_LEVELS];
+};
+
+BwdLayout bwd_layout(const FwdParams& f, const PromoBwdScratch& ps, const LocalScratch& ls) {
+  BwdLayout w;
+  const int64_t bh = int64_t(f.B) * f.H, kv = int64_t(f.K) * f.V, cv = int64_t(kC) * f.V;
+  int64_t o = 0;
+  auto take = [&](int64_t n) { const int64_t at = o; o = align_floats(o + n); return at; };
+  w.params32 = take(f.pl.size);
+  w.chunks = take(bh * f.NT * f.rec.size);
+  w.scan = take(bh * f.ss.size);
+  w.fin = take(bh * f.L * kv);
+  w.ck0 = take(bh * (f.NT + 1) * kv);
+  int64_t up = 0;
+  for (int l = 0; l < NGDN2_MAX_LEVELS; ++l) {
+    w.ck_up_off[l] = up;
+    w.ck_up_n[l] = 0;
+    if (l >= 1 && l < f.L) {
+      w.ck_up_n[l] = (f.NT + f.firing[l] - 1) / f.firing[l] + 1;
+      up = align_floats(up + bh * w.ck_up_n[l] * kv);
+    }
+  }
+  w.ck_up = take(up);
+  w.ck_vnew = take(bh * f.NT * cv);
+  w.dparams = take(int64_t(f.B) * f.pl.size);
+  w.dS = take(bh * f.L * kv);
+  w.dsn = take(bh * f.NT * kv);
+  w.dvn = take(bh * f.NT * cv);
+  w.pscr = take(bh * ps.size);
+  w.lscr = take(bh * f.NT * ls.size);
+  w.size = o;
+  return w;
+}
+
+int64_t bwd_workspace_floats(const FwdParams& f) {
+  return bwd_layout(f, PromoBwdScratch::make(f.K, f.V, f.NP), LocalScratch::make(f.K, f.V)).size;
+}
+
+int num_launches_bwd(const FwdParams& f) {
+  return (f.L > 1 ? 2 : 0) + (f.NT > 0 ? 1 : 0) + 1 + 1 + (f.NT > 0 ? 1 : 0);
+}
+
+// x[i] = sum over rows r < R of x[r * n + i], in row order.
+__global__ void reduce_rows_kernel(float* x, int64_t n, int R) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    float s = x[i];
+    for (int r = 1; r < R; ++r) s += x[r * n + i];
+    x[i] = s;
+  }
+}
+
+// The forward's SIMT prep and checkpointing scan, then the two backward
+// kernels. `bp` carries the caller's pointers; the workspace regions are
+// filled in here.
+cudaError_t launch_bwd(BwdParams bp, float* ws, float* const dparam_out[5], cudaStream_t stream) {
+  FwdParams& f = bp.f;
+  bp.ps = PromoBwdScratch::make(f.K, f.V, f.NP);
+  bp.ls = LocalScratch::make(f.K, f.V);
+  const BwdLayout w = bwd_layout(f, bp.ps, bp.ls);
+  f.params32 = ws + w.params32;
+  f.chunks = ws + w.chunks;
+  f.scan = ws + w.scan;
+  f.fin = ws + w.fin;
+  f.o = nullptr;
+  f.ck0 = ws + w.ck0;
+  f.ck_up = ws + w.ck_up;
+  for (int l = 0; l < NGDN2_MAX_LEVELS; ++l) {
+    f.ck_up_off[l] = w.ck_up_off[l];
+    f.ck_up_n[l] = w.ck_up_n[l];
+  }
+  f.ck_vnew = ws + w.ck_vnew;
+  bp.dparams = f.L > 1 ? ws + w.dparams : nullptr;
+  bp.dS = ws + w.dS;
+  bp.dsn = ws + w.dsn;
+  bp.dvn = ws + w.dvn;
+  bp.pscr = ws + w.pscr;
+  bp.lscr = ws + w.lscr;
+  cudaError_t err = launch_fwd_simt(f, 0, stream);
+  if (err != cudaSuccess) return err;
+  if (bp.dparams) {
+    err = cudaMemsetAsync(bp.dparams, 0, sizeof(float) * f.B * f.pl.size, stream);
+    if (err != cudaSuccess) return err;
+  }
+  bwd_scan_kernel<<<dim3(f.H, f.B), 256, 0, stream>>>(bp);
+  if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  if (f.NT > 0) {
+    const size_t smem = bwd_local_smem(f.K);
+    err = cudaFuncSetAttribute(bwd_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               int(smem));
+    if (err != cudaSuccess) return err;
+    bwd_local_kernel<<<dim3(f.NT, f.H, f.B), 256, smem, stream>>>(bp);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  }
+  if (bp.dparams) {
+    reduce_rows_kernel<<<256, 256, 0, stream>>>(bp.dparams, f.pl.size, f.B);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    const int64_t n = int64_t(f.L - 1) * f.H;
+    const int64_t counts[5] = {n * f.n_max * f.K, n * f.K * f.V, n * f.V * f.K, n * f.V * f.V,
+                               n * f.V * f.K};
+    const int64_t offs[5] = {f.pl.qb, f.pl.kp, f.pl.bp, f.pl.wp, f.pl.gp};
+    for (int a = 0; a < 5; ++a) {
+      if (!dparam_out[a]) continue;
+      err = cudaMemcpyAsync(dparam_out[a], bp.dparams + offs[a], sizeof(float) * counts[a],
+                            cudaMemcpyDeviceToDevice, stream);
+      if (err != cudaSuccess) return err;
+    }
+  }
+  return cudaSuccess;
+}
+
+}  // namespace ngdn2
+
+namespace ngdn2 {
+
+cudaError_t launch_bwd_abi(const ngdn2_bwd_args* a, const FwdParams& f, cudaStream_t stream) {
+  BwdParams bp;
+  memset(&bp, 0, sizeof(bp));
+  bp.f = f;
+  bp.d_o = a->d_o;
+  bp.d_o_dtype = a->d_o_dtype;
+  for (int i = 0; i < 4; ++i) bp.dos[i] = a->d_o_stride[i];
+  bp.d_final = a->d_final;
+  bp.dq = a->dq;
+  bp.dk = a->dk;
+  bp.dv = a->dv;
+  bp.dg = a->dg;
+  bp.db = a->db;
+  bp.dw = a->dw;
+  bp.dmix = a->dmix;
+  bp.dinit = a->dinitial_state;
+  float* const outs[5] = {a->dquery_banks, a->dkey_projections, a->db_projections,
+                          a->dw_projections, a->dg_projections};
+  return launch_bwd(bp, reinterpret_cast<float*>(a->workspace), outs, stream);
+}
+
+}  // namespace ngdn2

@@ -112,6 +112,16 @@ struct FwdParams {
   ChunkRecord rec;
   float* scan;
   ScanScratch ss;
+  // Checkpoints for the backward (null in a plain forward): the level-0
+  // state entering every chunk plus the final one, [B, H, NT + 1, K, V];
+  // each upper level's state entering every group plus the final one,
+  // [B, H, NG_l + 1, K, V] at ck_up + ck_up_off[l]; and v_new of every chunk,
+  // [B, H, NT, 64, V]. With these set the scan writes no output o.
+  float* ck0;
+  float* ck_up;
+  int64_t ck_up_off[NGDN2_MAX_LEVELS];
+  int ck_up_n[NGDN2_MAX_LEVELS];  // NG_l + 1
+  float* ck_vnew;
 };
 
 // Arguments of the update-scan kernel (update_fwd.py:131-204).

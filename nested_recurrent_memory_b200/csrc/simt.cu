@@ -175,8 +175,22 @@ __global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
   __syncthreads();
   float* Vn = sc + p.ss.vn;
   float* Ot = sc + p.ss.ot;
+  const bool ckpt = p.ck0 != nullptr;
+  // Backward checkpoints: a copy of the state of `level` into slot `j`.
+  auto save = [&](int level, int j) {
+    const float* src = S + int64_t(level) * K * V;
+    float* dst = level == 0 ? p.ck0 + (bh * (p.NT + 1) + j) * K * V
+                            : p.ck_up + p.ck_up_off[level] + (bh * p.ck_up_n[level] + j) * K * V;
+    for (int e = tid; e < K * V; e += blockDim.x) dst[e] = src[e];
+  };
   for (int n = 0; n < p.NT; ++n) {
     const float* rec = p.chunks + (bh * p.NT + n) * p.rec.size;
+    if (ckpt) {
+      save(0, n);
+      for (int l = 1; l < L; ++l)
+        if (n % p.firing[l] == 0) save(l, n / p.firing[l]);
+      __syncthreads();
+    }
     const float* Wm = rec + p.rec.W;
     const float* Um = rec + p.rec.U;
     const float* Am = rec + p.rec.A;
@@ -186,9 +200,13 @@ __global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
     // v_new = U - W S0 (naive.py:376)
     block_gemm(kC, V, K, [&](int i, int k) { return Wm[i * K + k]; },
                [&](int k, int c) { return S[k * V + c]; }, gsm,
-               [&](int i, int c, float a) { Vn[i * V + c] = Um[i * V + c] - a; });
+               [&](int i, int c, float a) {
+                 Vn[i * V + c] = Um[i * V + c] - a;
+                 if (ckpt) p.ck_vnew[(bh * p.NT + n) * kC * V + i * V + c] = Um[i * V + c] - a;
+               });
     // o = sum_l (mix_l scale q_l [e^G at l=0]) S_l + mix_0 scale A_qk v_new
-    for (int l = 0; l < L; ++l) {
+    // (not formed when only the backward's checkpoints are wanted)
+    for (int l = 0; l < L && p.o; ++l) {
       const float* Ql = Qm + int64_t(l) * kC * K;
       const float* Sl = S + int64_t(l) * K * V;
       block_gemm(kC, V, K, [&](int i, int k) { return Ql[i * K + k]; },
@@ -197,10 +215,11 @@ __global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
                    if (l == 0) Ot[i * V + c] = a; else Ot[i * V + c] += a;
                  });
     }
-    block_gemm(kC, V, kC, [&](int i, int j) { return Am[i * kC + j]; },
-               [&](int j, int c) { return Vn[j * V + c]; }, gsm,
-               [&](int i, int c, float a) { Ot[i * V + c] += a; });
-    for (int e = tid; e < kC * V; e += blockDim.x) {
+    if (p.o)
+      block_gemm(kC, V, kC, [&](int i, int j) { return Am[i * kC + j]; },
+                 [&](int j, int c) { return Vn[j * V + c]; }, gsm,
+                 [&](int i, int c, float a) { Ot[i * V + c] += a; });
+    for (int e = tid; e < kC * V && p.o; e += blockDim.x) {
       const int i = e / V, c = e % V, t = n * kC + i;
       if (t < p.T) store_elem(p.o, ((int64_t(b) * p.T + t) * p.H + h) * V + c, Ot[e], p.dtype);
     }
@@ -211,6 +230,11 @@ __global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
     // Levels whose firing this chunk completes, bottom-up (naive.py:394-415).
     for (int l = 1; l < L; ++l)
       if ((n + 1) % p.firing[l] == 0) promote_simt(p, b, h, l, S, sc, gsm);
+  }
+  if (ckpt) {
+    __syncthreads();
+    save(0, p.NT);
+    for (int l = 1; l < L; ++l) save(l, p.ck_up_n[l] - 1);
   }
 }
 

@@ -28,6 +28,7 @@ from . import _lib
 __all__ = [
     "chunk_nested_gdn2",
     "chunk_nested_gdn2_fwd",
+    "chunk_nested_gdn2_bwd",
     "update_state",
     "step_nested_gdn2",
     "n_groups",
@@ -232,8 +233,8 @@ def chunk_nested_gdn2_fwd(
     [B, H, L, K, V] or None. Returns ``(o, final_state)`` with o in q's dtype
     and final_state fp32 (None unless ``output_final_state``); with
     ``return_aux`` also a dict, which here holds only ``scale`` and the
-    per-level ``finals`` -- this forward-only build keeps no backward
-    intermediates.
+    per-level ``finals``: the backward (chunk_nested_gdn2_bwd) recomputes
+    its intermediates instead of keeping the reference's aux tensors.
 
     Keyword-only extras: ``path`` ("auto", "simt" or "tc") picks the kernel
     family; ``workspace`` is an optional preallocated uint8 CUDA tensor.
@@ -251,8 +252,87 @@ def chunk_nested_gdn2_fwd(
     return o, final_state, aux
 
 
+def chunk_nested_gdn2_bwd(q, k, v, g, b, w, mix_weights, query_banks, key_projections,
+                          b_projections, w_projections, g_projections, n_queries_per_level,
+                          firing_intervals, L, do, d_final=None, scale=None, initial_state=None,
+                          chunk_size=64, promotion="learned", workspace=None):
+    """Gradients of ``sum(o * do) + sum(final_state * d_final)`` with respect
+    to every differentiable input (the job of chunk.py:368-564 behind
+    ChunkNestedGDN2Function.backward, chunk.py:650-719).
+
+    Runs ``ngdn2_bwd``: a checkpointing re-run of the forward on CUDA cores,
+    then the reverse scan and the per-chunk gradients, all fp32. Returns
+    ``(dq, dk, dv, dg, db, dw, dmix, dquery_banks, dkey_projections,
+    db_projections, dw_projections, dg_projections, dinitial_state)`` in the
+    dtypes of the corresponding inputs (``dinitial_state`` is None without an
+    initial state).
+    """
+    B, T, H, _, K = q.shape
+    V = v.shape[-1]
+    if chunk_size != 64:  # chunk.py:230-231
+        raise ValueError(f"chunk_size must be 64 for GDN-2, got {chunk_size}")
+    if promotion not in _lib.PROMOTION:
+        raise KeyError(promotion)
+    if scale is None:
+        scale = K ** -0.5
+    _require_cuda(q, k, v, g, b, w, mix_weights, do, initial_state, d_final)
+    firing = [int(x) for x in firing_intervals]
+    nq = [int(x) for x in n_queries_per_level]
+    dev = q.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    dq = torch.zeros(B, T, H, L, K, **f32)
+    dk, dg, db = (torch.zeros(B, T, H, K, **f32) for _ in range(3))
+    dv, dw = (torch.zeros(B, T, H, V, **f32) for _ in range(2))
+    dmix = torch.zeros(B, T, H, L, **f32)
+    raw = (query_banks, key_projections, b_projections, w_projections, g_projections)
+    dparams = [torch.zeros(t.shape, **f32) for t in raw]
+    dinit = torch.zeros(B, H, L, K, V, **f32) if initial_state is not None else None
+    if T > 0:
+        params, n_max = [], 1
+        if L > 1:
+            params = [t.to(dev, query_banks.dtype).contiguous() for t in raw]
+            n_max = query_banks.shape[2]
+        init = (initial_state.to(torch.float32).contiguous()
+                if initial_state is not None else None)
+        # The forward's o and final_state are not used by the backward; do
+        # stands in for o so the argument struct validates.
+        fa = _build_fwd_args(q, k, v, g, b, w, mix_weights, params, n_max, nq, firing, L,
+                             scale, init, do, dq, chunk_size, promotion, "simt")
+        a = _lib.BwdArgs()
+        a.abi_version = _lib.ABI_VERSION
+        a.fwd = fa
+        _fill_tok(a, "d_o", do, 4)
+        dfin = d_final.to(torch.float32).contiguous() if d_final is not None else None
+        a.d_final = dfin.data_ptr() if dfin is not None else None
+        a.dq, a.dk, a.dv, a.dg = dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr()
+        a.db, a.dw, a.dmix = db.data_ptr(), dw.data_ptr(), dmix.data_ptr()
+        if L > 1:
+            (a.dquery_banks, a.dkey_projections, a.db_projections, a.dw_projections,
+             a.dg_projections) = (t.data_ptr() for t in dparams)
+        a.dinitial_state = dinit.data_ptr() if dinit is not None else None
+        lib = _lib.load()
+        nbytes = ctypes.c_size_t(0)
+        rc = lib.ngdn2_bwd_workspace_size(ctypes.byref(a), ctypes.byref(nbytes))
+        _raise_for(rc, "ngdn2_bwd_workspace_size", chunk_size=chunk_size)
+        if workspace is None or workspace.numel() < nbytes.value:
+            workspace = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=dev)
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.ngdn2_bwd(ctypes.byref(a), ctypes.c_void_p(stream))
+        _raise_for(rc, "ngdn2_bwd", chunk_size=chunk_size)
+    elif dinit is not None and d_final is not None:
+        dinit.copy_(d_final)
+    out = [dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg.to(g.dtype), db.to(b.dtype),
+           dw.to(w.dtype), dmix.to(mix_weights.dtype)]
+    out += [d.to(t.dtype) for d, t in zip(dparams, raw)]
+    out.append(dinit.to(initial_state.dtype) if dinit is not None else None)
+    return tuple(out)
+
+
 class ChunkNestedGDN2Function(torch.autograd.Function):
-    """Autograd node for the whole op (chunk.py:567-719), forward only."""
+    """Autograd node for the whole op (chunk.py:567-719). The forward runs the
+    fast path and keeps only its inputs; the backward recomputes what it needs
+    (chunk_nested_gdn2_bwd)."""
 
     @staticmethod
     def forward(ctx, q, k, v, g, b, w, mix_weights, query_banks, key_projections,
@@ -264,13 +344,23 @@ class ChunkNestedGDN2Function(torch.autograd.Function):
             w_projections, g_projections, n_queries_per_level, firing_intervals, L,
             scale=scale, initial_state=initial_state, output_final_state=True,
             chunk_size=chunk_size, promotion=promotion)
+        ctx.save_for_backward(q, k, v, g, b, w, mix_weights, query_banks, key_projections,
+                              b_projections, w_projections, g_projections, initial_state)
+        ctx.meta = ([int(x) for x in n_queries_per_level], [int(x) for x in firing_intervals],
+                    L, scale, chunk_size, promotion)
         return o, (final_state if output_final_state else None)
 
     @staticmethod
     def backward(ctx, do, dfinal):
-        raise NotImplementedError(
-            "nested_recurrent_memory_b200 implements the forward hot path only; "
-            "the chunkwise backward (reference chunk.py:307-564) is not built")
+        (q, k, v, g, b, w, mix, qb, kp, bp, wp, gp, init) = ctx.saved_tensors
+        nq, firing, L, scale, chunk_size, promotion = ctx.meta
+        if do is None:
+            do = torch.zeros(*q.shape[:3], v.shape[-1], dtype=q.dtype, device=q.device)
+        grads = chunk_nested_gdn2_bwd(
+            q, k, v, g, b, w, mix, qb, kp, bp, wp, gp, nq, firing, L, do.contiguous(),
+            d_final=dfinal, scale=scale, initial_state=init, chunk_size=chunk_size,
+            promotion=promotion)
+        return (*grads[:12], None, None, None, None, grads[12], None, None, None)
 
 
 def chunk_nested_gdn2(q, k, v, g, b, w, mix_weights, query_banks, key_projections,

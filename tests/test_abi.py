@@ -96,6 +96,47 @@ def test_fwd_rejects_missing_workspace(lib):
     assert lib.ngdn2_fwd(ctypes.byref(a), None) == -10
 
 
+def _fake_bwd(**over):
+    a = _lib.BwdArgs()
+    a.abi_version = _lib.ABI_VERSION
+    fa = _fake_fwd(**{k: v for k, v in over.items() if k in _lib.FwdArgs.__dict__})
+    fa.o = None
+    fa.final_state = None   # not used by the backward
+    a.fwd = fa
+    for name in ("d_o", "dq", "dk", "dv", "dg", "db", "dw", "dmix"):
+        setattr(a, name, 0x1000)
+    for k, v in over.items():
+        if k not in _lib.FwdArgs.__dict__:
+            setattr(a, k, v)
+    return a
+
+
+def test_bwd_workspace_size_is_positive(lib):
+    n = ctypes.c_size_t(0)
+    assert lib.ngdn2_bwd_workspace_size(ctypes.byref(_fake_bwd()), ctypes.byref(n)) == 0
+    assert n.value > 0
+    assert lib.ngdn2_bwd_num_launches(ctypes.byref(_fake_bwd())) == 6
+
+
+@pytest.mark.parametrize(("over", "code"), [
+    (dict(chunk_size=32), _lib.ERR_CHUNK_SIZE),
+    (dict(n_queries=(24, 16)), _lib.ERR_N_POW2),
+    (dict(d_o=None), -9),
+    (dict(dmix=None), -9),
+    (dict(d_o_dtype=5), -8),
+    (dict(abi_version=99), -13),
+])
+def test_bwd_validation_codes(lib, over, code):
+    n = ctypes.c_size_t(0)
+    a = _fake_bwd(**over)
+    assert lib.ngdn2_bwd_workspace_size(ctypes.byref(a), ctypes.byref(n)) == code
+    assert lib.ngdn2_bwd(ctypes.byref(a), None) == code
+
+
+def test_bwd_rejects_missing_workspace(lib):
+    assert lib.ngdn2_bwd(ctypes.byref(_fake_bwd()), None) == -10
+
+
 def _fake_update(**over):
     u = _lib.UpdateArgs()
     u.abi_version = _lib.ABI_VERSION
