@@ -56,6 +56,8 @@ def parse_args():
     ap.add_argument("--model", action="store_true",
                     help="time the full-model forward harness (BASELINE config 4: 12-layer "
                          "NestedGDN-2 LM, B=32 sharded over the GPUs, T=4096); prints its own line")
+    ap.add_argument("--backward", action="store_true",
+                    help="time the op's forward plus backward (one GPU)")
     ap.add_argument("--decode", action="store_true",
                     help="time the one-token decode step (step_nested_gdn2) on the config's "
                          "B, H, K, V, L instead of the chunked forward; prints its own line")
@@ -466,6 +468,58 @@ def run_decode(args, w):
     }), flush=True)
 
 
+def run_backward(args, w):
+    """One step = the op's forward (fast path) plus its backward
+    (chunk_nested_gdn2_bwd: checkpointed CUDA-core forward re-run, reverse
+    scan, per-chunk gradients) on resident inputs with a resident upstream
+    gradient d_o. Single GPU; tokens/s = B * T / step time. The backward's
+    share is timed separately with events around the bwd call."""
+    import torch
+
+    from nested_recurrent_memory_b200 import FwdCall, chunk_nested_gdn2_bwd
+    from nested_recurrent_memory_b200.synthetic import config_inputs
+
+    dev = torch.device("cuda", 0)
+    inp = config_inputs(w["B"], w["T"], w["H"], w["K"], w["V"], w["L"], w["m"], w["firing"],
+                        dtype=w["dtype"], device=dev, gen_device=dev)
+    L = inp.pop("L")
+    call = FwdCall(**inp, L=L, path=args.path)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    d_o = torch.randn(w["B"], w["T"], w["H"], w["V"], generator=gen, device=dev).to(w["dtype"])
+
+    def bwd():
+        return chunk_nested_gdn2_bwd(**inp, L=L, do=d_o)
+
+    for _ in range(args.warmup):
+        call.launch()
+        bwd()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    t_f = t_b = 0.0
+    for _ in range(args.steps):
+        ev[0].record()
+        call.launch()
+        ev[1].record()
+        bwd()
+        ev[2].record()
+        torch.cuda.synchronize()
+        t_f += ev[0].elapsed_time(ev[1])
+        t_b += ev[1].elapsed_time(ev[2])
+    ms_f, ms_b = t_f / args.steps, t_b / args.steps
+    ms = ms_f + ms_b
+    tokens = w["B"] * w["T"]
+    print(json.dumps({
+        "metric": "nested-GDN layer fwd+bwd tokens/s (the op's training step)",
+        "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": str(w["dtype"]).replace("torch.", ""), "data": "synthetic",
+        "config": {"workload": f"{args.config}: B={w['B']}, T={w['T']}, H={w['H']}, "
+                               f"K=V={w['K']}, L={w['L']}, firing {'/'.join(map(str, w['firing']))}, "
+                               f"m={w['m']}; forward path {call.path}, backward fp32 CUDA cores"},
+        "fwd_ms": ms_f, "bwd_ms": ms_b,
+    }), flush=True)
+
+
 def run_model(args):
     """random-init 12-layer NestedGDN-2 LM forward in bf16,
     batch-sharded (32 sequences over the ranks), T=4096, token ids uniform
@@ -539,6 +593,8 @@ def main():
         w["B"] = args.batch
     if args.decode:
         run_decode(args, w)
+    elif args.backward:
+        run_backward(args, w)
     elif args.impl == "reference":
         run_reference(args, w)
     else:

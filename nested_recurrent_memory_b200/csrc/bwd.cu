@@ -61,7 +61,7 @@ struct PromoBwdScratch {
 
 // Per-chunk scratch of the local pass, fp32, offsets in floats.
 struct LocalScratch {
-  int64_t dqg, dkt, drw, dru, dkta, size;
+  int64_t dqg, dkt, drw, dru, dkta, dgc, size;
   __host__ __device__ static LocalScratch make(int K, int V) {
     LocalScratch s;
     s.dqg = 0;                                  // [64, K] d(q~ e^G), mix_0 folded
@@ -69,7 +69,8 @@ struct LocalScratch {
     s.drw = align_floats(s.dkt + kC * K);       // [64, K] dW, then dR_W
     s.dru = align_floats(s.drw + kC * K);       // [64, V] dU, then dR_U
     s.dkta = align_floats(s.dru + kC * V);      // [64, K] dk from the decayed blocks
-    s.size = align_floats(s.dkta + kC * K);
+    s.dgc = align_floats(s.dkta + kC * K);      // [64, K] dG, column part then whole
+    s.size = align_floats(s.dgc + kC * K);
     return s;
   }
 };
@@ -158,7 +159,7 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
                [&](int k, int c) { return X[k * V + c]; }, gsm,
                [&](int r, int c, float a) { Vp[r * V + c] = a; });
     vals = Vp;
-    block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+    block_gemm<false, true>(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
                [&](int v, int k) { return kp[k * V + v]; }, gsm,
                [&](int r, int k, float a) { Kk[r * K + k] = a; });
     for (int r = warp; r < m; r += nwarp) {
@@ -199,14 +200,14 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
                [&](int k, int c) { return Sd[k * V + c]; }, gsm,
                [&](int r, int c, float a) { Y[r * V + c] = a; });
     // dK = (V' * w - Y) dS'^T;  d(K*b) = -Z S_d^T
-    block_gemm(m, K, V, [&](int r, int c) { return vals[r * V + c] * Wg[r * V + c] - Y[r * V + c]; },
+    block_gemm<false, true>(m, K, V, [&](int r, int c) { return vals[r * V + c] * Wg[r * V + c] - Y[r * V + c]; },
                [&](int c, int k) { return dSl[k * V + c]; }, gsm,
                [&](int r, int k, float a) { dKk[r * K + k] = a; });
-    block_gemm(m, K, V, [&](int r, int c) { return Z[r * V + c]; },
+    block_gemm<false, true>(m, K, V, [&](int r, int c) { return Z[r * V + c]; },
                [&](int c, int k) { return Sd[k * V + c]; }, gsm,
                [&](int r, int k, float a) { dKB[r * K + k] = -a; });
     // dS_d = dS' - (K*b)^T Z
-    block_gemm(K, V, m, [&](int k, int r) { return Kk[r * K + k] * Bg[r * K + k]; },
+    block_gemm<true, false>(K, V, m, [&](int k, int r) { return Kk[r * K + k] * Bg[r * K + k]; },
                [&](int r, int c) { return Z[r * V + c]; }, gsm,
                [&](int k, int c, float a) { dSd[k * V + c] = dSl[k * V + c] - a; });
   } else {
@@ -259,7 +260,7 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
   }
   __syncthreads();
   // dV' += d(g logit) W_g^T + d(w logit) W_w^T + d(b logit) W_b^T
-  block_gemm(m, V, 2 * K + V,
+  block_gemm<false, true>(m, V, 2 * K + V,
              [&](int r, int j) {
                return j < K ? Zg[r * K + j] : j < 2 * K ? Bg[r * K + j - K] : Wg[r * V + j - 2 * K];
              },
@@ -268,7 +269,7 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
              },
              gsm, [&](int r, int v, float a) { dVp[r * V + v] += a; });
   // parameter gradients of the gates: V'^T d(logit)
-  block_gemm(V, 2 * K + V, m, [&](int v, int r) { return vals[r * V + v]; },
+  block_gemm<true, false>(V, 2 * K + V, m, [&](int v, int r) { return vals[r * V + v]; },
              [&](int r, int j) {
                return j < K ? Zg[r * K + j] : j < 2 * K ? Bg[r * K + j - K] : Wg[r * V + j - 2 * K];
              },
@@ -299,14 +300,14 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
   block_gemm(m, V, K, [&](int r, int k) { return dKk[r * K + k]; },
              [&](int k, int v) { return kp[k * V + v]; }, gsm,
              [&](int r, int v, float a) { dVp[r * V + v] += a; });
-  block_gemm(K, V, m, [&](int k, int r) { return dKk[r * K + k]; },
+  block_gemm<true, false>(K, V, m, [&](int k, int r) { return dKk[r * K + k]; },
              [&](int r, int v) { return vals[r * V + v]; }, gsm,
              [&](int k, int v, float a) { dkp[k * V + v] += a; });
   // V' = Q_bank X: dQ_bank += dV' X^T; dX = Q_bank^T dV'
-  block_gemm(m, K, V, [&](int r, int v) { return dVp[r * V + v]; },
+  block_gemm<false, true>(m, K, V, [&](int r, int v) { return dVp[r * V + v]; },
              [&](int v, int k) { return X[k * V + v]; }, gsm,
              [&](int r, int k, float a) { dqb[r * K + k] += a; });
-  block_gemm(K, V, m, [&](int k, int r) { return qb[r * K + k]; },
+  block_gemm<true, false>(K, V, m, [&](int k, int r) { return qb[r * K + k]; },
              [&](int r, int v) { return dVp[r * V + v]; }, gsm,
              [&](int k, int v, float a) { dSb[k * V + v] += a; });
 }
@@ -339,24 +340,24 @@ __global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
     for (int l = 1; l < L; ++l) {
       const float* Ql = rec + f.rec.Q + int64_t(l) * kC * K;
       float* dSl = dS + int64_t(l) * K * V;
-      block_gemm(K, V, kC, [&](int k, int i) { return Ql[i * K + k]; },
+      block_gemm<true, false>(K, V, kC, [&](int k, int i) { return Ql[i * K + k]; },
                  [&](int i, int c) { return d_o_at(p, b, t0 + i, h, c); }, gsm,
                  [&](int k, int c, float a) { dSl[k * V + c] += a; });
     }
     // Level 0: dv_new = (mix0 scale A_qk)^T dO + Kt dS0 (the S0 entering the
     // next chunk, naive.py:392), kept for the local pass with dS0 itself.
     float* dv = p.dvn + (bh * f.NT + n) * kC * V;
-    block_gemm(kC, V, kC + K,
-               [&](int i, int j) { return j < kC ? Am[j * kC + i] : Kt[i * K + j - kC]; },
-               [&](int j, int c) {
-                 return j < kC ? d_o_at(p, b, t0 + j, h, c) : dS[(j - kC) * V + c];
-               },
-               gsm, [&](int i, int c, float a) { dv[i * V + c] = a; });
+    block_gemm<true, false>(kC, V, kC, [&](int i, int j) { return Am[j * kC + i]; },
+                            [&](int j, int c) { return d_o_at(p, b, t0 + j, h, c); }, gsm,
+                            [&](int i, int c, float a) { dv[i * V + c] = a; });
+    block_gemm(kC, V, K, [&](int i, int k) { return Kt[i * K + k]; },
+               [&](int k, int c) { return dS[k * V + c]; }, gsm,
+               [&](int i, int c, float a) { dv[i * V + c] += a; });
     float* dsn = p.dsn + (bh * f.NT + n) * K * V;
     for (int e = tid; e < K * V; e += blockDim.x) dsn[e] = dS[e];
     __syncthreads();
     // dS0 <- e^(G_last) dS0 + (mix0 scale q e^G)^T dO - W^T dv_new
-    block_gemm(K, V, 2 * kC,
+    block_gemm<true, false>(K, V, 2 * kC,
                [&](int k, int i) { return i < kC ? Q0[i * K + k] : -Wm[(i - kC) * K + k]; },
                [&](int i, int c) { return i < kC ? d_o_at(p, b, t0 + i, h, c) : dv[(i - kC) * V + c]; },
                gsm, [&](int k, int c, float a) { dS[k * V + c] = eg[k] * dS[k * V + c] + a; });
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
 // ---------------------------------------------------------------------------
 
 size_t bwd_local_smem(int K) {
-  return sizeof(float) * (5 * size_t(kC) * (K + 1) + 3 * kC * 65 + kC + K + kGemmSmemFloats);
+  return sizeof(float) * (5 * size_t(kC) * (K + 1) + 3 * kC * 65 + kC + 2 * K + kGemmSmemFloats);
 }
 
 __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
@@ -385,13 +386,14 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   float* Qs = Gs + kC * KP;     // [64][K+1] scale q_0
   float* Ks = Qs + kC * KP;     // [64][K+1] k
   float* Bs = Ks + kC * KP;     // [64][K+1] b
-  float* dGs = Bs + kC * KP;    // [64][K+1] dG
-  float* Ts = dGs + kC * KP;    // [64][65] T (strictly lower)
+  float* Eg = Bs + kC * KP;     // [64][K+1] e^g (per token step)
+  float* Ts = Eg + kC * KP;     // [64][65] T (strictly lower)
   float* As = Ts + kC * 65;     // [64][65] A_qk, then dA_qk
   float* Dt = As + kC * 65;     // [64][65] dT
   float* mx = Dt + kC * 65;     // [64] mix_l of the rows
   float* dGl = mx + kC;         // [K] dG_last
-  float* gsm = dGl + K;
+  int* npos = reinterpret_cast<int*>(dGl + K);  // [K] channel has a g > 0 in the chunk
+  float* gsm = dGl + 2 * K;
   const float* rec = f.chunks + (bh * f.NT + n) * f.rec.size;
   const float* Um = rec + f.rec.U;
   const float* Wm = rec + f.rec.W;
@@ -405,6 +407,7 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   float* dRW = scr + p.ls.drw;
   float* dRU = scr + p.ls.dru;
   float* dKTA = scr + p.ls.dkta;
+  float* dGc = scr + p.ls.dgc;
   auto dO = [&](int i, int c) { return d_o_at(p, b, t0 + i, h, c); };
   // fp32 output row of token i (rows past T are never written)
   auto orow = [&](int i, int width) { return ((int64_t(b) * f.T + t0 + i) * f.H + h) * width; };
@@ -415,34 +418,33 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     const bool ok = t < f.T;
     Qs[i * KP + d] = ok ? f.q.at(b, t, h, 0, d) * f.scale : 0.f;
     Ks[i * KP + d] = ok ? f.k.at(b, t, h, d) : 0.f;
-    Gs[i * KP + d] = ok ? f.g.at(b, t, h, d) : 0.f;
+    const float g = ok ? f.g.at(b, t, h, d) : 0.f;
+    Gs[i * KP + d] = g;
+    Eg[i * KP + d] = expf(g);
     Bs[i * KP + d] = ok ? f.b.at(b, t, h, d) : 0.f;
-    dGs[i * KP + d] = 0.f;
   }
   for (int i = tid; i < kC; i += nth) mx[i] = t0 + i < f.T ? f.mix.at(b, t0 + i, h, 0) : 0.f;
   for (int k = tid; k < K; k += nth) dGl[k] = 0.f;
   __syncthreads();
   if (tid < K) {
     float acc = 0.f;
+    int pos = 0;
     for (int i = 0; i < kC; ++i) {
-      acc += Gs[i * KP + tid];
+      const float g = Gs[i * KP + tid];
+      pos |= g > 0.f;
+      acc += g;
       Gs[i * KP + tid] = acc;
     }
+    npos[tid] = pos;
   }
-  __syncthreads();
-  // T and A_qk with the reference's clamped decays (naive.py:335-344, 377-378).
-  for (int e = tid; e < kC * kC; e += nth) {
-    const int i = e / kC, j = e % kC;
-    float aq = 0.f, ak = 0.f;
-    if (j <= i) {
-      for (int d = 0; d < K; ++d) {
-        const float kd = Ks[j * KP + d] * expf(fminf(Gs[i * KP + d] - Gs[j * KP + d], 0.f));
-        aq = fmaf(Qs[i * KP + d], kd, aq);
-        ak = fmaf(Bs[i * KP + d] * Ks[i * KP + d], kd, ak);
-      }
+  // T and scale * A_qk as the forward's prep computed them (naive.py:335-344,
+  // 377-378, clamped decays).
+  {
+    const float* ta = f.ck_ta + (bh * f.NT + n) * 2 * kC * kC;
+    for (int e = tid; e < kC * kC; e += nth) {
+      Ts[(e / kC) * 65 + e % kC] = ta[e];
+      As[(e / kC) * 65 + e % kC] = ta[kC * kC + e];
     }
-    As[i * 65 + j] = aq;
-    Ts[i * 65 + j] = j < i ? ak : 0.f;
   }
   __syncthreads();
   // dmix_0 = sum_v dO r_0, r_0 = A_qk v_new + (q~ e^G) S0 (naive.py:377-390)
@@ -461,17 +463,17 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   }
   __syncthreads();
   // dA_qk = (mix_0 dO) v_new^T on the causal triangle; d(q~ e^G) = (mix_0 dO) S0^T
-  block_gemm(kC, kC + K, V, [&](int i, int c) { return mx[i] * dO(i, c); },
+  block_gemm<false, true>(kC, kC + K, V, [&](int i, int c) { return mx[i] * dO(i, c); },
              [&](int c, int j) { return j < kC ? vn[j * V + c] : S0[(j - kC) * V + c]; }, gsm,
              [&](int i, int j, float a) {
                if (j < kC) As[i * 65 + j] = j <= i ? a : 0.f;
                else dQG[i * K + j - kC] = a;
              });
   // dKt = v_new dS'^T; dW = -dv_new S0^T (the [W] half of dY); dU = dv_new
-  block_gemm(kC, K, V, [&](int i, int c) { return vn[i * V + c]; },
+  block_gemm<false, true>(kC, K, V, [&](int i, int c) { return vn[i * V + c]; },
              [&](int c, int k) { return dSn[k * V + c]; }, gsm,
              [&](int i, int k, float a) { dKt[i * K + k] = a; });
-  block_gemm(kC, K, V, [&](int i, int c) { return dvn[i * V + c]; },
+  block_gemm<false, true>(kC, K, V, [&](int i, int c) { return dvn[i * V + c]; },
              [&](int c, int k) { return S0[k * V + c]; }, gsm,
              [&](int i, int k, float a) { dRW[i * K + k] = -a; });
   for (int e = tid; e < kC * V; e += nth) dRU[e] = dvn[e];
@@ -499,7 +501,7 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   }
   __syncthreads();
   // dT = -dR [U | W]^T on the strict lower triangle
-  block_gemm(kC, kC, V + K,
+  block_gemm<false, true>(kC, kC, V + K,
              [&](int i, int c) { return c < V ? dRU[i * V + c] : dRW[i * K + c - V]; },
              [&](int c, int j) { return c < V ? Um[j * V + c] : Wm[j * K + c - V]; }, gsm,
              [&](int i, int j, float a) { Dt[i * 65 + j] = j < i ? -a : 0.f; });
@@ -513,30 +515,46 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     }
   }
   // Column pass over the decayed blocks: for key j, sums over the rows i.
+  // e^(G_i - G_j) is a running product of the steps' e^g (exact to a few ulp);
+  // a channel with a positive log-decay in the chunk takes the reference's
+  // clamped exponent term by term instead.
   for (int e = tid; e < kC * K; e += nth) {
     const int j = e / K, d = e % K;
     const float gj = Gs[j * KP + d];
-    float acc = 0.f, accg = 0.f;
+    const bool exact = npos[d] != 0;
+    float acc = 0.f, accg = 0.f, ex = 1.f;
     for (int i = j; i < kC; ++i) {
-      const float x = Gs[i * KP + d] - gj;
-      const float ex = expf(fminf(x, 0.f));
+      float x = 0.f;
+      if (exact) {
+        x = Gs[i * KP + d] - gj;
+        ex = expf(fminf(x, 0.f));
+      } else if (i > j) {
+        ex *= Eg[i * KP + d];
+      }
       const float term = (i > j ? Dt[i * 65 + j] * Bs[i * KP + d] * Ks[i * KP + d] : 0.f) +
                          As[i * 65 + j] * Qs[i * KP + d];
       acc = fmaf(term, ex, acc);
       if (x <= 0.f) accg = fmaf(term, ex, accg);
     }
     dKTA[j * K + d] = acc;
-    dGs[j * KP + d] = -Ks[j * KP + d] * accg;
+    dGc[j * K + d] = -Ks[j * KP + d] * accg;
   }
   __syncthreads();
   // Row pass and assembly of every gradient of the token row.
   for (int e = tid; e < kC * K; e += nth) {
     const int i = e / K, d = e % K, t = t0 + i;
     const float gi = Gs[i * KP + d];
-    float dbk = 0.f, dqs = 0.f, gbk = 0.f, gqs = 0.f;
-    for (int j = 0; j <= i; ++j) {
-      const float x = gi - Gs[j * KP + d];
-      const float kx = Ks[j * KP + d] * expf(fminf(x, 0.f));
+    const bool exact = npos[d] != 0;
+    float dbk = 0.f, dqs = 0.f, gbk = 0.f, gqs = 0.f, ex = 1.f;
+    for (int j = i; j >= 0; --j) {
+      float x = 0.f;
+      if (exact) {
+        x = gi - Gs[j * KP + d];
+        ex = expf(fminf(x, 0.f));
+      } else if (j < i) {
+        ex *= Eg[(j + 1) * KP + d];
+      }
+      const float kx = Ks[j * KP + d] * ex;
       const float tt = j < i ? Dt[i * 65 + j] : 0.f, aa = As[i * 65 + j];
       dbk = fmaf(tt, kx, dbk);
       dqs = fmaf(aa, kx, dqs);
@@ -548,9 +566,7 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     const float q = Qs[i * KP + d], k = Ks[i * KP + d], bb = Bs[i * KP + d];
     const float eG = expf(gi), eT = expf(Gs[(kC - 1) * KP + d] - gi);
     const float rw = dRW[i * K + d], qg = dQG[i * K + d], kt = dKt[i * K + d];
-    float dG = dGs[i * KP + d] + bb * k * gbk + q * gqs + rw * k * bb * eG + qg * q * eG -
-               kt * k * eT;
-    dGs[i * KP + d] = dG;
+    dGc[i * K + d] += bb * k * gbk + q * gqs + rw * k * bb * eG + qg * q * eG - kt * k * eT;
     if (t < f.T) {
       p.dq[(int64_t(b) * f.T + t) * f.H * f.L * K + (int64_t(h) * f.L) * K + d] =
           f.scale * (dqs + qg * eG);
@@ -567,7 +583,7 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     for (int i = 0; i < kC; ++i)
       acc += dKt[i * K + tid] * Ks[i * KP + tid] * expf(gl - Gs[i * KP + tid]);
     for (int i = kC - 1; i >= 0; --i) {
-      acc += dGs[i * KP + tid];
+      acc += dGc[i * K + tid];
       if (t0 + i < f.T) p.dg[orow(i, K) + tid] = acc;
     }
   }
@@ -578,7 +594,7 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     __syncthreads();
     for (int i = tid; i < kC; i += nth) mx[i] = t0 + i < f.T ? f.mix.at(b, t0 + i, h, l) : 0.f;
     __syncthreads();
-    block_gemm(kC, K, V, [&](int i, int c) { return dO(i, c); },
+    block_gemm<false, true>(kC, K, V, [&](int i, int c) { return dO(i, c); },
                [&](int c, int k) { return Sl[k * V + c]; }, gsm,
                [&](int i, int k, float a) {
                  if (t0 + i < f.T)
@@ -605,8 +621,8 @@ cudaError_t launch_fwd_simt(const FwdParams& p, int stage, cudaStream_t stream);
 
 // Workspace of the backward, in floats, region by region.
 struct BwdLayout {
-  int64_t params32, chunks, scan, fin, ck0, ck_up, ck_vnew, dparams, dS, dsn, dvn, pscr, lscr,
-      size;
+  int64_t params32, chunks, scan, fin, ck0, ck_up, ck_vnew, ck_ta, dparams, dS, dsn, dvn, pscr,
+      lscr, size;
   int64_t ck_up_off[NGDN2_MAX_LEVELS];
   int ck_up_n[NGDN2_MAX_LEVELS];
 };
@@ -632,6 +648,7 @@ BwdLayout bwd_layout(const FwdParams& f, const PromoBwdScratch& ps, const LocalS
   }
   w.ck_up = take(up);
   w.ck_vnew = take(bh * f.NT * cv);
+  w.ck_ta = take(bh * f.NT * 2 * kC * kC);
   w.dparams = take(int64_t(f.B) * f.pl.size);
   w.dS = take(bh * f.L * kv);
   w.dsn = take(bh * f.NT * kv);
@@ -680,6 +697,7 @@ cudaError_t launch_bwd(BwdParams bp, float* ws, float* const dparam_out[5], cuda
     f.ck_up_n[l] = w.ck_up_n[l];
   }
   f.ck_vnew = ws + w.ck_vnew;
+  f.ck_ta = ws + w.ck_ta;
   bp.dparams = f.L > 1 ? ws + w.dparams : nullptr;
   bp.dS = ws + w.dS;
   bp.dsn = ws + w.dsn;

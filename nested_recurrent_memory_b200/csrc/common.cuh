@@ -52,9 +52,12 @@ __device__ __forceinline__ float softplusf_(float x) {
 //
 // For m < M, n < N: epi(m, n, sum_k la(m, k) * lb(k, n)).
 // ``la`` and ``lb`` are element loaders (so strides, transposes, dtype
-// conversion and elementwise pre-products are free); operands are staged
-// through shared memory in 64x16 and 16x64 tiles and each thread owns a 4x4
-// block of outputs. The block needs at least kGemmThreads threads (more
+// conversion and elementwise pre-products are free); AT / BT say that the
+// loader's source is contiguous along m (A) / along k (B) rather than along
+// k / n, so that the tile loads are issued in the coalesced order; operands are staged
+// through shared memory in 64x16 and 16x64 tiles (the next tile's elements
+// load into registers during the current tile's FMAs) and each thread owns a
+// 4x4 block of outputs. The block needs at least kGemmThreads threads (more
 // only join the barriers) and every thread must call it (it synchronises). M and N are arbitrary; Kd
 // must be a multiple of 16. ``smem`` holds kGemmSmemFloats floats.
 // ---------------------------------------------------------------------------
@@ -63,7 +66,7 @@ constexpr int kGemmThreads = 256;
 constexpr int kGemmLd = 65;
 constexpr int kGemmSmemFloats = 2 * 16 * kGemmLd;
 
-template <class LA, class LB, class Epi>
+template <bool AT = false, bool BT = false, class LA, class LB, class Epi>
 __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi epi) {
   float* As = smem;                 // [16][65], k-major
   float* Bs = smem + 16 * kGemmLd;  // [16][65]
@@ -71,6 +74,7 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
   const bool act = tid < kGemmThreads;  // larger blocks: the rest only join the barriers
   const int tm = (tid / 16) * 4;
   const int tn = (tid % 16) * 4;
+  constexpr int kPer = 64 * 16 / kGemmThreads;  // tile elements each thread stages
   for (int m0 = 0; m0 < M; m0 += 64) {
     for (int n0 = 0; n0 < N; n0 += 64) {
       float acc[4][4];
@@ -78,21 +82,34 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+      // The next k-step's elements are loaded into registers while the
+      // current one is multiplied, so operand latency overlaps the FMAs.
+      float ra[kPer], rb[kPer];
+      auto fetch = [&](int k0) {
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+          const int e = tid + q * kGemmThreads;
+          const int mm = AT ? e % 64 : e / 16, ka = AT ? e / 64 : e % 16;
+          const int kb = BT ? e % 16 : e / 64, nn = BT ? e / 16 : e % 64;
+          ra[q] = m0 + mm < M ? la(m0 + mm, k0 + ka) : 0.f;
+          rb[q] = n0 + nn < N ? lb(k0 + kb, n0 + nn) : 0.f;
+        }
+      };
+      if (act) fetch(0);
       for (int k0 = 0; k0 < Kd; k0 += 16) {
         if (act) {
-          for (int e = tid; e < 64 * 16; e += kGemmThreads) {
-            int mm = e / 16, kk = e % 16;
-            int gm = m0 + mm;
-            As[kk * kGemmLd + mm] = gm < M ? la(gm, k0 + kk) : 0.f;
-          }
-          for (int e = tid; e < 64 * 16; e += kGemmThreads) {
-            int kk = e / 64, nn = e % 64;
-            int gn = n0 + nn;
-            Bs[kk * kGemmLd + nn] = gn < N ? lb(k0 + kk, gn) : 0.f;
+#pragma unroll
+          for (int q = 0; q < kPer; ++q) {
+            const int e = tid + q * kGemmThreads;
+            if (AT) As[(e / 64) * kGemmLd + e % 64] = ra[q];
+            else As[(e % 16) * kGemmLd + e / 16] = ra[q];
+            if (BT) Bs[(e % 16) * kGemmLd + e / 16] = rb[q];
+            else Bs[(e / 64) * kGemmLd + e % 64] = rb[q];
           }
         }
         __syncthreads();
         if (act) {
+          if (k0 + 16 < Kd) fetch(k0 + 16);
 #pragma unroll
           for (int kk = 0; kk < 16; ++kk) {
             float a[4], bb[4];

@@ -122,6 +122,9 @@ struct FwdParams {
   int64_t ck_up_off[NGDN2_MAX_LEVELS];
   int ck_up_n[NGDN2_MAX_LEVELS];  // NG_l + 1
   float* ck_vnew;
+  // And the chunk's A_kk (strict lower) and scale * A_qk (causal, no mix),
+  // [B, H, NT, 2, 64, 64].
+  float* ck_ta;
 };
 
 // Arguments of the update-scan kernel (update_fwd.py:131-204).

@@ -38,7 +38,7 @@ static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, flo
                [&](int r, int c, float a) { Vp[r * V + c] = a; });
     vals = Vp;
     // u = values . W_k^T (probe.py:99)
-    block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+    block_gemm<false, true>(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
                [&](int v, int k) { return kp[k * V + v]; }, gsm,
                [&](int r, int k, float a) { Kk[r * K + k] = a; });
   }
@@ -94,7 +94,7 @@ static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, flo
   block_gemm(m, V, K, [&](int r, int k) { return Bl[r * K + k]; },
              [&](int k, int c) { return Sl[k * V + c]; }, gsm,
              [&](int r, int c, float a) { Vn2[r * V + c] = Wl[r * V + c] - a; });
-  block_gemm(K, V, m, [&](int k, int r) { return Kk[r * K + k]; },
+  block_gemm<true, false>(K, V, m, [&](int k, int r) { return Kk[r * K + k]; },
              [&](int r, int c) { return Vn2[r * V + c]; }, gsm,
              [&](int k, int c, float a) { Sl[k * V + c] += a; });
 }

@@ -100,6 +100,11 @@ __global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
     }
     Aqk[i * 65 + j] = aq;
     Akk[i * 65 + j] = (j < i) ? ak : 0.f;
+    if (p.ck_ta) {
+      float* ta = p.ck_ta + ((int64_t(b) * p.H + h) * p.NT + n) * 2 * kC * kC;
+      ta[e] = (j < i) ? ak : 0.f;
+      ta[kC * kC + e] = aq * p.scale;
+    }
   }
   __syncthreads();
 
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
       if (t < p.T) store_elem(p.o, ((int64_t(b) * p.T + t) * p.H + h) * V + c, Ot[e], p.dtype);
     }
     // S0 <- e^(G_last) S0 + (k e^(G_last - G))^T v_new (naive.py:392)
-    block_gemm(K, V, kC, [&](int k, int i) { return Kt[i * K + k]; },
+    block_gemm<true, false>(K, V, kC, [&](int k, int i) { return Kt[i * K + k]; },
                [&](int i, int c) { return Vn[i * V + c]; }, gsm,
                [&](int k, int c, float a) { S[k * V + c] = eg[k] * S[k * V + c] + a; });
     // Levels whose firing this chunk completes, bottom-up (naive.py:394-415).

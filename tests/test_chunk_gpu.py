@@ -184,11 +184,14 @@ def test_repeatable_bit_exact():
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
 
 
-def test_backward_is_not_built():
+def test_backward_reaches_only_differentiable_inputs():
+    """Autograd through the op: q gets a gradient, the int schedule tensors
+    none (the backward's parity is tests/test_bwd_gpu.py)."""
     inp = op_inputs(1, 128, 1, 64, 64, 2, 16, firing_intervals=(1, 2))
     L = inp.pop("L")
     dev = _to_dev(inp)
     dev["q"].requires_grad_(True)
     o, _ = chunk_nested_gdn2(**dev, L=L)
-    with pytest.raises(NotImplementedError):
-        o.sum().backward()
+    o.sum().backward()
+    assert dev["q"].grad is not None and torch.isfinite(dev["q"].grad).all()
+    assert dev["q"].grad.shape == dev["q"].shape
