@@ -54,7 +54,9 @@ __device__ __forceinline__ float softplusf_(float x) {
 // ``la`` and ``lb`` are element loaders (so strides, transposes, dtype
 // conversion and elementwise pre-products are free); AT / BT say that the
 // loader's source is contiguous along m (A) / along k (B) rather than along
-// k / n, so that the tile loads are issued in the coalesced order; operands are staged
+// k / n, so that the tile loads are issued in the coalesced order; PF = false
+// loads each tile straight into shared memory when the previous one is
+// consumed (fewer live registers, for kernels at their register cap); operands are staged
 // through shared memory in 64x16 and 16x64 tiles (the next tile's elements
 // load into registers during the current tile's FMAs) and each thread owns a
 // 4x4 block of outputs. The block needs at least kGemmThreads threads (more
@@ -66,7 +68,7 @@ constexpr int kGemmThreads = 256;
 constexpr int kGemmLd = 65;
 constexpr int kGemmSmemFloats = 2 * 16 * kGemmLd;
 
-template <bool AT = false, bool BT = false, class LA, class LB, class Epi>
+template <bool AT = false, bool BT = false, bool PF = true, class LA, class LB, class Epi>
 __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi epi) {
   float* As = smem;                 // [16][65], k-major
   float* Bs = smem + 16 * kGemmLd;  // [16][65]
@@ -82,6 +84,36 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+      if constexpr (!PF) {
+        for (int k0 = 0; k0 < Kd; k0 += 16) {
+          if (act) {
+            for (int e = tid; e < 64 * 16; e += kGemmThreads) {
+              const int mm = AT ? e % 64 : e / 16, ka = AT ? e / 64 : e % 16;
+              As[ka * kGemmLd + mm] = m0 + mm < M ? la(m0 + mm, k0 + ka) : 0.f;
+            }
+            for (int e = tid; e < 64 * 16; e += kGemmThreads) {
+              const int kb = BT ? e % 16 : e / 64, nn = BT ? e / 16 : e % 64;
+              Bs[kb * kGemmLd + nn] = n0 + nn < N ? lb(k0 + kb, n0 + nn) : 0.f;
+            }
+          }
+          __syncthreads();
+          if (act) {
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) {
+              float a[4], bb[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + i];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + j];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+            }
+          }
+          __syncthreads();
+        }
+      } else {
       // The next k-step's elements are loaded into registers while the
       // current one is multiplied, so operand latency overlaps the FMAs.
       float ra[kPer], rb[kPer];
@@ -124,6 +156,7 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
           }
         }
         __syncthreads();
+      }
       }
       if (act) {
 #pragma unroll

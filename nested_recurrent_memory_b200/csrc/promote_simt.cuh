@@ -6,7 +6,10 @@
 
 namespace ngdn2 {
 
-// Promote level l-1 into level l for one (b, h): probe then update.
+// Promote level l-1 into level l for one (b, h): probe then update. PF is
+// block_gemm's prefetch switch (off inside the register-capped tensor-core
+// scan).
+template <bool PF = true>
 static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, float* S, float* sc,
                              float* gsm) {
   const int K = p.K, V = p.V;
@@ -33,23 +36,23 @@ static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, flo
   // level below itself for merge (probe.py:133-136).
   const float* vals = Sb;
   if (!merge) {
-    block_gemm(m, V, K, [&](int r, int k) { return qb[r * K + k]; },
+    block_gemm<false, false, PF>(m, V, K, [&](int r, int k) { return qb[r * K + k]; },
                [&](int k, int c) { return Sb[k * V + c]; }, gsm,
                [&](int r, int c, float a) { Vp[r * V + c] = a; });
     vals = Vp;
     // u = values . W_k^T (probe.py:99)
-    block_gemm<false, true>(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+    block_gemm<false, true, PF>(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
                [&](int v, int k) { return kp[k * V + v]; }, gsm,
                [&](int r, int k, float a) { Kk[r * K + k] = a; });
   }
   // gate logits (probe.py:59-62)
-  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+  block_gemm<false, false, PF>(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
              [&](int v, int k) { return bp[v * K + k]; }, gsm,
              [&](int r, int k, float a) { Bl[r * K + k] = a; });
-  block_gemm(m, V, V, [&](int r, int v) { return vals[r * V + v]; },
+  block_gemm<false, false, PF>(m, V, V, [&](int r, int v) { return vals[r * V + v]; },
              [&](int v, int u) { return wp[v * V + u]; }, gsm,
              [&](int r, int u, float a) { Wl[r * V + u] = a; });
-  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
+  block_gemm<false, false, PF>(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
              [&](int v, int k) { return gp[v * K + k]; }, gsm,
              [&](int r, int k, float a) { Gl[r * K + k] = a; });
   if (!merge) {
@@ -91,10 +94,10 @@ static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, flo
   // S <- e^g S; vn = v*w - (k*b) S; S <- S + k^T vn  (update_fwd.py:120-123)
   for (int e = tid; e < K * V; e += blockDim.x) Sl[e] *= expf(gv[e / V]);
   __syncthreads();
-  block_gemm(m, V, K, [&](int r, int k) { return Bl[r * K + k]; },
+  block_gemm<false, false, PF>(m, V, K, [&](int r, int k) { return Bl[r * K + k]; },
              [&](int k, int c) { return Sl[k * V + c]; }, gsm,
              [&](int r, int c, float a) { Vn2[r * V + c] = Wl[r * V + c] - a; });
-  block_gemm<true, false>(K, V, m, [&](int k, int r) { return Kk[r * K + k]; },
+  block_gemm<true, false, PF>(K, V, m, [&](int k, int r) { return Kk[r * K + k]; },
              [&](int r, int c) { return Vn2[r * V + c]; }, gsm,
              [&](int k, int c, float a) { Sl[k * V + c] += a; });
 }

@@ -1440,7 +1440,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
       for (int l = 1; l < L; ++l) {
         if (!(fire_mask >> l & 1u)) continue;
         if (!learned) {
-          promote_simt(p, b, h, l, Sg, sc, gsm);
+          promote_simt<false>(p, b, h, l, Sg, sc, gsm);
           refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
           fence_proxy_async();
           __syncthreads();
