@@ -148,6 +148,34 @@ typedef struct ngdn2_update_args {
   float* final_state;                           /* [B, H, K, V] out */
 } ngdn2_update_args;
 
+/* Arguments of ngdn2_update_state_bwd (update_bwd.py:167-263,
+ * update_state_bwd): the gradients of sum(states * d_states) +
+ * sum(final * d_final) for the write scan, fp32 outputs. */
+typedef struct ngdn2_update_bwd_args {
+  int32_t abi_version;
+  int32_t B, NF, NG, H, K, V, N;
+  int32_t block_v;      /* validated as in the forward; the kernel does not split V */
+  int32_t dtype;        /* of keys, values, b, w */
+  int32_t g_dtype;      /* of g */
+  int32_t has_init;     /* write dinit */
+  const float* states;                          /* [B, NG, H, K, V] from the forward */
+  const void* keys;   int64_t keys_stride[5];   /* [B, NF, H, N, K]; the K stride must be 1 */
+  const void* values;                           /* [B, NF, H, N, V] contiguous */
+  const void* g;                                /* [B, NF, H, K] contiguous */
+  const void* b;                                /* [B, NF, H, N, K] contiguous */
+  const void* w;                                /* [B, NF, H, N, V] contiguous */
+  const float* d_states;                        /* [B, NG, H, K, V] contiguous */
+  const float* d_final;                         /* [B, H, K, V] contiguous */
+  float* dkeys;                                 /* [B, NF, H, N, K] out */
+  float* dvalues;                               /* [B, NF, H, N, V] out */
+  float* dg;                                    /* [B, NF, H, K] out */
+  float* db;                                    /* [B, NF, H, N, K] out */
+  float* dw;                                    /* [B, NF, H, N, V] out */
+  float* dinit;                                 /* [B, H, K, V] out, or NULL */
+  void* workspace;                              /* >= ngdn2_update_bwd_workspace_size */
+  size_t workspace_bytes;
+} ngdn2_update_bwd_args;
+
 /* Arguments of ngdn2_step: one token of every batch row (naive.py:42-134).
  * Per-token inputs carry no T dimension. */
 typedef struct ngdn2_step_args {
@@ -222,6 +250,7 @@ NGDN2_API size_t ngdn2_sizeof_fwd_args(void);
 NGDN2_API size_t ngdn2_sizeof_update_args(void);
 NGDN2_API size_t ngdn2_sizeof_step_args(void);
 NGDN2_API size_t ngdn2_sizeof_bwd_args(void);
+NGDN2_API size_t ngdn2_sizeof_update_bwd_args(void);
 NGDN2_API const char* ngdn2_error_string(int code);
 
 /* Validates *args and returns the workspace ngdn2_fwd needs, in bytes. */
@@ -256,6 +285,11 @@ NGDN2_API int ngdn2_bwd_num_launches(const ngdn2_bwd_args* args);
 
 /* The promotion write scan on its own. */
 NGDN2_API int ngdn2_update_state(const ngdn2_update_args* args, void* stream);
+
+/* Its backward (update_bwd.py:167-263); same validation and error codes as
+ * the forward (update_bwd.py:197-206). */
+NGDN2_API int ngdn2_update_bwd_workspace_size(const ngdn2_update_bwd_args* args, size_t* bytes);
+NGDN2_API int ngdn2_update_state_bwd(const ngdn2_update_bwd_args* args, void* stream);
 
 /* Validates *args and returns the workspace ngdn2_step needs, in bytes
  * (fp32 parameter copies and promotion scratch). */

@@ -2,9 +2,9 @@
 
 A drop-in for the reference's ``nested_gdn2.ops`` ops (``chunk_nested_gdn2``
 with its backward, ``chunk_nested_gdn2_fwd``, ``chunk_nested_gdn2_bwd``,
-``update_state``, and the one-token decode step ``naive_step_nested_gdn2`` as
-``step_nested_gdn2``), computed by hand-written sm_100a CUDA kernels behind
-the C ABI in ``include/ngdn2.h``.
+``update_state``, ``update_state_bwd``, and the one-token decode step
+``naive_step_nested_gdn2`` as ``step_nested_gdn2``), computed by hand-written
+sm_100a CUDA kernels behind the C ABI in ``include/ngdn2.h``.
 """
 
 from .ops import (  # noqa: F401
@@ -18,6 +18,7 @@ from .ops import (  # noqa: F401
     n_groups,
     step_nested_gdn2,
     update_state,
+    update_state_bwd,
 )
 
 __version__ = "0.1.0"

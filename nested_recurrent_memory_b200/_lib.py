@@ -1,7 +1,8 @@
 """ctypes binding of ``libngdn2.so`` (the C ABI declared in include/ngdn2.h).
 
 The structs below mirror ``ngdn2_fwd_args``, ``ngdn2_update_args``,
-``ngdn2_step_args`` and ``ngdn2_bwd_args`` field for field; ``check_layout()`` compares their sizes with the library's own
+``ngdn2_step_args``, ``ngdn2_bwd_args`` and ``ngdn2_update_bwd_args`` field
+for field; ``check_layout()`` compares their sizes with the library's own
 ``sizeof``. Loading fails loudly: there is no fallback implementation.
 """
 
@@ -81,6 +82,20 @@ class StepArgs(ctypes.Structure):
     ]
 
 
+class UpdateBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", c_i32),
+        ("B", c_i32), ("NF", c_i32), ("NG", c_i32), ("H", c_i32), ("K", c_i32),
+        ("V", c_i32), ("N", c_i32), ("block_v", c_i32), ("dtype", c_i32), ("g_dtype", c_i32),
+        ("has_init", c_i32),
+        ("states", c_ptr), ("keys", c_ptr), ("keys_stride", c_i64 * 5),
+        ("values", c_ptr), ("g", c_ptr), ("b", c_ptr), ("w", c_ptr),
+        ("d_states", c_ptr), ("d_final", c_ptr),
+        ("dkeys", c_ptr), ("dvalues", c_ptr), ("dg", c_ptr), ("db", c_ptr), ("dw", c_ptr),
+        ("dinit", c_ptr), ("workspace", c_ptr), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 class BwdArgs(ctypes.Structure):
     _fields_ = [
         ("abi_version", c_i32), ("fwd", FwdArgs), *_tok("d_o", 4), ("d_final", c_ptr),
@@ -98,6 +113,7 @@ EXPORTS = (
     "ngdn2_fwd", "ngdn2_fwd_stage", "ngdn2_fwd_num_launches", "ngdn2_update_state",
     "ngdn2_fwd_noalloc", "ngdn2_sizeof_step_args", "ngdn2_step_workspace_size", "ngdn2_step",
     "ngdn2_sizeof_bwd_args", "ngdn2_bwd_workspace_size", "ngdn2_bwd", "ngdn2_bwd_num_launches",
+    "ngdn2_sizeof_update_bwd_args", "ngdn2_update_bwd_workspace_size", "ngdn2_update_state_bwd",
 )
 
 _LIB = None
@@ -145,6 +161,12 @@ def load(path: str | os.PathLike | None = None):
     lib.ngdn2_bwd.restype = ctypes.c_int
     lib.ngdn2_bwd_num_launches.argtypes = [ctypes.POINTER(BwdArgs)]
     lib.ngdn2_bwd_num_launches.restype = ctypes.c_int
+    lib.ngdn2_sizeof_update_bwd_args.restype = ctypes.c_size_t
+    lib.ngdn2_update_bwd_workspace_size.argtypes = [ctypes.POINTER(UpdateBwdArgs),
+                                                    ctypes.POINTER(ctypes.c_size_t)]
+    lib.ngdn2_update_bwd_workspace_size.restype = ctypes.c_int
+    lib.ngdn2_update_state_bwd.argtypes = [ctypes.POINTER(UpdateBwdArgs), c_ptr]
+    lib.ngdn2_update_state_bwd.restype = ctypes.c_int
     if path is None:
         _LIB = lib
     return lib
@@ -162,6 +184,8 @@ def check_layout(lib=None) -> None:
         raise RuntimeError("ngdn2_step_args layout mismatch")
     if lib.ngdn2_sizeof_bwd_args() != ctypes.sizeof(BwdArgs):
         raise RuntimeError("ngdn2_bwd_args layout mismatch")
+    if lib.ngdn2_sizeof_update_bwd_args() != ctypes.sizeof(UpdateBwdArgs):
+        raise RuntimeError("ngdn2_update_bwd_args layout mismatch")
 
 
 def error_string(code: int) -> str:

@@ -12,6 +12,7 @@ cudaError_t launch_update_simt(const UpdParams& u, cudaStream_t stream);
 int64_t bwd_workspace_floats(const FwdParams& f);
 int num_launches_bwd(const FwdParams& f);
 struct BwdParams;
+cudaError_t launch_update_bwd(const UpdBwdParams& u, cudaStream_t stream);
 cudaError_t launch_bwd_abi(const ngdn2_bwd_args* a, const FwdParams& f, cudaStream_t stream);
 }  // namespace ngdn2
 
@@ -234,6 +235,60 @@ int ngdn2_bwd(const ngdn2_bwd_args* a, void* stream) {
   const size_t need = size_t(bwd_workspace_floats(p)) * sizeof(float);
   if (!a->workspace || a->workspace_bytes < need) return NGDN2_ERR_WORKSPACE;
   const cudaError_t err = launch_bwd_abi(a, p, reinterpret_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? NGDN2_OK : NGDN2_ERR_CUDA;
+}
+
+size_t ngdn2_sizeof_update_bwd_args(void) { return sizeof(ngdn2_update_bwd_args); }
+
+// update_bwd.py:197-206 -- the forward's checks, same order.
+static int validate_update_bwd(const ngdn2_update_bwd_args* a) {
+  if (!a) return NGDN2_ERR_NULL;
+  if (a->abi_version != NGDN2_ABI_VERSION) return NGDN2_ERR_ABI;
+  if (a->N < 16 || !is_pow2(a->N)) return NGDN2_ERR_N_POW2;
+  if (a->block_v < 16 || !is_pow2(a->block_v)) return NGDN2_ERR_BLOCK_V;
+  if (a->V % a->block_v) return NGDN2_ERR_DIVISIBLE;
+  if (a->keys_stride[4] != 1) return NGDN2_ERR_UNIT_STRIDE;
+  if (!(a->NG - 1 <= a->NF && a->NF <= a->NG)) return NGDN2_ERR_INCONSISTENT;
+  if (!dtype_ok(a->dtype) || !dtype_ok(a->g_dtype)) return NGDN2_ERR_DTYPE;
+  if (a->B < 1 || a->H < 1 || a->NF < 0 || a->NG < 1 || a->N > 128 || !dim_ok(a->K) ||
+      !dim_ok(a->V))
+    return NGDN2_ERR_SHAPE;
+  if ((a->NF > 0 && (!a->keys || !a->values || !a->g || !a->b || !a->w || !a->dkeys ||
+                     !a->dvalues || !a->dg || !a->db || !a->dw)) ||
+      !a->states || !a->d_states || !a->d_final || (a->has_init && !a->dinit))
+    return NGDN2_ERR_NULL;
+  return NGDN2_OK;
+}
+
+static size_t update_bwd_bytes(const ngdn2_update_bwd_args* a) {
+  const int64_t kv = int64_t(a->K) * a->V, nv = int64_t(a->N) * a->V;
+  return sizeof(float) * size_t(a->B) * a->H * (align_floats(kv) * 3 + align_floats(nv) * 2);
+}
+
+int ngdn2_update_bwd_workspace_size(const ngdn2_update_bwd_args* a, size_t* bytes) {
+  const int rc = validate_update_bwd(a);
+  if (rc != NGDN2_OK) return rc;
+  if (!bytes) return NGDN2_ERR_NULL;
+  *bytes = update_bwd_bytes(a);
+  return NGDN2_OK;
+}
+
+int ngdn2_update_state_bwd(const ngdn2_update_bwd_args* a, void* stream) {
+  const int rc = validate_update_bwd(a);
+  if (rc != NGDN2_OK) return rc;
+  if (!a->workspace || a->workspace_bytes < update_bwd_bytes(a)) return NGDN2_ERR_WORKSPACE;
+  UpdBwdParams u;
+  u.B = a->B; u.NF = a->NF; u.NG = a->NG; u.H = a->H; u.K = a->K; u.V = a->V; u.N = a->N;
+  u.dtype = a->dtype; u.g_dtype = a->g_dtype; u.has_init = a->has_init;
+  u.states = a->states; u.keys = a->keys;
+  u.skb = a->keys_stride[0]; u.skf = a->keys_stride[1]; u.skh = a->keys_stride[2];
+  u.skn = a->keys_stride[3];
+  u.values = a->values; u.g = a->g; u.b = a->b; u.w = a->w;
+  u.d_states = a->d_states; u.d_final = a->d_final;
+  u.dkeys = a->dkeys; u.dvalues = a->dvalues; u.dg = a->dg; u.db = a->db; u.dw = a->dw;
+  u.dinit = a->dinit;
+  u.scr = reinterpret_cast<float*>(a->workspace);
+  const cudaError_t err = launch_update_bwd(u, reinterpret_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? NGDN2_OK : NGDN2_ERR_CUDA;
 }
 

@@ -141,4 +141,20 @@ struct UpdParams {
   float* fin;
 };
 
+// Arguments of the write-scan backward (update_bwd.py:167-263).
+struct UpdBwdParams {
+  int B, NF, NG, H, K, V, N, dtype, g_dtype, has_init;
+  const float* states;
+  const void* keys;
+  int64_t skb, skf, skh, skn;
+  const void* values;
+  const void* g;
+  const void* b;
+  const void* w;
+  const float* d_states;
+  const float* d_final;
+  float *dkeys, *dvalues, *dg, *db, *dw, *dinit;
+  float* scr;  // per (b, h): dS, S_d, dS_d, Z, Y
+};
+
 }  // namespace ngdn2

@@ -30,6 +30,7 @@ __all__ = [
     "chunk_nested_gdn2_fwd",
     "chunk_nested_gdn2_bwd",
     "update_state",
+    "update_state_bwd",
     "step_nested_gdn2",
     "n_groups",
     "n_firings",
@@ -372,6 +373,75 @@ def chunk_nested_gdn2(q, k, v, g, b, w, mix_weights, query_banks, key_projection
         q, k, v, g, b, w, mix_weights, query_banks, key_projections, b_projections,
         w_projections, g_projections, n_queries_per_level, firing_intervals, L, scale,
         initial_state, output_final_state, chunk_size, promotion)
+
+
+def update_state_bwd(states, keys, values, g, b, w, d_states, d_final, has_init=False,
+                     block_v=16):
+    """Backward of ``update_state`` (update_bwd.py:167-263): the gradients of
+    ``sum(states * d_states) + sum(final * d_final)``.
+
+    states [B, NG, H, K, V] (from the forward); keys [B, NF, H, N, K] (may be
+    a broadcast view); values, w [B, NF, H, N, V]; g [B, NF, H, K]; b
+    [B, NF, H, N, K]; d_states like states; d_final [B, H, K, V]. Returns a
+    dict with float32 ``dkeys``, ``dvalues``, ``dg``, ``db``, ``dw`` and, when
+    ``has_init``, ``dinit`` -- as the reference.
+    """
+    B, NF, H, N, K = keys.shape
+    NG = states.shape[1]
+    V = values.shape[-1]
+    # update_bwd.py:197-206, same checks and order.
+    if N < 16 or N & (N - 1):
+        raise ValueError(f"pairs per firing must be a power of two >= 16, got {N}")
+    if block_v < 16 or block_v & (block_v - 1):
+        raise ValueError(f"block_v must be a power of two >= 16, got {block_v}")
+    if V % block_v:
+        raise ValueError(f"V={V} must be divisible by block_v={block_v}")
+    if keys.stride(-1) != 1:
+        raise ValueError("keys must be unit-stride along K")
+    if not (NG - 1 <= NF <= NG):
+        raise ValueError(f"NF={NF} inconsistent with NG={NG}")
+    _require_cuda(states, keys, values, g, b, w, d_states, d_final)
+    dt = values.dtype
+    if keys.dtype != dt:
+        keys = keys.to(dt)
+    values, b, w = (t.to(dt).contiguous() for t in (values, b, w))
+    g = g.contiguous()
+    states, d_states, d_final = (t.to(torch.float32).contiguous()
+                                 for t in (states, d_states, d_final))
+    f32 = dict(dtype=torch.float32, device=values.device)
+    out = {"dkeys": torch.zeros(B, NF, H, N, K, **f32),
+           "dvalues": torch.zeros(B, NF, H, N, V, **f32),
+           "dg": torch.zeros(B, NF, H, K, **f32),
+           "db": torch.zeros(B, NF, H, N, K, **f32),
+           "dw": torch.zeros(B, NF, H, N, V, **f32)}
+    dinit = torch.zeros(B, H, K, V, **f32) if has_init else None
+    a = _lib.UpdateBwdArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.B, a.NF, a.NG, a.H, a.K, a.V, a.N = B, NF, NG, H, K, V, N
+    a.block_v = block_v
+    a.dtype, a.g_dtype = _code(values), _code(g)
+    a.has_init = int(bool(has_init))
+    a.states = states.data_ptr()
+    a.keys = keys.data_ptr()
+    for i, st in enumerate(keys.stride()):
+        a.keys_stride[i] = st
+    a.values, a.g, a.b, a.w = values.data_ptr(), g.data_ptr(), b.data_ptr(), w.data_ptr()
+    a.d_states, a.d_final = d_states.data_ptr(), d_final.data_ptr()
+    (a.dkeys, a.dvalues, a.dg, a.db, a.dw) = (out[n].data_ptr() for n in
+                                              ("dkeys", "dvalues", "dg", "db", "dw"))
+    a.dinit = dinit.data_ptr() if dinit is not None else None
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    rc = lib.ngdn2_update_bwd_workspace_size(ctypes.byref(a), ctypes.byref(nbytes))
+    _raise_for(rc, "ngdn2_update_bwd_workspace_size", N=N, block_v=block_v, V=V, NF=NF, NG=NG)
+    ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=values.device)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    stream = torch.cuda.current_stream(values.device).cuda_stream
+    rc = lib.ngdn2_update_state_bwd(ctypes.byref(a), ctypes.c_void_p(stream))
+    _raise_for(rc, "ngdn2_update_state_bwd", N=N, block_v=block_v, V=V, NF=NF, NG=NG)
+    if has_init:
+        out["dinit"] = dinit
+    return out
 
 
 def update_state(keys, values, g, b, w, n_groups, initial_state=None, block_v=16):

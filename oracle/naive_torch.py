@@ -11,7 +11,8 @@ Follows, by file:line within the reference project:
 * ``nested_gdn2/ops/naive.py:7-39``    -- ``naive_update_step``;
 * ``nested_gdn2/ops/naive.py:226-420`` -- ``naive_chunk_nested_gdn2``;
 * ``nested_gdn2/ops/probe.py:34-136``  -- ``_gates``, ``probe_learned``,
-  ``probe_merge``.
+  ``probe_merge``;
+* ``tests/ops/_update_ref.py:34-51``   -- the group scan over the update step.
 
 Arithmetic runs in ``dtype`` (float64 by default). Layouts are the
 reference's: per-token tensors ``[B, T, H, ...]`` (q ``[B, T, H, L, K]``),
@@ -62,6 +63,24 @@ def update_step(state, keys, values, b, w, g):
     S = state * g.exp().unsqueeze(-1)
     gram = keys.transpose(-1, -2) @ (keys * b)
     return S - gram @ S + keys.transpose(-1, -2) @ (values * w)
+
+
+def update_scan(keys, values, g, b, w, n_groups, initial_state=None):
+    """tests/ops/_update_ref.py:34-51 (the reference's group loop over
+    naive_update_step), differentiable. keys/b [B, NF, H, N, K]; values/w
+    [B, NF, H, N, V]; g [B, NF, H, K]. Returns states [B, NG, H, K, V] (the
+    state entering each group) and the final state [B, H, K, V]."""
+    B, NF, H, _, K = keys.shape
+    V = values.shape[-1]
+    S = initial_state if initial_state is not None else torch.zeros(
+        B, H, K, V, dtype=values.dtype)
+    states = []
+    for j in range(n_groups):
+        states.append(S)
+        if j < NF:
+            S = torch.stack([update_step(S[:, h], keys[:, j, h], values[:, j, h], b[:, j, h],
+                                         w[:, j, h], g[:, j, h]) for h in range(H)], dim=1)
+    return torch.stack(states, dim=1), S
 
 
 def chunk_forward(q, k, v, g, b, w, mix_weights, query_banks, key_projections, b_projections,

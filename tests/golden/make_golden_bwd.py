@@ -10,7 +10,8 @@ through ``naive_chunk_nested_gdn2`` -- the check the reference applies to its
 own backward (tests/ops/test_chunk.py:62-83, 94-111) -- on seeded fp32 CPU
 inputs, and writes ``bwd_*.npz`` next to this script: the op inputs, the
 upstream gradients ``d_o`` and ``d_final``, and ``grad_<input>`` for every
-differentiable input (``grad_initial_state`` when one is given).
+differentiable input (``grad_initial_state`` when one is given); and
+``bwdupd_scan.npz`` for the write scan's backward (update_state_bwd).
 """
 
 from __future__ import annotations
@@ -41,8 +42,44 @@ CASES = [
 ]
 
 
+def update_case(naive):
+    """update_state_bwd's contract (update_bwd.py:167-263): autograd through
+    the reference's group scan over naive_update_step, in float64 as
+    tests/ops/test_update_bwd.py:36-48 does. NG = NF + 1 (ragged) with an
+    initial state."""
+    gen = torch.Generator().manual_seed(21)
+    B, NF, NG, H, K, V, N = 2, 4, 5, 2, 16, 32, 16
+    r = lambda *s: torch.randn(*s, generator=gen, dtype=torch.float64)  # noqa: E731
+    leaves = dict(keys=torch.nn.functional.normalize(r(B, NF, H, N, K), dim=-1),
+                  values=r(B, NF, H, N, V) * V ** -0.5,
+                  g=-torch.nn.functional.softplus(r(B, NF, H, K)),
+                  b=torch.sigmoid(r(B, NF, H, N, K)), w=torch.sigmoid(r(B, NF, H, N, V)))
+    init = r(B, H, K, V) * K ** -0.5
+    leaves = {k: t.requires_grad_(True) for k, t in leaves.items()}
+    init.requires_grad_(True)
+    S, states = init, []
+    for j in range(NG):
+        states.append(S)
+        if j < NF:
+            S = naive.naive_update_step(S, leaves["keys"][:, j], leaves["values"][:, j],
+                                        leaves["b"][:, j], leaves["w"][:, j], leaves["g"][:, j])
+    states = torch.stack(states, 1)
+    d_states = r(B, NG, H, K, V)
+    d_final = r(B, H, K, V)
+    ((states * d_states).sum() + (S * d_final).sum()).backward()
+    arrays = {k: t.detach().numpy() for k, t in leaves.items()}
+    arrays.update(initial_state=init.detach().numpy(), n_groups=NG, out_states=states.detach().numpy(),
+                  out_final=S.detach().numpy(), d_states=d_states.numpy(), d_final=d_final.numpy())
+    for k, t in leaves.items():
+        arrays[f"grad_{k}"] = t.grad.numpy()
+    arrays["grad_initial_state"] = init.grad.numpy()
+    np.savez_compressed(HERE / "bwdupd_scan.npz", **arrays)
+    print("bwdupd_scan", {k: v.shape for k, v in arrays.items() if k.startswith("grad_")})
+
+
 def main(ref_root: str):
     naive, _ = _import_reference(ref_root)
+    update_case(naive)
     for (name, B, T, H, K, V, L, N, firing, nq, promo, with_init) in CASES:
         inp = op_inputs(B, T, H, K, V, L, N, firing_intervals=firing, n_queries_per_level=nq,
                         seed=13)

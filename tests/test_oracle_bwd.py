@@ -71,3 +71,30 @@ def test_torch_oracle_forward_matches_numpy_oracle(promotion):
                                      promotion=promotion)
     assert rel_err(o.numpy(), ro) < 1e-12
     assert rel_err(s.numpy(), rs) < 1e-12
+
+
+def update_oracle_grads(d, dtype=torch.float64):
+    """Autograd through the torch oracle's write scan of
+    sum(states * d_states) + sum(final * d_final)."""
+    names = ("keys", "values", "g", "b", "w")
+    leaves = {n: torch.tensor(d[n], dtype=dtype, requires_grad=True) for n in names}
+    init = d.get("initial_state")
+    init_t = torch.tensor(init, dtype=dtype, requires_grad=True) if init is not None else None
+    states, final = naive_torch.update_scan(**leaves, n_groups=int(d["n_groups"]),
+                                            initial_state=init_t)
+    loss = (states * torch.tensor(d["d_states"], dtype=dtype)).sum() + \
+        (final * torch.tensor(d["d_final"], dtype=dtype)).sum()
+    loss.backward()
+    out = {n: t.grad.numpy() for n, t in leaves.items()}
+    if init_t is not None:
+        out["initial_state"] = init_t.grad.numpy()
+    return states.detach().numpy(), final.detach().numpy(), out
+
+
+def test_torch_oracle_update_scan_gradients_match_reference():
+    d = dict(np.load(GOLDEN / "bwdupd_scan.npz"))
+    states, final, grads = update_oracle_grads(d)
+    assert rel_err(states, d["out_states"]) < 1e-12
+    assert rel_err(final, d["out_final"]) < 1e-12
+    for n, gr in grads.items():
+        assert rel_err(gr, d[f"grad_{n}"]) < 1e-10, n
