@@ -61,7 +61,7 @@ struct PromoBwdScratch {
 
 // Per-chunk scratch of the local pass, fp32, offsets in floats.
 struct LocalScratch {
-  int64_t dqg, dkt, drw, dru, dkta, dgc, size;
+  int64_t dqg, dkt, drw, dru, dkta, dgc, dos, size;
   __host__ __device__ static LocalScratch make(int K, int V) {
     LocalScratch s;
     s.dqg = 0;                                  // [64, K] d(q~ e^G), mix_0 folded
@@ -70,7 +70,8 @@ struct LocalScratch {
     s.dru = align_floats(s.drw + kC * K);       // [64, V] dU, then dR_U
     s.dkta = align_floats(s.dru + kC * V);      // [64, K] dk from the decayed blocks
     s.dgc = align_floats(s.dkta + kC * K);      // [64, K] dG, column part then whole
-    s.size = align_floats(s.dgc + kC * K);
+    s.dos = align_floats(s.dgc + kC * K);       // [64, V] d_o of the chunk, fp32
+    s.size = align_floats(s.dos + kC * V);
     return s;
   }
 };
@@ -92,6 +93,43 @@ struct BwdParams {
   float* lscr;           // [B, H, NT] x LocalScratch
   LocalScratch ls;
 };
+
+// 8 consecutive elements from element offset o (element stride sd) as fp32:
+// one or two vector loads when contiguous and 16-byte aligned.
+__device__ __forceinline__ void load8_any(const void* base, int dt, int64_t o, int64_t sd,
+                                          float* out) {
+  if (sd == 1) {
+    if (dt != NGDN2_F32) {
+      const uint16_t* p16 = reinterpret_cast<const uint16_t*>(base) + o;
+      if ((reinterpret_cast<uintptr_t>(p16) & 15) == 0) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(p16);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (dt == NGDN2_BF16) {
+            out[2 * i] = __uint_as_float(w[i] << 16);
+            out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+          } else {
+            out[2 * i] = __half2float(__ushort_as_half(uint16_t(w[i] & 0xffffu)));
+            out[2 * i + 1] = __half2float(__ushort_as_half(uint16_t(w[i] >> 16)));
+          }
+        }
+        return;
+      }
+    } else {
+      const float* p32 = reinterpret_cast<const float*>(base) + o;
+      if ((reinterpret_cast<uintptr_t>(p32) & 15) == 0) {
+        const float4 a = *reinterpret_cast<const float4*>(p32);
+        const float4 c = *reinterpret_cast<const float4*>(p32 + 4);
+        out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+        out[4] = c.x; out[5] = c.y; out[6] = c.z; out[7] = c.w;
+        return;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = load_elem(base, o + i * sd, dt);
+}
 
 __device__ __forceinline__ float d_o_at(const BwdParams& p, int b, int t, int h, int c) {
   if (t >= p.f.T) return 0.f;
@@ -408,20 +446,47 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   float* dRU = scr + p.ls.dru;
   float* dKTA = scr + p.ls.dkta;
   float* dGc = scr + p.ls.dgc;
-  auto dO = [&](int i, int c) { return d_o_at(p, b, t0 + i, h, c); };
+  float* dOs = scr + p.ls.dos;
+  auto dO = [&](int i, int c) { return dOs[i * V + c]; };
   // fp32 output row of token i (rows past T are never written)
   auto orow = [&](int i, int width) { return ((int64_t(b) * f.T + t0 + i) * f.H + h) * width; };
 
-  // Inputs of the chunk; tokens past T are zeros (naive.py:302-312).
-  for (int e = tid; e < kC * K; e += nth) {
-    const int i = e / K, d = e % K, t = t0 + i;
-    const bool ok = t < f.T;
-    Qs[i * KP + d] = ok ? f.q.at(b, t, h, 0, d) * f.scale : 0.f;
-    Ks[i * KP + d] = ok ? f.k.at(b, t, h, d) : 0.f;
-    const float g = ok ? f.g.at(b, t, h, d) : 0.f;
-    Gs[i * KP + d] = g;
-    Eg[i * KP + d] = expf(g);
-    Bs[i * KP + d] = ok ? f.b.at(b, t, h, d) : 0.f;
+  // Inputs of the chunk, 8 channels per load; tokens past T are zeros
+  // (naive.py:302-312). d_o is staged once as fp32 for the GEMMs below.
+  for (int e = tid; e < kC * K / 8; e += nth) {
+    const int i = e / (K / 8), d0 = 8 * (e % (K / 8)), t = t0 + i;
+    float q8[8], k8[8], g8[8], b8[8];
+    if (t < f.T) {
+      load8_any(f.q.p, f.q.dt, f.q.off(b, t, h, 0, d0), f.q.sd, q8);
+      load8_any(f.k.p, f.k.dt, f.k.off(b, t, h, d0), f.k.sd, k8);
+      load8_any(f.g.p, f.g.dt, f.g.off(b, t, h, d0), f.g.sd, g8);
+      load8_any(f.b.p, f.b.dt, f.b.off(b, t, h, d0), f.b.sd, b8);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) q8[u] = k8[u] = g8[u] = b8[u] = 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int x = i * KP + d0 + u;
+      Qs[x] = q8[u] * f.scale;
+      Ks[x] = k8[u];
+      Gs[x] = g8[u];
+      Eg[x] = expf(g8[u]);
+      Bs[x] = b8[u];
+    }
+  }
+  for (int e = tid; e < kC * V / 8; e += nth) {
+    const int i = e / (V / 8), c0 = 8 * (e % (V / 8)), t = t0 + i;
+    float o8[8];
+    if (t < f.T) {
+      load8_any(p.d_o, p.d_o_dtype, b * p.dos[0] + t * p.dos[1] + h * p.dos[2] + c0 * p.dos[3],
+                p.dos[3], o8);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o8[u] = 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) dOs[i * V + c0 + u] = o8[u];
   }
   for (int i = tid; i < kC; i += nth) mx[i] = t0 + i < f.T ? f.mix.at(b, t0 + i, h, 0) : 0.f;
   for (int k = tid; k < K; k += nth) dGl[k] = 0.f;
@@ -593,6 +658,19 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     const float* Sl = ck_level(f, bh, l, n / f.firing[l]);
     __syncthreads();
     for (int i = tid; i < kC; i += nth) mx[i] = t0 + i < f.T ? f.mix.at(b, t0 + i, h, l) : 0.f;
+    // q_l of the chunk, staged as fp32 in the spent dR_W scratch
+    for (int e = tid; e < kC * K / 8; e += nth) {
+      const int i = e / (K / 8), d0 = 8 * (e % (K / 8)), t = t0 + i;
+      float q8[8];
+      if (t < f.T) {
+        load8_any(f.q.p, f.q.dt, f.q.off(b, t, h, l, d0), f.q.sd, q8);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) q8[u] = 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) dRW[i * K + d0 + u] = q8[u];
+    }
     __syncthreads();
     block_gemm<false, true>(kC, K, V, [&](int i, int c) { return dO(i, c); },
                [&](int c, int k) { return Sl[k * V + c]; }, gsm,
@@ -602,7 +680,7 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
                        f.scale * mx[i] * a;
                });
     block_gemm(kC, V, K,
-               [&](int i, int k) { return t0 + i < f.T ? f.q.at(b, t0 + i, h, l, k) : 0.f; },
+               [&](int i, int k) { return dRW[i * K + k]; },
                [&](int k, int c) { return Sl[k * V + c]; }, gsm,
                [&](int i, int c, float a) { dRU[i * V + c] = a * dO(i, c); });
     for (int i = tid; i < kC; i += nth) {
