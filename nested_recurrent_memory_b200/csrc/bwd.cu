@@ -35,7 +35,7 @@ namespace ngdn2 {
 
 // Per-(b, h) scratch of the promotion backward, fp32, offsets in floats.
 struct PromoBwdScratch {
-  int64_t vp, keys, nrm, bg, wg, zg, z, y, dkeys, dkb, dvp, sd, dsd, gv, dgv, size;
+  int64_t vp, keys, nrm, bg, wg, zg, z, y, dkeys, dkb, dvp, sd, dsd, gv, dgv, dos, size;
   __host__ __device__ static PromoBwdScratch make(int K, int V, int NP) {
     PromoBwdScratch s;
     const int64_t mv = int64_t(NP) * V, mk = int64_t(NP) * K, kv = int64_t(K) * V;
@@ -54,7 +54,8 @@ struct PromoBwdScratch {
     s.dsd = align_floats(s.sd + kv);       // [K, V] d(e^g S)
     s.gv = align_floats(s.dsd + kv);       // [K] g
     s.dgv = align_floats(s.gv + K);        // [K] dg
-    s.size = align_floats(s.dgv + K);
+    s.dos = align_floats(s.dgv + K);       // [64, V] d_o of the current chunk, fp32
+    s.size = align_floats(s.dos + int64_t(kC) * V);
     return s;
   }
 };
@@ -129,11 +130,6 @@ __device__ __forceinline__ void load8_any(const void* base, int dt, int64_t o, i
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) out[i] = load_elem(base, o + i * sd, dt);
-}
-
-__device__ __forceinline__ float d_o_at(const BwdParams& p, int b, int t, int h, int c) {
-  if (t >= p.f.T) return 0.f;
-  return load_elem(p.d_o, b * p.dos[0] + t * p.dos[1] + h * p.dos[2] + c * p.dos[3], p.d_o_dtype);
 }
 
 __device__ __forceinline__ const float* ck_level(const FwdParams& f, int64_t bh, int level, int j) {
@@ -371,6 +367,22 @@ __global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
     const float* Kt = rec + f.rec.Kt;
     const float* eg = rec + f.rec.eg;
     const int t0 = n * kC;
+    // d_o of the chunk as fp32 (rows past T zero), for the GEMMs below.
+    float* dOs = p.pscr + bh * p.ps.size + p.ps.dos;
+    for (int e = tid; e < kC * V / 8; e += blockDim.x) {
+      const int i = e / (V / 8), c0 = 8 * (e % (V / 8)), t = t0 + i;
+      float o8[8];
+      if (t < f.T) {
+        load8_any(p.d_o, p.d_o_dtype, b * p.dos[0] + t * p.dos[1] + h * p.dos[2] + c0 * p.dos[3],
+                  p.dos[3], o8);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) o8[u] = 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) dOs[i * V + c0 + u] = o8[u];
+    }
+    __syncthreads();
     // The firings after this chunk, top level first (naive.py:394-415 reversed).
     for (int l = L - 1; l >= 1; --l)
       if ((n + 1) % f.firing[l] == 0) promote_bwd(p, b, h, l, n, gsm);
@@ -379,14 +391,14 @@ __global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
       const float* Ql = rec + f.rec.Q + int64_t(l) * kC * K;
       float* dSl = dS + int64_t(l) * K * V;
       block_gemm<true, false>(K, V, kC, [&](int k, int i) { return Ql[i * K + k]; },
-                 [&](int i, int c) { return d_o_at(p, b, t0 + i, h, c); }, gsm,
+                 [&](int i, int c) { return dOs[i * V + c]; }, gsm,
                  [&](int k, int c, float a) { dSl[k * V + c] += a; });
     }
     // Level 0: dv_new = (mix0 scale A_qk)^T dO + Kt dS0 (the S0 entering the
     // next chunk, naive.py:392), kept for the local pass with dS0 itself.
     float* dv = p.dvn + (bh * f.NT + n) * kC * V;
     block_gemm<true, false>(kC, V, kC, [&](int i, int j) { return Am[j * kC + i]; },
-                            [&](int j, int c) { return d_o_at(p, b, t0 + j, h, c); }, gsm,
+                            [&](int j, int c) { return dOs[j * V + c]; }, gsm,
                             [&](int i, int c, float a) { dv[i * V + c] = a; });
     block_gemm(kC, V, K, [&](int i, int k) { return Kt[i * K + k]; },
                [&](int k, int c) { return dS[k * V + c]; }, gsm,
@@ -397,7 +409,7 @@ __global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
     // dS0 <- e^(G_last) dS0 + (mix0 scale q e^G)^T dO - W^T dv_new
     block_gemm<true, false>(K, V, 2 * kC,
                [&](int k, int i) { return i < kC ? Q0[i * K + k] : -Wm[(i - kC) * K + k]; },
-               [&](int i, int c) { return i < kC ? d_o_at(p, b, t0 + i, h, c) : dv[(i - kC) * V + c]; },
+               [&](int i, int c) { return i < kC ? dOs[i * V + c] : dv[(i - kC) * V + c]; },
                gsm, [&](int k, int c, float a) { dS[k * V + c] = eg[k] * dS[k * V + c] + a; });
   }
   if (p.dinit)

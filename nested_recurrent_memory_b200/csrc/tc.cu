@@ -110,9 +110,6 @@ __device__ __forceinline__ void set_status(const FwdParams& p, int bits) {
 __device__ __forceinline__ float fast_sigmoid(float x) {
   return __fdividef(1.f, 1.f + __expf(fminf(-x, 80.f)));
 }
-__device__ __forceinline__ float fast_softplus(float x) {
-  return x > 20.f ? x : __logf(1.f + __expf(x));
-}
 // softplus(x) = max(x, 0) + log(1 + e^-|x|) with the hardware exponential
 // and logarithm (absolute error about 1e-7; the decay gate's values are
 // rounded to fp16 partials right after).
@@ -163,9 +160,6 @@ __device__ __forceinline__ void load8(const TokView& tv, int b, int t, int h, in
   load8_raw(tv.p, tv.dt, tv.off(b, t, h, d), tv.sd, out);
 }
 
-__device__ __forceinline__ void load8q(const QView& qv, int b, int t, int h, int l, int d, float* out) {
-  load8_raw(qv.p, qv.dt, qv.off(b, t, h, l, d), qv.sd, out);
-}
 
 // 8 consecutive 16-bit elements of a token row as their raw 16 bytes: one
 // vector load when contiguous and aligned, else element loads re-packed in
@@ -296,10 +290,6 @@ __device__ __forceinline__ int kgroup_elems(int J) {
   return (J == 0 ? 0 : J == 1 ? 2 : J == 2 ? 6 : 12) * 1024;
 }
 
-__device__ __forceinline__ void scale8(float* x, float s) {
-#pragma unroll
-  for (int u = 0; u < 8; ++u) x[u] *= s;
-}
 
 __global__ void __launch_bounds__(kPrepThreads, 2)
 prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
