@@ -218,12 +218,18 @@ namespace ngdn2 {
 namespace {
 
 // ---------------------------------------------------------------------------
-// tc_params: grid (L-1, H). Promotion operands of each (level, head) in the
-// scan's shared-memory layouts (bf16), read by bulk copies at firings.
+// tc_params: grid (L-1, H, kParamSlices). Promotion operands of each
+// (level, head) in the scan's shared-memory layouts (bf16), read by bulk
+// copies at firings. The 16-byte items of one (level, head) are spread over
+// kParamSlices CTAs: its transposed parameter reads are strided, so the
+// kernel needs many loads in flight rather than few CTAs.
 // ---------------------------------------------------------------------------
+
+constexpr int kParamSlices = 16;
 
 __global__ void __launch_bounds__(256) tc_params_kernel(FwdParams p, TcLayout lay, char* ws) {
   const int l = blockIdx.x + 1, h = blockIdx.y;
+  const int i0 = blockIdx.z * blockDim.x + threadIdx.x, di = gridDim.z * blockDim.x;
   const int64_t pidx = int64_t(l - 1) * p.H + h;
   char* base = ws + lay.ptc_off + pidx * PT_SIZE;
   bf16* qb = reinterpret_cast<bf16*>(base + PT_QB);
@@ -232,7 +238,7 @@ __global__ void __launch_bounds__(256) tc_params_kernel(FwdParams p, TcLayout la
   const int nq = p.nq[l - 1], mp = pad_pairs(nq);
   const int dt = p.param_dtype;
   // Query bank rows past n_queries are ignored (probe.py:97): zero rows.
-  for (int it = threadIdx.x; it < mp * 16; it += blockDim.x) {
+  for (int it = i0; it < mp * 16; it += di) {
     const int r = it >> 4, k0 = (it & 15) * 8;
     float x[8];
 #pragma unroll
@@ -243,7 +249,7 @@ __global__ void __launch_bounds__(256) tc_params_kernel(FwdParams p, TcLayout la
   // B operands over the reduction index v: row n < 128 of W2A is W_k[n][:]
   // (u = values . W_k^T, probe.py:99), row 128 + k is W_b[:][k]; W2B holds
   // W_w[:][n] and W_g[:][k] (probe.py:60-62).
-  for (int it = threadIdx.x; it < 256 * 16; it += blockDim.x) {
+  for (int it = i0; it < 256 * 16; it += di) {
     const int n = it >> 4, v0 = (it & 15) * 8;
     float xa[8], xb[8];
 #pragma unroll
@@ -1538,7 +1544,7 @@ cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t 
   if (stage == 0 || stage == 1) {
     if ((err = launch_convert_params(p, stream)) != cudaSuccess) return err;
     if (p.L > 1) {
-      tc_params_kernel<<<dim3(p.L - 1, p.H), 256, 0, stream>>>(p, lay, ws);
+      tc_params_kernel<<<dim3(p.L - 1, p.H, kParamSlices), 256, 0, stream>>>(p, lay, ws);
       if ((err = cudaGetLastError()) != cudaSuccess) return err;
     }
     if (p.NT > 0) {
