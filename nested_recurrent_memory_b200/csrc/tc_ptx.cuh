@@ -306,7 +306,7 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-// Tiled tensor-map load (no multicast) of one 4-D box into shared memory,
+// Tiled tensor-map load (this CTA only) of one 4-D box into shared memory,
 // completing its bytes on ``bar``. The tensor map lives in kernel parameter
 // space (__grid_constant__); the innermost coordinate is always 0 here.
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0, int c1, int c2,
