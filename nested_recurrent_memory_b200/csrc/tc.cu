@@ -358,6 +358,8 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       for (int u = 0; u < 8; ++u) G[ci][u] = 0.f;
     }
   }
+  // The first column chunk's loads, in flight together with g's.
+  fetch(0, cur);
 #pragma unroll
   for (int off = 1; off < 8; off <<= 1) {
 #pragma unroll
@@ -376,8 +378,6 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
       for (int u = 0; u < 8; ++u) carry[warp * TK + 8 * (c4 + 4 * ci) + u] = G[ci][u];
   }
   __syncthreads();
-  // The first column chunk's loads.
-  fetch(0, cur);
   if (tid < TK) {
     float run = 0.f;
 #pragma unroll
@@ -525,15 +525,20 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   float* Af = reinterpret_cast<float*>(sm + P_AF);
   bf16* Xb = reinterpret_cast<bf16*>(sm + P_XB);
   {
+    // All 64 columns of this warp in one TMEM round trip.
     const int q = warp & 3, ch = warp >> 2, j = 16 * q + lane;
+    uint32_t raw[64];
+    tmem_ld32_nowait(taddr(tb, 32 * q, 64 * ch), raw);
+    tmem_ld32_nowait(taddr(tb, 32 * q, 64 * ch + 32), raw + 32);
+    tmem_wait_ld();
+    tmem_regs_after_wait32(raw);
+    tmem_regs_after_wait32(raw + 32);
+#pragma unroll
     for (int c16 = 0; c16 < 4; ++c16) {
-      float v[16];
-      const int col0 = 64 * ch + 16 * c16;
-      tmem_ld16(taddr(tb, 32 * q, col0), v);
-      tmem_wait_ld();
+      const float* v = reinterpret_cast<const float*>(raw + 16 * c16);
       if (lane < 16) {
-        const int J = col0 >> 5;
-        if (col0 & 16) {
+        const int J = 2 * ch + (c16 >> 1);
+        if (c16 & 1) {
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const int i = 16 * J + c;
@@ -646,20 +651,28 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
     bf16* Ug = reinterpret_cast<bf16*>(rec + lay.rec.U);
     bf16* Wg = reinterpret_cast<bf16*>(rec + lay.rec.W);
     const int q = warp & 3, ch = warp >> 2, i = 16 * q + lane;
-    for (int c16 = 0; c16 < 8; ++c16) {
-      float v[16];
-      tmem_ld16(taddr(tb, 32 * q, 128 * ch + 16 * c16), v);
+    // 64 columns per TMEM round trip.
+    for (int c64 = 0; c64 < 2; ++c64) {
+      uint32_t raw[64];
+      tmem_ld32_nowait(taddr(tb, 32 * q, 128 * ch + 64 * c64), raw);
+      tmem_ld32_nowait(taddr(tb, 32 * q, 128 * ch + 64 * c64 + 32), raw + 32);
       tmem_wait_ld();
-      if (lane < 16) {
-        const int d0 = 16 * c16;
-        if (ch == 0) {
-          // 8-column pieces, rows consecutive within a piece: the scan's
-          // lane-per-row loads of one piece are then contiguous.
-          *reinterpret_cast<uint4*>(Ug + (d0 / 8) * (kC * 8) + i * 8) = pack8(v);
-          *reinterpret_cast<uint4*>(Ug + (d0 / 8 + 1) * (kC * 8) + i * 8) = pack8(v + 8);
-        } else {
-          *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0, 128)) = pack8(v);
-          *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0 + 8, 128)) = pack8(v + 8);
+      tmem_regs_after_wait32(raw);
+      tmem_regs_after_wait32(raw + 32);
+#pragma unroll
+      for (int c16 = 0; c16 < 4; ++c16) {
+        const float* v = reinterpret_cast<const float*>(raw + 16 * c16);
+        if (lane < 16) {
+          const int d0 = 64 * c64 + 16 * c16;
+          if (ch == 0) {
+            // 8-column pieces, rows consecutive within a piece: the scan's
+            // lane-per-row loads of one piece are then contiguous.
+            *reinterpret_cast<uint4*>(Ug + (d0 / 8) * (kC * 8) + i * 8) = pack8(v);
+            *reinterpret_cast<uint4*>(Ug + (d0 / 8 + 1) * (kC * 8) + i * 8) = pack8(v + 8);
+          } else {
+            *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0, 128)) = pack8(v);
+            *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0 + 8, 128)) = pack8(v + 8);
+          }
         }
       }
     }
