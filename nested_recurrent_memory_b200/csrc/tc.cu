@@ -297,8 +297,18 @@ __device__ __forceinline__ int kgroup_elems(int J) {
 }
 
 
+// Tensor maps of the prep inputs for L2 prefetches: q (level 0), g, k, b, v,
+// w, each a 3-D view [H][B * T][K] whose (K, 64, 1) box is one chunk's rows
+// of one head. ``valid`` has bit i set when map i could be made (unit
+// inner stride, batch and time collapsing into one row stride, 16-byte
+// aligned base and strides).
+struct PrepMaps {
+  CUtensorMap m[6];
+  unsigned valid;
+};
+
 __global__ void __launch_bounds__(kPrepThreads, 2)
-prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
+prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ PrepMaps maps) {
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tbase;
@@ -312,6 +322,9 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws) {
   const int t0 = n * kC;
   char* rec = ws + lay.chunks_off + ((int64_t(b) * p.H + h) * p.NT + n) * lay.rec.size;
 
+  // One L2 prefetch per input tensor of this chunk's rows: the column
+  // chunks that the loads below fetch one at a time then come from L2.
+  if (tid < 6 && (maps.valid >> tid & 1u)) tc::tma_prefetch_l2_3d(&maps.m[tid], 0, b * p.T + t0, h);
   if (warp == 0) tmem_alloc(&tbase, kPrepCols);
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -1517,17 +1530,25 @@ bool tc_supports(const ngdn2_fwd_args* a) {
 
 // Tensor map of q for the scan (see scan_tc_kernel): 4-D view whose
 // (64, 64, 2, 1) box is one chunk's [64 x 128] operand, 128-byte swizzled.
-static bool make_q_map(const FwdParams& p, CUtensorMap* m) {
-  static PFN_cuTensorMapEncodeTiled encode = nullptr;
-  if (!encode) {
+static PFN_cuTensorMapEncodeTiled g_encode = nullptr;
+
+// Looks up cuTensorMapEncodeTiled once; false when the driver lacks it.
+static bool encoder_ready() {
+  if (!g_encode) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
             cudaSuccess ||
         q != cudaDriverEntryPointSuccess || !fn)
       return false;
-    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
   }
+  return true;
+}
+
+static bool make_q_map(const FwdParams& p, CUtensorMap* m) {
+  if (!encoder_ready()) return false;
+  const auto encode = g_encode;
   // Both (head, level) layouts step from one pair to the next by K elements.
   const cuuint64_t dims[4] = {64, cuuint64_t(p.B) * p.T, TK / 64, cuuint64_t(p.H) * p.L};
   const cuuint64_t strides[3] = {cuuint64_t(p.q.st) * 2, 128, cuuint64_t(TK) * 2};
@@ -1539,6 +1560,38 @@ static bool make_q_map(const FwdParams& p, CUtensorMap* m) {
       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// The prep inputs' prefetch maps (see PrepMaps); a tensor whose layout the
+// 3-D view cannot describe (a stride-0 broadcast gate, say) is left out.
+static void make_prep_maps(const FwdParams& p, PrepMaps* pm) {
+  memset(pm, 0, sizeof(*pm));
+  if (!encoder_ready()) return;
+  struct View { const void* ptr; int dt; int64_t sb, st, sh, sd; };
+  const View views[6] = {{p.q.p, p.q.dt, p.q.sb, p.q.st, p.q.sh, p.q.sd},
+                         {p.g.p, p.g.dt, p.g.sb, p.g.st, p.g.sh, p.g.sd},
+                         {p.k.p, p.k.dt, p.k.sb, p.k.st, p.k.sh, p.k.sd},
+                         {p.b.p, p.b.dt, p.b.sb, p.b.st, p.b.sh, p.b.sd},
+                         {p.v.p, p.v.dt, p.v.sb, p.v.st, p.v.sh, p.v.sd},
+                         {p.w.p, p.w.dt, p.w.sb, p.w.st, p.w.sh, p.w.sd}};
+  for (int i = 0; i < 6; ++i) {
+    const View& v = views[i];
+    const int64_t es = v.dt == NGDN2_F32 ? 4 : 2;
+    if (v.sd != 1 || v.st <= 0 || v.sh <= 0 || v.sb != int64_t(p.T) * v.st ||
+        (v.st * es) % 16 != 0 || (v.sh * es) % 16 != 0 ||
+        (reinterpret_cast<uintptr_t>(v.ptr) & 15) != 0)
+      continue;
+    const cuuint64_t dims[3] = {cuuint64_t(TK), cuuint64_t(p.B) * p.T, cuuint64_t(p.H)};
+    const cuuint64_t strides[2] = {cuuint64_t(v.st * es), cuuint64_t(v.sh * es)};
+    const cuuint32_t box[3] = {cuuint32_t(TK), cuuint32_t(kC), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = g_encode(
+        &pm->m[i], es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 3,
+        const_cast<void*>(v.ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS) pm->valid |= 1u << i;
+  }
 }
 
 size_t tc_workspace_bytes(const FwdParams& p) { return size_t(tc_layout(p).total); }
@@ -1564,7 +1617,9 @@ cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t 
       err = cudaFuncSetAttribute(prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kPrepSmem);
       if (err != cudaSuccess) return err;
-      prep_tc_kernel<<<dim3(p.NT, p.H, p.B), kPrepThreads, kPrepSmem, stream>>>(p, lay, ws);
+      PrepMaps pm;
+      make_prep_maps(p, &pm);
+      prep_tc_kernel<<<dim3(p.NT, p.H, p.B), kPrepThreads, kPrepSmem, stream>>>(p, lay, ws, pm);
       if ((err = cudaGetLastError()) != cudaSuccess) return err;
     }
   }

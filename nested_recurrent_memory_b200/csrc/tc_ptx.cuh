@@ -306,6 +306,15 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// Hint: bring one 3-D box of a tiled tensor map into L2 (no shared memory,
+// no completion). The innermost coordinate is always 0 here.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 // Tiled tensor-map load (this CTA only) of one 4-D box into shared memory,
 // completing its bytes on ``bar``. The tensor map lives in kernel parameter
 // space (__grid_constant__); the innermost coordinate is always 0 here.
