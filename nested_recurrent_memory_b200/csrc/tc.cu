@@ -325,13 +325,6 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   // One L2 prefetch per input tensor of this chunk's rows: the column
   // chunks that the loads below fetch one at a time then come from L2.
   if (tid < 6 && (maps.valid >> tid & 1u)) tc::tma_prefetch_l2_3d(&maps.m[tid], 0, b * p.T + t0, h);
-  if (warp == 0) tmem_alloc(&tbase, kPrepCols);
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
-  if (tid < kC) mixs[0][tid] = (t0 + tid < p.T) ? p.mix.at(b, t0 + tid, h, 0) * p.scale : 0.f;
-
   // Phase A mapping: warp w owns rows 8w .. 8w+7; lane = 8 * c4 + r8 holds
   // row 8w + r8 and the 8-column chunks c4, c4 + 4, c4 + 8, c4 + 12. A warp
   // load then touches 8 rows x 64 contiguous bytes, and the 16-byte shared
@@ -361,18 +354,40 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
 
   // A1. G = cumsum of g along the chunk (naive.py:329): a scan over the 8
   //     rows of each warp, then the carries of the row blocks above.
+  //     Every global load of this phase (g, the first column chunk of the
+  //     other inputs, mix_0) is issued as raw bits before anything waits on
+  //     one, and TMEM and the mbarrier are set up while they are in flight.
   float G[4][8];
+  uint4 graw[4];
+  const bool g16 = p.g.dt != NGDN2_F32;
 #pragma unroll
   for (int ci = 0; ci < 4; ++ci) {
     const int d0 = 8 * (c4 + 4 * ci);
-    if (valid) load8(p.g, b, t, h, d0, G[ci]);
-    else {
+    if (g16) {
+      graw[ci] = valid ? raw8_at(p.g.p, p.g.dt, p.g.off(b, t, h, d0), p.g.sd) : make_uint4(0, 0, 0, 0);
+    } else if (valid) {
+      load8(p.g, b, t, h, d0, G[ci]);
+    } else {
 #pragma unroll
       for (int u = 0; u < 8; ++u) G[ci][u] = 0.f;
     }
   }
-  // The first column chunk's loads, in flight together with g's.
   fetch(0, cur);
+  uint32_t mix_bits = 0;
+  if (tid < kC && t0 + tid < p.T) {
+    const int64_t o = p.mix.off(b, t0 + tid, h, 0);
+    mix_bits = p.mix.dt == NGDN2_F32 ? __float_as_uint(reinterpret_cast<const float*>(p.mix.p)[o])
+                                     : uint32_t(reinterpret_cast<const uint16_t*>(p.mix.p)[o]);
+  }
+  if (warp == 0) tmem_alloc(&tbase, kPrepCols);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (g16) {
+#pragma unroll
+    for (int ci = 0; ci < 4; ++ci) unpack8(graw[ci], p.g.dt, G[ci]);
+  }
 #pragma unroll
   for (int off = 1; off < 8; off <<= 1) {
 #pragma unroll
@@ -389,6 +404,12 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
     for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
       for (int u = 0; u < 8; ++u) carry[warp * TK + 8 * (c4 + 4 * ci) + u] = G[ci][u];
+  }
+  if (tid < kC) {
+    const float m0 = p.mix.dt == NGDN2_F32   ? __uint_as_float(mix_bits)
+                     : p.mix.dt == NGDN2_BF16 ? __uint_as_float(mix_bits << 16)
+                                              : __half2float(__ushort_as_half(uint16_t(mix_bits)));
+    mixs[0][tid] = m0 * p.scale;
   }
   __syncthreads();
   if (tid < TK) {
@@ -577,8 +598,9 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   // D. (I + A_kk)^-1 in fp32 by 2x2 block recursion (for unit lower
   //    triangular [[L11, 0], [L21, L22]], X21 = -X22 L21 X11): 16x16
   //    diagonal blocks by forward substitution, then the 16-row off-diagonal
-  //    blocks of both 32x32 halves, then the 32-row block of the whole. Only
-  //    the lower triangle of Xf is ever read; blocks above it hold garbage.
+  //    blocks of both 32x32 halves, then the 32-row block of the whole. Both
+  //    32x32 diagonal halves of Xf are written in full (zeros above the
+  //    diagonal); its upper-right 32x32 block is never read.
   float* Xf = reinterpret_cast<float*>(sm + P_XF);
   if (tid < 64) {
     const int o = 16 * (tid >> 4), c = tid & 15;
@@ -592,6 +614,13 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
     }
 #pragma unroll
     for (int rr = 0; rr < 16; ++rr) Xf[(o + rr) * XS + o + c] = x[rr];
+  } else {
+    // The upper off-diagonal 16x16 block of each 32x32 half: read, as the
+    // zeros of a lower-triangular matrix, by the unrolled 64-level products.
+    for (int e = tid - 64; e < 2 * 256; e += kPrepThreads - 64) {
+      const int half = e >> 8, rr = (e >> 4) & 15, c = e & 15;
+      Xf[(32 * half + rr) * XS + 32 * half + 16 + c] = 0.f;
+    }
   }
   __syncthreads();
   auto fma4 = [](float a, const float4& x, float4& acc) {
@@ -614,26 +643,32 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
     }
     __syncthreads();
     if (tid < 128) {
+      // X22's strict upper triangle holds exact zeros: a fixed trip count
+      // adds only zeros and lets every load issue up front.
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int m = 0; m <= rr; ++m)
+#pragma unroll
+      for (int m = 0; m < 16; ++m)
         fma4(Xf[(r0 + rr) * XS + r0 + m], *reinterpret_cast<const float4*>(&Tt[hh * 256 + m * 16 + cq]), acc);
       *reinterpret_cast<float4*>(&Xf[(r0 + rr) * XS + k0 + cq]) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     }
     __syncthreads();
   }
-  // 64-level: T = A[32.., 0..31] X_A (X_A lower triangular, so k >= column),
-  // then X[32.., 0..31] = -X_B T (X_B lower triangular); 32x32 each, a
-  // thread owns 4 columns of one row (256 threads).
+  // 64-level: T = A[32.., 0..31] X_A, then X[32.., 0..31] = -X_B T; 32x32
+  // each, a thread owns 4 columns of one row (256 threads). X_A and X_B are
+  // fully written lower triangles with exact zeros above the diagonal, so
+  // the fixed, unrolled trip counts add only zeros.
   {
     const int rr = tid >> 3, cq = (tid & 7) * 4;
     constexpr int TS = 36;  // row stride (floats) of T
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = cq; k < 32; ++k)
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
       fma4(Af[(32 + rr) * 65 + k], *reinterpret_cast<const float4*>(&Xf[k * XS + cq]), acc);
     *reinterpret_cast<float4*>(&Tt[rr * TS + cq]) = acc;
     __syncthreads();
     acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int m = 0; m <= rr; ++m)
+#pragma unroll
+    for (int m = 0; m < 32; ++m)
       fma4(Xf[(32 + rr) * XS + 32 + m], *reinterpret_cast<const float4*>(&Tt[m * TS + cq]), acc);
     *reinterpret_cast<float4*>(&Xf[(32 + rr) * XS + cq]) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     __syncthreads();
