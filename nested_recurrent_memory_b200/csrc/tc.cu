@@ -654,23 +654,60 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
     __syncthreads();
   }
   // 64-level: T = A[32.., 0..31] X_A, then X[32.., 0..31] = -X_B T; 32x32
-  // each, a thread owns 4 columns of one row (256 threads). X_A and X_B are
-  // fully written lower triangles with exact zeros above the diagonal, so
-  // the fixed, unrolled trip counts add only zeros.
+  // each. X_A and X_B are fully written lower triangles with exact zeros
+  // above the diagonal, so full-length products add only zeros. A thread
+  // owns a 4 x 4 block (rows r4 .. r4 + 3, columns cq .. cq + 3) over one
+  // quarter kq of the reduction index, and the quarters are summed by two
+  // butterfly rounds that leave lane kq with row r4 + kq. Each quarter-warp
+  // shares kq, so its 16-byte loads cover one contiguous 128-byte row
+  // segment; the 4 x 4 blocking reads each loaded value four times, which
+  // matters because the shared-memory pipe is this kernel's busiest unit.
   {
-    const int rr = tid >> 3, cq = (tid & 7) * 4;
     constexpr int TS = 36;  // row stride (floats) of T
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int cq = (tid & 7) * 4, kq = (tid >> 3) & 3, r4 = (tid >> 5) * 4;
+    const int b0 = kq & 1, b1 = kq >> 1;
+    // Sum of the four quarters' partial rows; returns row r4 + kq.
+    auto reduce = [&](float4* acc) {
+      float4 kept[2];
 #pragma unroll
-    for (int k = 0; k < 32; ++k)
-      fma4(Af[(32 + rr) * 65 + k], *reinterpret_cast<const float4*>(&Xf[k * XS + cq]), acc);
-    *reinterpret_cast<float4*>(&Tt[rr * TS + cq]) = acc;
+      for (int j = 0; j < 2; ++j) {
+        const float4 mine = b0 ? acc[2 * j + 1] : acc[2 * j];
+        const float4 send = b0 ? acc[2 * j] : acc[2 * j + 1];
+        kept[j] = make_float4(mine.x + __shfl_xor_sync(0xffffffffu, send.x, 8),
+                              mine.y + __shfl_xor_sync(0xffffffffu, send.y, 8),
+                              mine.z + __shfl_xor_sync(0xffffffffu, send.z, 8),
+                              mine.w + __shfl_xor_sync(0xffffffffu, send.w, 8));
+      }
+      const float4 mine = b1 ? kept[1] : kept[0];
+      const float4 send = b1 ? kept[0] : kept[1];
+      return make_float4(mine.x + __shfl_xor_sync(0xffffffffu, send.x, 16),
+                         mine.y + __shfl_xor_sync(0xffffffffu, send.y, 16),
+                         mine.z + __shfl_xor_sync(0xffffffffu, send.z, 16),
+                         mine.w + __shfl_xor_sync(0xffffffffu, send.w, 16));
+    };
+    float4 acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int k = 8 * kq + kk;
+      const float4 x = *reinterpret_cast<const float4*>(&Xf[k * XS + cq]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) fma4(Af[(32 + r4 + i) * 65 + k], x, acc[i]);
+    }
+    *reinterpret_cast<float4*>(&Tt[(r4 + kq) * TS + cq]) = reduce(acc);
     __syncthreads();
-    acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int m = 0; m < 32; ++m)
-      fma4(Xf[(32 + rr) * XS + 32 + m], *reinterpret_cast<const float4*>(&Tt[m * TS + cq]), acc);
-    *reinterpret_cast<float4*>(&Xf[(32 + rr) * XS + cq]) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
+    for (int i = 0; i < 4; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int mm = 0; mm < 8; ++mm) {
+      const int m = 8 * kq + mm;
+      const float4 x = *reinterpret_cast<const float4*>(&Tt[m * TS + cq]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) fma4(Xf[(32 + r4 + i) * XS + 32 + m], x, acc[i]);
+    }
+    const float4 x21 = reduce(acc);
+    *reinterpret_cast<float4*>(&Xf[(32 + r4 + kq) * XS + cq]) = make_float4(-x21.x, -x21.y, -x21.z, -x21.w);
     __syncthreads();
   }
   for (int it = tid; it < kC * 8; it += kPrepThreads) {
