@@ -710,11 +710,18 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
     *reinterpret_cast<float4*>(&Xf[(32 + r4 + kq) * XS + cq]) = make_float4(-x21.x, -x21.y, -x21.z, -x21.w);
     __syncthreads();
   }
+  // The inverse as a bf16 K-major tile: eight consecutive lanes take the
+  // eight rows of one core matrix, so each quarter-warp reads 16 bytes from
+  // eight rows in distinct banks (row stride 68 floats) and writes one
+  // contiguous 128-byte core matrix.
   for (int it = tid; it < kC * 8; it += kPrepThreads) {
-    const int i = it >> 3, j0 = (it & 7) * 8;
+    const int i = 8 * (it >> 6) + (it & 7), j0 = ((it >> 3) & 7) * 8;
+    const float4 a0 = *reinterpret_cast<const float4*>(&Xf[i * XS + j0]);
+    const float4 a1 = *reinterpret_cast<const float4*>(&Xf[i * XS + j0 + 4]);
+    const float raw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     float x[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) x[u] = (j0 + u <= i) ? Xf[i * XS + j0 + u] : 0.f;
+    for (int u = 0; u < 8; ++u) x[u] = (j0 + u <= i) ? raw[u] : 0.f;
     *reinterpret_cast<uint4*>(Xb + kmajor_off(i, j0, 64)) = pack8(x);
   }
   fence_proxy_async();
