@@ -325,6 +325,18 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   // One L2 prefetch per input tensor of this chunk's rows: the column
   // chunks that the loads below fetch one at a time then come from L2.
   if (tid < 6 && (maps.valid >> tid & 1u)) tc::tma_prefetch_l2_3d(&maps.m[tid], 0, b * p.T + t0, h);
+  // g is the first input the kernel waits on. Blocks start in index order as
+  // slots free up, so the block two waves ahead (this index + two CTAs per
+  // SM) takes this slot about one CTA lifetime from now: its g rows are
+  // pulled into L2 as well, so that its first wait sees L2 latency.
+  if (tid == 32 && (maps.valid & 2u)) {
+    uint32_t nsm;
+    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+    const int64_t lin2 = n + int64_t(p.NT) * (h + int64_t(p.H) * b) + 2 * int64_t(nsm);
+    const int64_t b2 = lin2 / (int64_t(p.NT) * p.H);
+    if (b2 < p.B)
+      tc::tma_prefetch_l2_3d(&maps.m[1], 0, int(b2 * p.T + (lin2 % p.NT) * kC), int(lin2 / p.NT % p.H));
+  }
   // Phase A mapping: warp w owns rows 8w .. 8w+7; lane = 8 * c4 + r8 holds
   // row 8w + r8 and the 8-column chunks c4, c4 + 4, c4 + 8, c4 + 12. A warp
   // load then touches 8 rows x 64 contiguous bytes, and the 16-byte shared
