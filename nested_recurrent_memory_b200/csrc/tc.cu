@@ -554,9 +554,13 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   __syncthreads();
   fence_after_sync();
 
-  // B. MMA1: D[j, 32J + c] = K^(J)[j] . [Q_J ; BK_J][c], M=64, N=32, K=128.
+  // B. MMA1: D[j, 32J + c] = K^(J)[j] . [Q_J ; BK_J][c], N=32, K=128. Issued
+  //    as M=128 (same tensor-pipe time as M=64): A rows 64..127 read the
+  //    shared memory after the tile and land in TMEM lanes 64..127, which
+  //    nothing reads, while rows 0..63 fill lanes 0..63 densely, so the
+  //    read-outs below move no idle lanes.
   if (tid == 0) {
-    const uint32_t id = idesc_f16(64, 32, true, false, false);
+    const uint32_t id = idesc_f16(128, 32, true, false, false);
     for (int J = 0; J < 4; ++J)
       mma_tile(tb + 32 * J, smem_u32(KG + kgroup_elems(J)), smem_u32(QB + J * 32 * 128), 128, id,
                false);
@@ -570,9 +574,10 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   //    bf16 tile and copied to the record with 16-byte stores.
   float* Af = reinterpret_cast<float*>(sm + P_AF);
   bf16* Xb = reinterpret_cast<bf16*>(sm + P_XB);
-  {
-    // All 64 columns of this warp in one TMEM round trip.
-    const int q = warp & 3, ch = warp >> 2, j = 16 * q + lane;
+  if ((warp & 3) < 2) {
+    // Warps 0, 1, 4, 5 own TMEM lanes 0..63 (row j = 32q + lane); all 64
+    // columns of a warp in one TMEM round trip.
+    const int q = warp & 3, ch = warp >> 2, j = 32 * q + lane;
     uint32_t raw[64];
     tmem_ld32_nowait(taddr(tb, 32 * q, 64 * ch), raw);
     tmem_ld32_nowait(taddr(tb, 32 * q, 64 * ch + 32), raw + 32);
@@ -582,20 +587,18 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
 #pragma unroll
     for (int c16 = 0; c16 < 4; ++c16) {
       const float* v = reinterpret_cast<const float*>(raw + 16 * c16);
-      if (lane < 16) {
-        const int J = 2 * ch + (c16 >> 1);
-        if (c16 & 1) {
+      const int J = 2 * ch + (c16 >> 1);
+      if (c16 & 1) {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int i = 16 * J + c;
-            Af[i * 65 + j] = (j < i) ? v[c] : 0.f;
-          }
-        } else {
+        for (int c = 0; c < 16; ++c) {
+          const int i = 16 * J + c;
+          Af[i * 65 + j] = (j < i) ? v[c] : 0.f;
+        }
+      } else {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int i = 16 * J + c;
-            Xb[kmajor_off(i, j, 64)] = __float2bfloat16_rn(j <= i ? v[c] * mixs[0][i] : 0.f);
-          }
+        for (int c = 0; c < 16; ++c) {
+          const int i = 16 * J + c;
+          Xb[kmajor_off(i, j, 64)] = __float2bfloat16_rn(j <= i ? v[c] * mixs[0][i] : 0.f);
         }
       }
     }
@@ -743,7 +746,9 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
 
   // E. MMA2: [U | W] = X . R, M=64, N=256, K=64 (naive.py:346-351).
   if (tid == 0) {
-    mma_tile(tb, smem_u32(Xb), smem_u32(Rs), 64, idesc_f16(64, 256, true, false, true), false);
+    // M=128 for the same reason as MMA1 (A rows 64..127 are the shared
+    // memory after the inverse tile; their TMEM lanes are never read).
+    mma_tile(tb, smem_u32(Xb), smem_u32(Rs), 64, idesc_f16(128, 256, true, false, true), false);
     mma_commit(&bar);
   }
   __syncwarp();
@@ -754,9 +759,10 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   {
     bf16* Ug = reinterpret_cast<bf16*>(rec + lay.rec.U);
     bf16* Wg = reinterpret_cast<bf16*>(rec + lay.rec.W);
-    const int q = warp & 3, ch = warp >> 2, i = 16 * q + lane;
-    // 64 columns per TMEM round trip.
-    for (int c64 = 0; c64 < 2; ++c64) {
+    // Warps 0, 1, 4, 5 own TMEM lanes 0..63 (row i = 32q + lane); 64
+    // columns per TMEM round trip.
+    const int q = warp & 3, ch = warp >> 2, i = 32 * q + lane;
+    for (int c64 = 0; c64 < 2 && q < 2; ++c64) {
       uint32_t raw[64];
       tmem_ld32_nowait(taddr(tb, 32 * q, 128 * ch + 64 * c64), raw);
       tmem_ld32_nowait(taddr(tb, 32 * q, 128 * ch + 64 * c64 + 32), raw + 32);
@@ -766,17 +772,15 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
 #pragma unroll
       for (int c16 = 0; c16 < 4; ++c16) {
         const float* v = reinterpret_cast<const float*>(raw + 16 * c16);
-        if (lane < 16) {
-          const int d0 = 64 * c64 + 16 * c16;
-          if (ch == 0) {
-            // 8-column pieces, rows consecutive within a piece: the scan's
-            // lane-per-row loads of one piece are then contiguous.
-            *reinterpret_cast<uint4*>(Ug + (d0 / 8) * (kC * 8) + i * 8) = pack8(v);
-            *reinterpret_cast<uint4*>(Ug + (d0 / 8 + 1) * (kC * 8) + i * 8) = pack8(v + 8);
-          } else {
-            *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0, 128)) = pack8(v);
-            *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0 + 8, 128)) = pack8(v + 8);
-          }
+        const int d0 = 64 * c64 + 16 * c16;
+        if (ch == 0) {
+          // 8-column pieces, rows consecutive within a piece: the scan's
+          // lane-per-row loads of one piece are then contiguous.
+          *reinterpret_cast<uint4*>(Ug + (d0 / 8) * (kC * 8) + i * 8) = pack8(v);
+          *reinterpret_cast<uint4*>(Ug + (d0 / 8 + 1) * (kC * 8) + i * 8) = pack8(v + 8);
+        } else {
+          *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0, 128)) = pack8(v);
+          *reinterpret_cast<uint4*>(Wg + kmajor_off(i, d0 + 8, 128)) = pack8(v + 8);
         }
       }
     }
