@@ -595,10 +595,23 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
           Af[i * 65 + j] = (j < i) ? v[c] : 0.f;
         }
       } else {
+        // Lanes j and j ^ 1 pair up: the even lane writes rows 16J + 2m and
+        // the odd lane rows 16J + 2m + 1, each as one 4-byte (j, j + 1)
+        // bf16 pair, so a store instruction covers two rows of each core
+        // matrix it touches instead of one 2-byte column element.
+        const bool odd = lane & 1;
+        const int j0 = j & ~1;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int i = 16 * J + c;
-          Xb[kmajor_off(i, j, 64)] = __float2bfloat16_rn(j <= i ? v[c] * mixs[0][i] : 0.f);
+        for (int m = 0; m < 8; ++m) {
+          const int ie = 16 * J + 2 * m, io = ie + 1;
+          const float ae = j <= ie ? v[2 * m] * mixs[0][ie] : 0.f;
+          const float ao = j <= io ? v[2 * m + 1] * mixs[0][io] : 0.f;
+          // Each lane keeps its own row's value and receives the partner's.
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? ae : ao, 1);
+          const int i = odd ? io : ie;
+          const __nv_bfloat162 pr = odd ? __floats2bfloat162_rn(other, ao)
+                                        : __floats2bfloat162_rn(ae, other);
+          *reinterpret_cast<__nv_bfloat162*>(Xb + kmajor_off(i, j0, 64)) = pr;
         }
       }
     }
