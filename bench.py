@@ -44,7 +44,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", default="config1")
@@ -99,25 +99,80 @@ def alg_counts(w):
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
+    """SM clocks and clock-event reasons of one GPU during the timed region.
+
+    NVML is polled every ~2 ms from a background thread; only samples taken
+    between ``begin()`` and ``end()`` (which bracket the timed region on the
+    host, whose final synchronize waits out the device work) count. Without
+    NVML, ``nvidia-smi -lms 20`` is read instead."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    # NVML clock-event reason bits of the four reasons above.
+    BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+            "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
         self.gpu_index = gpu_index
         self.proc = None
+        self.handle = None
+        self.samples = []
+        self.window = False
 
     def start(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu_index)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            gi = str(self.gpu_index)
+            self.handle = (pynvml.nvmlDeviceGetHandleByUUID(gi) if gi.startswith(("GPU-", "MIG-"))
+                           else pynvml.nvmlDeviceGetHandleByIndex(int(gi)))
+            self.nvml = pynvml
+        except Exception:
+            self.handle = None
+        if self.handle is None:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "20", "-i", str(self.gpu_index)],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                self.proc = None
+            return
+        self.stop_flag = threading.Event()
+        self.thread = threading.Thread(target=self._poll, daemon=True)
+        self.thread.start()
+
+    def _poll(self):
+        nv, h = self.nvml, self.handle
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop_flag.is_set():
+            if self.window:
+                try:
+                    self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx,
+                                         nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                except Exception:
+                    pass
+            time.sleep(0.002)
+
+    def begin(self):
+        self.window = True
+
+    def end(self):
+        self.window = False
 
     def stop(self):
+        if self.handle is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            reasons = {name for name, bit in self.BITS.items()
+                       if any(r & bit for _, _, r in self.samples)}
+            return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
+                    "sm_max_mhz": max(m for _, m, _ in self.samples),
+                    "samples": len(self.samples), "reasons": sorted(reasons), "source": "nvml"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -142,7 +197,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "samples": len(sm), "reasons": sorted(reasons), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
@@ -290,11 +345,13 @@ def run_ours(args, w):
     time.sleep(0.3)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    clocks.begin()
     start.record()
     for _ in range(args.steps):
         call.launch()
     end.record()
     barrier()
+    clocks.end()
     clk = clocks.stop()
     ms_max = max_over_ranks(start.elapsed_time(end), world, dev)
     ms_step = ms_max / args.steps
@@ -379,24 +436,47 @@ def run_ours(args, w):
     token_heads = w["B"] * w["T"] * w["H"]
     alg_bytes = bytes_th * token_heads
     alg_flops = flop_th * token_heads
-    achieved_gbs = alg_bytes / (ms_step / 1e3) / 1e9
+    # The algorithmic bytes split by the kernel that moves them: prep reads
+    # q's level-0 slice, k, v, g, b, w and mix; the scan reads the upper
+    # levels' queries and the weights and writes o and the final states.
+    s_el = 2 if str(w["dtype"]).endswith(("bfloat16", "float16")) else 4
+    prep_bytes = s_el * (4 * w["K"] + 2 * w["V"] + w["L"]) * token_heads
+    kernel_bytes = {1: prep_bytes, 2: alg_bytes - prep_bytes}
     traffic = None
+    kernel_traffic = {1: None, 2: None}
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         tj = json.loads(tfile.read_text())
         key = f"{args.config}:{call.path}"
         if key in tj:
             traffic = tj[key]["dram_bytes_per_token_head"] * token_heads
+            per = tj[key].get("per_kernel_dram_bytes_per_token_head", {})
+            for st, name in ((1, "prep_tc_kernel"), (2, "scan_tc_kernel")):
+                if name in per:
+                    kernel_traffic[st] = per[name] * token_heads
     dominant = max(stage_ms, key=stage_ms.get)
+    dom_name = {1: "prep_tc_kernel" if call.path == "tc" else "prep_simt_kernel",
+                2: "scan_tc_kernel" if call.path == "tc" else "scan_simt_kernel"}[dominant]
+    dom_gbs = kernel_bytes[dominant] / (stage_ms[dominant] / 1e3) / 1e9
+    whole_gbs = alg_bytes / (ms_step / 1e3) / 1e9
     roofline = {
-        "bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-        "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
+        "bound": "hbm", "kernel": dom_name, "achieved": dom_gbs, "peak": peaks["hbm_gbs"],
+        "unit": "GB/s", "frac": dom_gbs / peaks["hbm_gbs"], "traffic": kernel_traffic[dominant],
         "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
-        "scope": "whole forward (prep + scan); algorithmic bytes = inputs + o + final state + weights",
-        "alg_bytes_per_launch": alg_bytes,
+        "scope": ("dominant kernel; algorithmic bytes = the op's inputs it reads (prep: q level 0, "
+                  "k, v, g, b, w, mix) or the rest of the op's bytes (scan); time = its stage's "
+                  "CUDA events on the launching stream (prep's stage includes the two small "
+                  "parameter-layout kernels); traffic = its ncu DRAM bytes per launch"),
+        "alg_bytes_per_launch": kernel_bytes[dominant],
+        "whole_forward": {"achieved": whole_gbs, "frac": whole_gbs / peaks["hbm_gbs"],
+                          "traffic": traffic, "alg_bytes_per_launch": alg_bytes,
+                          "scope": "prep + scan; algorithmic bytes = inputs + o + final state + weights"},
         "tensor_tflops": alg_flops / (ms_step / 1e3) / 1e12,
         "tensor_frac_of_bf16_peak": alg_flops / (ms_step / 1e3) / 1e12 / peaks["bf16_tflops"],
         "kernels": {"prep_ms": stage_ms[1], "scan_ms": stage_ms[2],
+                    "prep_alg_bytes": kernel_bytes[1], "scan_alg_bytes": kernel_bytes[2],
+                    "prep_frac": kernel_bytes[1] / (stage_ms[1] / 1e3) / 1e9 / peaks["hbm_gbs"],
+                    "scan_frac": kernel_bytes[2] / (stage_ms[2] / 1e3) / 1e9 / peaks["hbm_gbs"],
                     "dominant": "prep" if dominant == 1 else "scan",
                     "dominant_share": stage_ms[dominant] / max(sum(stage_ms.values()), 1e-9)},
     }
