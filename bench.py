@@ -129,6 +129,10 @@ class ClockSampler:
             self.handle = (pynvml.nvmlDeviceGetHandleByUUID(gi) if gi.startswith(("GPU-", "MIG-"))
                            else pynvml.nvmlDeviceGetHandleByIndex(int(gi)))
             self.nvml = pynvml
+            # The first queries can be slow: make them here, before the window.
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
         except Exception:
             self.handle = None
         if self.handle is None:
@@ -145,8 +149,7 @@ class ClockSampler:
         self.thread.start()
 
     def _poll(self):
-        nv, h = self.nvml, self.handle
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        nv, h, mx = self.nvml, self.handle, self.max_mhz
         while not self.stop_flag.is_set():
             if self.window:
                 try:
