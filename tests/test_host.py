@@ -85,3 +85,11 @@ def test_config_recipe():
     assert torch.count_nonzero(inp["b_projections"]) == 0
     again = config_inputs(B, 128, H, K, V, L, m, firing, dtype=dtype)
     assert torch.equal(inp["v"], again["v"])
+
+
+def test_host_pipeline_rejects_pageable_inputs_before_touching_cuda():
+    """HostPipeline only takes pinned host batches (its copies are
+    asynchronous); a pageable tensor is refused at construction."""
+    from nested_recurrent_memory_b200 import HostPipeline
+    with pytest.raises(ValueError, match="pinned"):
+        HostPipeline({"q": torch.zeros(1, 64, 1, 2, 16)}, L=2)
