@@ -1704,8 +1704,15 @@ static void make_prep_maps(const FwdParams& p, PrepMaps* pm) {
 
 size_t tc_workspace_bytes(const FwdParams& p) { return size_t(tc_layout(p).total); }
 
+// The fp32 parameter copy feeds only the CUDA-core promotion, which the
+// tensor-core scan runs for the merge arm; learned promotions read the bf16
+// layouts of tc_params.
+static bool tc_needs_params32(const FwdParams& p) {
+  return p.L > 1 && p.promotion == NGDN2_PROMOTION_MERGE;
+}
+
 int num_launches_tc(const FwdParams& p) {
-  return (p.L > 1 ? 2 : 0) + (p.NT > 0 ? 1 : 0) + 1;
+  return (tc_needs_params32(p) ? 1 : 0) + (p.L > 1 ? 1 : 0) + (p.NT > 0 ? 1 : 0) + 1;
 }
 
 cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t stream) {
@@ -1716,7 +1723,7 @@ cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t 
   p.chunks = nullptr;
   cudaError_t err;
   if (stage == 0 || stage == 1) {
-    if ((err = launch_convert_params(p, stream)) != cudaSuccess) return err;
+    if (tc_needs_params32(p) && (err = launch_convert_params(p, stream)) != cudaSuccess) return err;
     if (p.L > 1) {
       tc_params_kernel<<<dim3(p.L - 1, p.H, kParamSlices), 256, 0, stream>>>(p, lay, ws);
       if ((err = cudaGetLastError()) != cudaSuccess) return err;
