@@ -11,8 +11,9 @@ firing every 1/4/16 chunks, m=64, bf16 inputs, fp32 state). Under torchrun
 (weak scaling; the path shards by (batch, head) and needs no collective);
 times are CUDA-event times, max over ranks.
 
-Rank 0 prints one JSON line. ``value`` is whole-job tokens/s with inputs
-resident in HBM; ``e2e`` is the same metric through the public API with
+Rank 0 prints one JSON line. ``value`` is whole-job tokens/s (all GPUs)
+with inputs resident in HBM, ``value_per_gpu`` the same divided by the GPU
+count (the metric's "/GPU" figure); ``e2e`` is the same metric through the public API with
 host (pinned) inputs copied in and o / final state copied out every step.
 ``roofline`` relates the forward to HBM bandwidth (the bound of this path),
 ``cpu_baseline`` is the CPU oracle (numpy restatement of the reference's
@@ -496,7 +497,8 @@ def run_ours(args, w):
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC, "value": value, "unit": "tokens/s (whole job, all GPUs)",
+            "value_per_gpu": value / world, "unit_per_gpu": "tokens/s/GPU", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16" if "bfloat16" in str(w["dtype"]) else str(w["dtype"]).replace("torch.", ""),

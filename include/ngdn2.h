@@ -40,7 +40,7 @@ extern "C" {
 #define NGDN2_API
 #endif
 
-#define NGDN2_ABI_VERSION 1
+#define NGDN2_ABI_VERSION 2
 #define NGDN2_MAX_LEVELS 8
 #define NGDN2_CHUNK 64
 
@@ -124,11 +124,27 @@ typedef struct ngdn2_fwd_args {
   void* workspace;              /* device scratch, >= ngdn2_fwd_workspace_size */
   size_t workspace_bytes;
   int32_t* status;              /* optional device word; kernels OR in NGDN2_STATUS_* */
+
+  /* Optional start gate: a device-visible word (device memory or mapped
+   * pinned host memory) that a producer sets nonzero once the inputs are in
+   * place. When non-NULL, the forward's first kernel polls it at most
+   * gate_polls times (0 means 2^24) before any other work; if it is still
+   * zero, NGDN2_STATUS_GATE_TIMEOUT is set in *status (status must then be
+   * non-NULL) and every kernel of this forward returns without touching the
+   * outputs. Lets a caller enqueue the forward before a host or peer
+   * producer has finished writing its inputs, with a bounded wait instead
+   * of a hang. */
+  const volatile int32_t* gate;
+  uint32_t gate_polls;
 } ngdn2_fwd_args;
 
-/* Device status bits (written to ngdn2_fwd_args.status when non-NULL). */
+/* Device status bits (written to ngdn2_fwd_args.status when non-NULL). The
+ * word is sticky: kernels only OR bits in; the caller clears it. */
 enum {
-  NGDN2_STATUS_WAIT_TIMEOUT = 1  /* a bounded pipeline wait gave up */
+  NGDN2_STATUS_WAIT_TIMEOUT = 1, /* a bounded pipeline wait gave up: outputs are not valid, and
+                                    the CUDA context should be treated as suspect (an MMA or copy
+                                    the wait was for may still have been in flight) */
+  NGDN2_STATUS_GATE_TIMEOUT = 2  /* the start gate stayed zero: nothing was computed */
 };
 
 /* Arguments of ngdn2_update_state (update_fwd.py:131-204). */
@@ -313,7 +329,10 @@ NGDN2_API int ngdn2_step(const ngdn2_step_args* args, void* stream);
  * on every GPU that loads it until exit. Calls needing more scratch than
  * that return NGDN2_ERR_WORKSPACE. All calls on a device share the buffer,
  * so calls that overlap on the GPU race; the first call on each device
- * looks the buffer up and should come before any stream capture. */
+ * looks the buffer up and should come before any stream capture. The looked-up
+ * address is cached for the life of the process: after cudaDeviceReset (or
+ * any teardown of the device's primary context) this entry point must not be
+ * called again in that process. */
 NGDN2_API int ngdn2_fwd_noalloc(const ngdn2_fwd_args* args, void* stream);
 
 #ifdef __cplusplus

@@ -10,6 +10,8 @@ runs the op over host-resident batches with their copies overlapped.
 
 from .ops import (  # noqa: F401
     FwdCall,
+    KernelStatusError,
+    check_status,
     chunk_nested_gdn2,
     chunk_nested_gdn2_bwd,
     chunk_nested_gdn2_fwd,

@@ -15,7 +15,7 @@ import pathlib
 HERE = pathlib.Path(__file__).resolve().parent
 LIB_PATH = HERE / "libngdn2.so"
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_LEVELS = 8
 CHUNK = 64
 
@@ -30,6 +30,9 @@ ERR_BLOCK_V = -3
 ERR_DIVISIBLE = -4
 ERR_UNIT_STRIDE = -5
 ERR_INCONSISTENT = -6
+
+STATUS_WAIT_TIMEOUT = 1
+STATUS_GATE_TIMEOUT = 2
 
 c_i32, c_i64, c_ptr = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
 
@@ -51,6 +54,7 @@ class FwdArgs(ctypes.Structure):
         ("w_projections", c_ptr), ("g_projections", c_ptr),
         ("initial_state", c_ptr), ("o", c_ptr), ("final_state", c_ptr),
         ("workspace", c_ptr), ("workspace_bytes", ctypes.c_size_t), ("status", c_ptr),
+        ("gate", c_ptr), ("gate_polls", ctypes.c_uint32),
     ]
 
 

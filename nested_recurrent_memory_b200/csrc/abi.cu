@@ -56,7 +56,21 @@ int validate_fwd(const ngdn2_fwd_args* a, bool outputs = true) {
   if (a->L > 1 && (!a->query_banks || !a->key_projections || !a->b_projections ||
                    !a->w_projections || !a->g_projections))
     return NGDN2_ERR_NULL;
+  if (a->gate && !a->status) return NGDN2_ERR_NULL;
   return NGDN2_OK;
+}
+
+// The start gate (ngdn2_fwd_args.gate): one thread polls the word, sleeping
+// briefly between polls, and gives up after ``polls`` polls (0: 2^24, about
+// a second), setting NGDN2_STATUS_GATE_TIMEOUT; every later kernel of the
+// forward then returns at once (gate_closed).
+__global__ void gate_kernel(const volatile int32_t* gate, uint32_t polls, int32_t* status) {
+  const uint32_t n = polls ? polls : (1u << 24);
+  for (uint32_t i = 0; i < n; ++i) {
+    if (*gate != 0) return;
+    __nanosleep(64);
+  }
+  atomicOr(status, NGDN2_STATUS_GATE_TIMEOUT);
 }
 
 void fill_params(const ngdn2_fwd_args* a, FwdParams* p) {
@@ -165,7 +179,7 @@ int ngdn2_fwd_num_launches(const ngdn2_fwd_args* a) {
   if (path < 0) return path;
   FwdParams p;
   fill_params(a, &p);
-  return path == NGDN2_PATH_TC ? num_launches_tc(p) : num_launches_simt(p);
+  return (a->gate ? 1 : 0) + (path == NGDN2_PATH_TC ? num_launches_tc(p) : num_launches_simt(p));
 }
 
 int ngdn2_fwd_stage(const ngdn2_fwd_args* a, int stage, void* stream) {
@@ -178,6 +192,10 @@ int ngdn2_fwd_stage(const ngdn2_fwd_args* a, int stage, void* stream) {
   fill_params(a, &p);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t err;
+  if (a->gate && (stage == 0 || stage == 1)) {
+    gate_kernel<<<1, 1, 0, st>>>(a->gate, a->gate_polls, a->status);
+    if (cudaGetLastError() != cudaSuccess) return NGDN2_ERR_CUDA;
+  }
   if (path == NGDN2_PATH_TC) {
     const size_t need = tc_workspace_bytes(p);
     if (need > 0 && (!a->workspace || a->workspace_bytes < need)) return NGDN2_ERR_WORKSPACE;

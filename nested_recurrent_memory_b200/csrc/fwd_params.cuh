@@ -127,6 +127,16 @@ struct FwdParams {
   float* ck_ta;
 };
 
+// True when this forward's start gate timed out: the gate kernel, which
+// runs before every other kernel of the forward on the same stream, set
+// NGDN2_STATUS_GATE_TIMEOUT. Kernels then return before any other work.
+// Nothing sets that bit while the forward's later kernels run, so every
+// thread of a CTA reads the same value.
+__device__ __forceinline__ bool gate_closed(const FwdParams& p) {
+  return p.status &&
+         (*reinterpret_cast<const volatile int32_t*>(p.status) & NGDN2_STATUS_GATE_TIMEOUT);
+}
+
 // Arguments of the update-scan kernel (update_fwd.py:131-204).
 struct UpdParams {
   int B, NF, NG, H, K, V, N, bv, dtype, g_dtype;

@@ -23,7 +23,10 @@
 //     serialise them.
 //   * The first call on each device looks up the buffer's device address
 //     (cudaGetSymbolAddress) with that device current and caches it. Make
-//     that first call before any stream capture.
+//     that first call before any stream capture. The cache lives as long as
+//     the process: after cudaDeviceReset (or any teardown and re-creation of
+//     the device's primary context) the cached address is stale, so a
+//     process that resets a device must not call this entry point again.
 
 #include <mutex>
 

@@ -28,6 +28,7 @@
 namespace ngdn2 {
 
 __global__ void convert_params_kernel(FwdParams p) {
+  if (gate_closed(p)) return;
   const int64_t n = int64_t(p.L - 1) * p.H;
   const int64_t counts[5] = {n * p.n_max * p.K, n * p.K * p.V, n * p.V * p.K,
                              n * p.V * p.V, n * p.V * p.K};
@@ -44,6 +45,7 @@ __global__ void convert_params_kernel(FwdParams p) {
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
+  if (gate_closed(p)) return;
   extern __shared__ float sm[];
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int K = p.K, V = p.V, KP = K + 1;
@@ -169,6 +171,7 @@ __global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
+  if (gate_closed(p)) return;
   __shared__ float gsm[kGemmSmemFloats];
   const int h = blockIdx.x, b = blockIdx.y;
   const int K = p.K, V = p.V, L = p.L, tid = threadIdx.x;

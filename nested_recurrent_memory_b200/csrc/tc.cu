@@ -228,6 +228,7 @@ namespace {
 constexpr int kParamSlices = 16;
 
 __global__ void __launch_bounds__(256) tc_params_kernel(FwdParams p, TcLayout lay, char* ws) {
+  if (gate_closed(p)) return;
   const int l = blockIdx.x + 1, h = blockIdx.y;
   const int i0 = blockIdx.z * blockDim.x + threadIdx.x, di = gridDim.z * blockDim.x;
   const int64_t pidx = int64_t(l - 1) * p.H + h;
@@ -309,6 +310,7 @@ struct PrepMaps {
 
 __global__ void __launch_bounds__(kPrepThreads, 2)
 prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ PrepMaps maps) {
+  if (gate_closed(p)) return;
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tbase;
@@ -1163,6 +1165,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
 __global__ void __launch_bounds__(kScanThreads, 1)
 scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUtensorMap qmap,
                int hl_mode) {
+  if (gate_closed(p)) return;
   extern __shared__ __align__(1024) uint8_t sm_raw[];
   __shared__ uint64_t bar_ld, bar_ld2, bar_mma, bar_q, bar_lvl;
   __shared__ uint32_t tbase;

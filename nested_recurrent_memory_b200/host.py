@@ -55,7 +55,13 @@ class HostPipeline:
 
     def submit(self, host_inputs: dict):
         """Enqueue one batch (pinned CPU tensors shaped like ``example``);
-        returns a handle for ``result``."""
+        returns a handle for ``result``.
+
+        The uploads are asynchronous: they read ``host_inputs`` after this
+        call returns. The caller must leave those host tensors unchanged
+        until ``wait_uploaded(handle)`` returns (or ``result(handle)``,
+        which implies it); refilling one pinned staging buffer right after
+        ``submit`` would upload a mix of two batches."""
         s = self.count % 2
         bufs = self.slots[s]
         with torch.cuda.stream(self.up):
@@ -84,6 +90,19 @@ class HostPipeline:
             self.downloaded[s].record(self.down)
         self.count += 1
         return s, self.count - 1
+
+    def wait_uploaded(self, handle):
+        """Block until a batch's host inputs have been copied to the device,
+        after which the caller may reuse those host tensors. Only valid for
+        one of the two most recent submissions (a slot's event is re-recorded
+        when the slot is reused)."""
+        s, _ = handle
+        self.uploaded[s].synchronize()
+
+    def uploaded_event(self, handle):
+        """The CUDA event recorded after a batch's uploads (valid for one of
+        the two most recent submissions)."""
+        return self.uploaded[handle[0]]
 
     def result(self, handle):
         """Wait for a batch and return its (o, final_state) host tensors."""

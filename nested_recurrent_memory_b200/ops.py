@@ -36,11 +36,102 @@ __all__ = [
     "n_firings",
     "fwd_workspace_bytes",
     "last_path",
+    "check_status",
+    "KernelStatusError",
     "FwdCall",
 ]
 
 _DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 _LAST_PATH = [None]
+
+
+class KernelStatusError(RuntimeError):
+    """A forward's kernels reported a device status (include/ngdn2.h
+    NGDN2_STATUS_*): a bounded wait gave up, so that forward's outputs are
+    not valid."""
+
+
+def _status_message(bits: int) -> str:
+    parts = []
+    if bits & _lib.STATUS_WAIT_TIMEOUT:
+        parts.append("a bounded pipeline wait timed out (outputs invalid; treat the CUDA "
+                     "context as suspect)")
+    if bits & _lib.STATUS_GATE_TIMEOUT:
+        parts.append("the start gate stayed closed (nothing was computed)")
+    return "; ".join(parts) or f"status bits {bits:#x}"
+
+
+class _DeviceStatus:
+    """The sticky status word every forward on one device reports into.
+
+    Kernels only OR bits into the device word. After each launch a 4-byte
+    copy of it goes to pinned host memory on the launching stream, and an
+    event marks that copy; the next launch on the device (or ``check``)
+    reads the copy once its event has completed and raises
+    ``KernelStatusError`` for a nonzero word, then clears it. So a timed-out
+    wait surfaces at the latest one call later, with no synchronisation on
+    the fast path; ``check(sync=True)`` waits for the device instead.
+    With NGDN2_SYNC_CHECK=1 in the environment every launch checks
+    synchronously. During CUDA-graph capture no copy is queued; the word is
+    still set on replay and ``check_status`` reads it."""
+
+    _by_device: dict = {}
+
+    def __init__(self, device):
+        self.device = device
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.copied = torch.cuda.Event()
+        self.pending = False
+
+    @classmethod
+    def get(cls, device) -> "_DeviceStatus":
+        key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+        st = cls._by_device.get(key)
+        if st is None:
+            st = cls._by_device[key] = cls(torch.device("cuda", key[1]))
+        return st
+
+    def _raise_if_set(self, bits: int):
+        if bits:
+            self.word.zero_()
+            self.host.zero_()
+            raise KernelStatusError(f"nested GDN-2 forward: {_status_message(bits)}")
+
+    def poll(self):
+        """Raise for a status copied back by an earlier launch, if its copy is done."""
+        if self.pending and self.copied.query():
+            self.pending = False
+            self._raise_if_set(int(self.host.item()))
+
+    def after_launch(self):
+        stream = torch.cuda.current_stream(self.device)
+        if torch.cuda.is_current_stream_capturing():
+            return
+        if _SYNC_CHECK:
+            self.check(sync=True)
+            return
+        self.host.copy_(self.word, non_blocking=True)
+        self.copied.record(stream)
+        self.pending = True
+
+    def check(self, sync: bool = True):
+        if sync:
+            self.pending = False
+            self._raise_if_set(int(self.word.item()))
+        else:
+            self.poll()
+
+
+_SYNC_CHECK = __import__("os").environ.get("NGDN2_SYNC_CHECK", "0") not in ("", "0")
+
+
+def check_status(device=None, sync: bool = True):
+    """Raise ``KernelStatusError`` if a forward on ``device`` (default: the
+    current CUDA device) reported a device status since the last check, then
+    clear it. ``sync=True`` waits for the device's queued work first."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    _DeviceStatus.get(dev).check(sync=sync)
 
 
 def last_path():
@@ -151,7 +242,7 @@ class FwdCall:
     def __init__(self, q, k, v, g, b, w, mix_weights, query_banks, key_projections,
                  b_projections, w_projections, g_projections, n_queries_per_level,
                  firing_intervals, L, scale=None, initial_state=None, chunk_size=64,
-                 promotion="learned", path="auto", workspace=None):
+                 promotion="learned", path="auto", workspace=None, gate=None, gate_polls=0):
         B, T, H, _, K = q.shape
         if chunk_size != 64:  # chunk.py:230-231
             raise ValueError(f"chunk_size must be 64 for GDN-2, got {chunk_size}")
@@ -199,6 +290,16 @@ class FwdCall:
         self.workspace = workspace
         self.args.workspace = workspace.data_ptr()
         self.args.workspace_bytes = workspace.numel()
+        # Every forward reports into its device's sticky status word.
+        self._status = _DeviceStatus.get(q.device)
+        self.args.status = self._status.word.data_ptr()
+        if gate is not None:
+            _require_cuda(gate)
+            if gate.dtype != torch.int32 or gate.numel() < 1:
+                raise TypeError("gate must be an int32 CUDA tensor")
+            self._keep = self._keep + (gate,)
+            self.args.gate = gate.data_ptr()
+            self.args.gate_polls = int(gate_polls)
 
     @property
     def num_launches(self) -> int:
@@ -211,11 +312,20 @@ class FwdCall:
         if self.args is None:
             self.final.copy_(self.init if self.init is not None else torch.zeros_like(self.final))
             return self.o, self.final
+        self._status.poll()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         rc = _lib.load().ngdn2_fwd_stage(ctypes.byref(self.args), stage, ctypes.c_void_p(stream))
         _raise_for(rc, "ngdn2_fwd", chunk_size=self.args.chunk_size)
         _LAST_PATH[0] = self.path
+        self._status.after_launch()
         return self.o, self.final
+
+    def check(self, sync: bool = True):
+        """Raise ``KernelStatusError`` if a forward on this call's device
+        reported a device status (a bounded wait gave up, or the start gate
+        stayed closed); ``sync`` waits for the device first."""
+        if self.args is not None:
+            self._status.check(sync=sync)
 
 
 def chunk_nested_gdn2_fwd(
@@ -239,6 +349,10 @@ def chunk_nested_gdn2_fwd(
 
     Keyword-only extras: ``path`` ("auto", "simt" or "tc") picks the kernel
     family; ``workspace`` is an optional preallocated uint8 CUDA tensor.
+
+    Device-side failures (a bounded wait that gave up) are reported through
+    a sticky per-device status word: the next forward on the device raises
+    ``KernelStatusError``, and so does ``check_status()`` at any time.
     """
     call = FwdCall(q, k, v, g, b, w, mix_weights, query_banks, key_projections, b_projections,
                    w_projections, g_projections, n_queries_per_level, firing_intervals, L,

@@ -84,6 +84,7 @@ def test_workspace_size_is_positive(lib):
     (dict(firing=(1, 0, 4)), -14),
     (dict(K=200), -7),
     (dict(dtype=7), -8),
+    (dict(gate=0x2000), -9),  # a start gate needs a status word to report into
 ])
 def test_fwd_validation_codes(lib, over, code):
     rc, _ = _ws(lib, _fake_fwd(**over))
@@ -94,6 +95,12 @@ def test_fwd_validation_codes(lib, over, code):
 def test_fwd_rejects_missing_workspace(lib):
     a = _fake_fwd()
     assert lib.ngdn2_fwd(ctypes.byref(a), None) == -10
+
+
+def test_gate_adds_one_launch(lib):
+    plain = lib.ngdn2_fwd_num_launches(ctypes.byref(_fake_fwd()))
+    gated = lib.ngdn2_fwd_num_launches(ctypes.byref(_fake_fwd(gate=0x2000, status=0x3000)))
+    assert plain > 0 and gated == plain + 1
 
 
 def _fake_bwd(**over):
