@@ -58,12 +58,16 @@ enum {
   NGDN2_PROMOTION_MERGE = 1    /* probe.py:105-136 */
 };
 
-/* Kernel families. AUTO picks the tensor-core path when it supports the
- * shape and dtype, else the CUDA-core fp32 path. */
+/* Kernel families. AUTO picks a tensor-core family when the shape and dtype
+ * allow (K = V = 128, 16-bit q/k/v/b/w/o): the fused one-pass family for
+ * L <= 3 with many (batch, head) pairs, else the level-segmented family;
+ * otherwise the CUDA-core fp32 family. */
 enum {
   NGDN2_PATH_AUTO = 0,
-  NGDN2_PATH_SIMT = 1,  /* CUDA-core kernels, fp32 arithmetic throughout */
-  NGDN2_PATH_TC = 2     /* tcgen05 tensor-core kernels, bf16/fp16 operands, fp32 accumulate */
+  NGDN2_PATH_SIMT = 1,   /* CUDA-core kernels, fp32 arithmetic throughout */
+  NGDN2_PATH_TC = 2,     /* tcgen05 kernels, one fused scan per (batch, head); L <= 3 */
+  NGDN2_PATH_TC_SEG = 3  /* tcgen05 kernels, every level a segmented scan (compose, combine,
+                            replay) so few (batch, head) pairs still fill the GPU; any L */
 };
 
 /* Return codes. The Python host layer maps each to the reference's

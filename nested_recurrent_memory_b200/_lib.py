@@ -21,8 +21,8 @@ CHUNK = 64
 
 F32, BF16, F16 = 0, 1, 2
 PROMOTION = {"learned": 0, "merge": 1}
-PATHS = {"auto": 0, "simt": 1, "tc": 2}
-PATH_NAMES = {1: "simt", 2: "tc"}
+PATHS = {"auto": 0, "simt": 1, "tc": 2, "tc_seg": 3}
+PATH_NAMES = {1: "simt", 2: "tc", 3: "tc_seg"}
 
 ERR_CHUNK_SIZE = -1
 ERR_N_POW2 = -2

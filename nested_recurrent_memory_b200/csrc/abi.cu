@@ -39,7 +39,7 @@ int validate_fwd(const ngdn2_fwd_args* a, bool outputs = true) {
   if (!dim_ok(a->K) || !dim_ok(a->V)) return NGDN2_ERR_SHAPE;
   if (a->promotion != NGDN2_PROMOTION_LEARNED && a->promotion != NGDN2_PROMOTION_MERGE)
     return NGDN2_ERR_SHAPE;
-  if (a->path < NGDN2_PATH_AUTO || a->path > NGDN2_PATH_TC) return NGDN2_ERR_SHAPE;
+  if (a->path < NGDN2_PATH_AUTO || a->path > NGDN2_PATH_TC_SEG) return NGDN2_ERR_SHAPE;
   for (int l = 0; l < a->L; ++l)
     if (a->firing[l] < 1) return NGDN2_ERR_FIRING;
   for (int l = 1; l < a->L; ++l) {
@@ -110,11 +110,20 @@ void fill_params(const ngdn2_fwd_args* a, FwdParams* p) {
   p->ss = ScanScratch::make(a->K, a->V, np);
 }
 
+// (batch, head) pairs from which the fused family's one scan CTA per pair
+// keeps enough SMs busy; below it the segmented family splits each level's
+// sequence instead.
+constexpr int kFusedMinPairs = 64;
+
 int select_path(const ngdn2_fwd_args* a) {
-  const bool tc_ok = tc_supports(a);
+  const bool tc_ok = tc_supports(a), seg_ok = seg_supports(a);
   if (a->path == NGDN2_PATH_SIMT) return NGDN2_PATH_SIMT;
   if (a->path == NGDN2_PATH_TC) return tc_ok ? int(NGDN2_PATH_TC) : int(NGDN2_ERR_UNSUPPORTED);
-  return tc_ok ? int(NGDN2_PATH_TC) : int(NGDN2_PATH_SIMT);
+  if (a->path == NGDN2_PATH_TC_SEG)
+    return seg_ok ? int(NGDN2_PATH_TC_SEG) : int(NGDN2_ERR_UNSUPPORTED);
+  if (tc_ok && a->B * a->H >= kFusedMinPairs) return NGDN2_PATH_TC;
+  if (seg_ok) return NGDN2_PATH_TC_SEG;
+  return NGDN2_PATH_SIMT;
 }
 
 // Workspace of the SIMT path in floats: converted parameters, the chunk
@@ -166,6 +175,7 @@ int ngdn2_fwd_workspace_size(const ngdn2_fwd_args* a, size_t* bytes) {
   FwdParams p;
   fill_params(a, &p);
   if (path == NGDN2_PATH_TC) *bytes = tc_workspace_bytes(p);
+  else if (path == NGDN2_PATH_TC_SEG) *bytes = seg_workspace_bytes(p);
   else *bytes = size_t(simt_workspace_floats(p)) * sizeof(float);
   return NGDN2_OK;
 }
@@ -179,7 +189,9 @@ int ngdn2_fwd_num_launches(const ngdn2_fwd_args* a) {
   if (path < 0) return path;
   FwdParams p;
   fill_params(a, &p);
-  return (a->gate ? 1 : 0) + (path == NGDN2_PATH_TC ? num_launches_tc(p) : num_launches_simt(p));
+  return (a->gate ? 1 : 0) + (path == NGDN2_PATH_TC       ? num_launches_tc(p)
+                               : path == NGDN2_PATH_TC_SEG ? num_launches_seg(p)
+                                                           : num_launches_simt(p));
 }
 
 int ngdn2_fwd_stage(const ngdn2_fwd_args* a, int stage, void* stream) {
@@ -200,6 +212,10 @@ int ngdn2_fwd_stage(const ngdn2_fwd_args* a, int stage, void* stream) {
     const size_t need = tc_workspace_bytes(p);
     if (need > 0 && (!a->workspace || a->workspace_bytes < need)) return NGDN2_ERR_WORKSPACE;
     err = launch_fwd_tc(p, a->workspace, stage, st);
+  } else if (path == NGDN2_PATH_TC_SEG) {
+    const size_t need = seg_workspace_bytes(p);
+    if (!a->workspace || a->workspace_bytes < need) return NGDN2_ERR_WORKSPACE;
+    err = launch_fwd_seg(p, a->workspace, stage, st);
   } else {
     const size_t need = size_t(simt_workspace_floats(p)) * sizeof(float);
     if (!a->workspace || a->workspace_bytes < need) return NGDN2_ERR_WORKSPACE;

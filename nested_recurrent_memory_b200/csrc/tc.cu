@@ -68,7 +68,8 @@ __global__ void __launch_bounds__(256) tc_params_kernel(FwdParams p, TcLayout la
   bf16* qb = reinterpret_cast<bf16*>(base + PT_QB);
   bf16* w2a = reinterpret_cast<bf16*>(base + PT_W2A);
   bf16* w2b = reinterpret_cast<bf16*>(base + PT_W2B);
-  const int nq = p.nq[l - 1], mp = pad_pairs(nq);
+  // (The merge arm ignores n_queries; never read past the bank's rows.)
+  const int nq = min(p.nq[l - 1], p.n_max), mp = pad_pairs(nq);
   const int dt = p.param_dtype;
   // Query bank rows past n_queries are ignored (probe.py:97): zero rows.
   for (int it = i0; it < mp * 16; it += di) {

@@ -106,15 +106,21 @@ def test_tc_agrees_with_simt():
     assert rel_err(_np(s1), _np(s2)) < LOWP_REL
 
 
-def test_auto_selects_tc_and_is_repeatable():
+def test_auto_selects_tensor_cores_and_is_repeatable():
+    """AUTO picks a tensor-core family for 16-bit K = V = 128 inputs: the
+    level-segmented one for few (batch, head) pairs, the fused one for many;
+    either way two runs give the same bits."""
+    from nested_recurrent_memory_b200 import last_path
     inp = config_inputs(1, 256, 2, 128, 128, 2, 32, (1, 2), dtype=torch.bfloat16, seed=6)
     inp.pop("L")
     d = _dev(inp)
     o1, s1 = chunk_nested_gdn2(**d, L=2, output_final_state=True)
     o2, s2 = chunk_nested_gdn2(**d, L=2, output_final_state=True)
-    from nested_recurrent_memory_b200 import last_path
-    assert last_path() == "tc"
+    assert last_path() == "tc_seg"
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    many = config_inputs(4, 128, 16, 128, 128, 2, 32, (1, 2), dtype=torch.bfloat16, seed=6)
+    many.pop("L")
+    assert FwdCall(**_dev(many), L=2).path == "tc"
 
 
 def test_broadcast_gates_match_dense():
