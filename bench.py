@@ -49,7 +49,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", default="config1")
-    ap.add_argument("--path", choices=("auto", "simt", "tc"), default="auto")
+    ap.add_argument("--path", choices=("auto", "simt", "tc", "tc_seg"), default="auto")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--batch", type=int, default=None,
@@ -73,10 +73,17 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+# Configurations whose global problem is split by heads across the GPUs
+# (strong scaling: 32 / N heads per GPU of one fixed sequence); the others
+# give every GPU its own batch (weak scaling).
+HEAD_SHARDED = {"config3"}
+
+
 def workload(cfg_name):
     from nested_recurrent_memory_b200.synthetic import CONFIGS
     B, T, H, K, V, L, m, firing, dtype = CONFIGS[cfg_name]
-    return dict(B=B, T=T, H=H, K=K, V=V, L=L, m=m, firing=tuple(firing), dtype=dtype)
+    return dict(B=B, T=T, H=H, K=K, V=V, L=L, m=m, firing=tuple(firing), dtype=dtype,
+                shard="heads" if cfg_name in HEAD_SHARDED else "batch")
 
 
 def alg_counts(w):
@@ -273,11 +280,19 @@ def run_reference(args, w):
 # ---------------------------------------------------------------------------
 
 def shard(world, rank, w):
-    """Weak scaling: every rank runs the configuration's per-GPU batch on its
-    own seeded rows of a global batch of ``world * B`` sequences; (b, h)
+    """Weak scaling (batch-sharded configurations): every rank runs the
+    configuration's per-GPU batch on its own seeded rows of a global batch of
+    ``world * B`` sequences. Strong scaling (head-sharded ones): rank r runs
+    heads [r H / N, (r + 1) H / N) of the one global sequence batch. (b, h)
     states are independent, so no rank needs another's data."""
+    if w["shard"] == "heads":
+        if w["H"] % world:
+            raise SystemExit(f"{w['H']} heads do not split over {world} GPUs")
+        hl = w["H"] // world
+        return {"seed": 1000 + rank, "heads": (rank * hl, (rank + 1) * hl), "H_local": hl,
+                "global_batch": w["B"]}
     return {"seed": 1000 + rank, "rows": (rank * w["B"], (rank + 1) * w["B"]),
-            "global_batch": world * w["B"]}
+            "global_batch": world * w["B"], "H_local": w["H"]}
 
 
 def max_over_ranks(value, world, device="cpu"):
@@ -292,17 +307,27 @@ def max_over_ranks(value, world, device="cpu"):
 
 
 def job_tokens_per_s(w, world, ms_per_step):
-    """Whole-job tokens/s: all ranks' tokens over the slowest rank's time."""
-    return world * w["B"] * w["T"] / (ms_per_step / 1e3)
+    """Whole-job tokens/s: all ranks' tokens over the slowest rank's time
+    (head-sharded: the ranks share one batch's tokens, each doing its heads)."""
+    rows = w["B"] if w["shard"] == "heads" else world * w["B"]
+    return rows * w["T"] / (ms_per_step / 1e3)
 
 
 def config_dict(args, w):
+    if w["shard"] == "heads":
+        split = (f"B={w['B']}, H={w['H']} split {w['H'] // args.gpus} heads per GPU")
+        par = f"head sharding (strong scaling), {args.gpus} GPU(s), no collective"
+        gb = w["B"]
+    else:
+        split = f"B={w['B']} per GPU, H={w['H']}"
+        par = f"(batch, head) sharding (weak scaling), {args.gpus} GPU(s), no collective"
+        gb = w["B"] * args.gpus
     return {
-        "workload": (f"{args.config}: B={w['B']} per GPU, T={w['T']}, H={w['H']}, "
+        "workload": (f"{args.config}: {split}, T={w['T']}, "
                      f"K=V={w['K']}, L={w['L']} firing {'/'.join(map(str, w['firing']))} chunks, "
                      f"m={w['m']}, C=64, {str(w['dtype']).replace('torch.', '')} inputs, fp32 state"),
-        "global_batch": w["B"] * args.gpus, "seq_len": w["T"], "heads": w["H"],
-        "parallelism": f"(batch, head) sharding, {args.gpus} GPU(s), no collective",
+        "global_batch": gb, "seq_len": w["T"], "heads": w["H"],
+        "parallelism": par,
         "l2": "inputs larger than L2 (no flush needed)",
     }
 
@@ -333,8 +358,9 @@ def run_ours(args, w):
         torch.cuda.synchronize()
 
     plan = shard(world, rank, w)
-    inp = config_inputs(w["B"], w["T"], w["H"], w["K"], w["V"], w["L"], w["m"], w["firing"],
-                        dtype=w["dtype"], seed=plan["seed"], device=dev, gen_device=dev)
+    inp = config_inputs(w["B"], w["T"], plan["H_local"], w["K"], w["V"], w["L"], w["m"],
+                        w["firing"], dtype=w["dtype"], seed=plan["seed"], device=dev,
+                        gen_device=dev)
     L = inp.pop("L")
     call = FwdCall(**inp, L=L, path=args.path)
     launches_per_step = call.num_launches
@@ -437,7 +463,7 @@ def run_ours(args, w):
 
     peaks, peak_src = load_peaks()
     flop_th, bytes_th = alg_counts(w)
-    token_heads = w["B"] * w["T"] * w["H"]
+    token_heads = w["B"] * w["T"] * plan["H_local"]
     alg_bytes = bytes_th * token_heads
     alg_flops = flop_th * token_heads
     # The algorithmic bytes split by the kernel that moves them: prep reads
@@ -459,8 +485,10 @@ def run_ours(args, w):
                 if name in per:
                     kernel_traffic[st] = per[name] * token_heads
     dominant = max(stage_ms, key=stage_ms.get)
-    dom_name = {1: "prep_tc_kernel" if call.path == "tc" else "prep_simt_kernel",
-                2: "scan_tc_kernel" if call.path == "tc" else "scan_simt_kernel"}[dominant]
+    stage_names = {"tc": ("prep_tc_kernel", "scan_tc_kernel"),
+                   "tc_seg": ("prep_tc_kernel", "seg levels (seg_scan/combine/probe/read kernels)"),
+                   "simt": ("prep_simt_kernel", "scan_simt_kernel")}[call.path]
+    dom_name = stage_names[dominant - 1]
     dom_gbs = kernel_bytes[dominant] / (stage_ms[dominant] / 1e3) / 1e9
     whole_gbs = alg_bytes / (ms_step / 1e3) / 1e9
     roofline = {
@@ -487,7 +515,7 @@ def run_ours(args, w):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        heads = 16
+        heads = 2 if w["T"] > 16384 else 16
         secs, th = cpu_sample_run(w, heads)
         cpu = {"value": th / w["H"] / secs, "unit": "tokens/s", "cores": cpu_threads(),
                "kind": "port",
@@ -500,7 +528,8 @@ def run_ours(args, w):
             "metric": METRIC, "value": value, "unit": "tokens/s (whole job, all GPUs)",
             "value_per_gpu": value / world, "unit_per_gpu": "tokens/s/GPU", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if w["shard"] == "heads" else "weak",
+            "vs_baseline": None,
             "dtype": "bf16" if "bfloat16" in str(w["dtype"]) else str(w["dtype"]).replace("torch.", ""),
             "data": "synthetic (seeded; BASELINE config recipe)",
             "config": config_dict(args, w) | {"kernel_path": call.path},

@@ -58,7 +58,6 @@ constexpr int kReadThreads = 256;
 constexpr int kStateBytes = TK * TV * 2;     // one bf16 state in the B-operand layout
 constexpr int kMzBytes = 2 * kStateBytes + TK * TV * 4;  // M hi, M lo (bf16), Z (fp32)
 constexpr int kSMs = 148;                    // B200; sizes the segment split only
-constexpr int kReadLevels = 3;               // upper levels per round of the read kernel
 
 // Byte offsets of one step record's operands (see the file comment).
 struct StepRec {
@@ -133,7 +132,7 @@ struct SegLayout {
   int nseg[NGDN2_MAX_LEVELS], seglen[NGDN2_MAX_LEVELS], nE[NGDN2_MAX_LEVELS];
   int64_t mz_off[NGDN2_MAX_LEVELS], start_off[NGDN2_MAX_LEVELS], E_off[NGDN2_MAX_LEVELS];
   int64_t prec_off[NGDN2_MAX_LEVELS];
-  int64_t o0_off, total;
+  int64_t total;
 };
 
 inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
@@ -167,11 +166,15 @@ inline SegLayout seg_layout(const FwdParams& p) {
     s.prec_off[l] = align256(off);
     if (l > 0) off = s.prec_off[l] + bh * steps * probe_rec(level_rows(p, l)).size;
   }
-  s.o0_off = align256(off);
-  off = s.o0_off + (p.L > 1 ? bh * p.NT * kC * TV * 4 : 0);
   s.total = align256(off);
   return s;
 }
+
+// fp32 [K][V] states kept between kernels (segment transitions Z, segment
+// start states) in a lane-major layout: element (k, v) at
+// ((v / 4) * K + k) * 4 + v % 4, so the 32 lanes of a warp that own rows
+// k .. k + 31 access 512 contiguous bytes per float4 instead of 32 rows.
+__device__ __forceinline__ int lm_off(int k, int v) { return ((v >> 2) * TK + k) * 4 + (v & 3); }
 
 __device__ __forceinline__ bool seg_gate_closed(const int32_t* status) {
   return status && (*reinterpret_cast<const volatile int32_t*>(status) & NGDN2_STATUS_GATE_TIMEOUT);
@@ -184,7 +187,7 @@ __device__ __forceinline__ bool seg_gate_closed(const int32_t* status) {
 // ---------------------------------------------------------------------------
 
 struct SegScanArgs {
-  int level, L, H, T, NTp;       // NTp: chunks (output rows / 64)
+  int level, L, H, T;
   int nsteps, seglen, nseg;
   StepRec rec;
   const char* recs;              // [B][H][nsteps] records
@@ -194,9 +197,8 @@ struct SegScanArgs {
   bf16* E;                       // [B][H][nE] emitted states
   int nE, emit_every;            // level 0: level 1's interval; levels: 0 (after every step)
   float* fin;                    // [B][H][L][K][V]
-  int out;                       // level-0 output: 0 none, 1 fp32 partial o0, 2 o itself
-  float* o0;                     // [B][H][NTp * 64][V]
-  void* o;
+  int out;                       // 1: level 0's replay writes its output part to o
+  void* o;                       // [B][T][H][V] (the read kernel adds the upper levels)
   int dtype;
   int32_t* status;
 };
@@ -268,10 +270,15 @@ seg_scan_kernel(SegScanArgs a, int replay) {
   };
 
   // Start state: identity (M), zero (Z), or the state entering the segment.
-  const float* src = nullptr;
+  const float* src = nullptr;   // start state: segment starts lane-major, init row-major
+  bool src_lm = false;
   if (mode == 2) {
-    if (a.nseg > 1 && s > 0) src = a.starts + (bh * a.nseg + s) * TK * TV;
-    else if (a.init) src = a.init + (bh * a.L + a.level) * TK * TV;
+    if (a.nseg > 1 && s > 0) {
+      src = a.starts + (bh * a.nseg + s) * TK * TV;
+      src_lm = true;
+    } else if (a.init) {
+      src = a.init + (bh * a.L + a.level) * TK * TV;
+    }
   }
   float dcur = j0 < j1 ? fetch_d(j0) : 1.f;
   if (j0 < j1) fetch_y(j0);
@@ -284,7 +291,8 @@ seg_scan_kernel(SegScanArgs a, int replay) {
     if (src) {
 #pragma unroll
       for (int t = 0; t < 32; t += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src + k * TV + cc + t);
+        const float4 v = *reinterpret_cast<const float4*>(src + (src_lm ? lm_off(k, cc + t)
+                                                                           : k * TV + cc + t));
         x[t] = v.x; x[t + 1] = v.y; x[t + 2] = v.z; x[t + 3] = v.w;
       }
     }
@@ -419,7 +427,7 @@ seg_scan_kernel(SegScanArgs a, int replay) {
                                             2 * kStateBytes);
 #pragma unroll
         for (int t = 0; t < 32; t += 4)
-          *reinterpret_cast<float4*>(z + k * TV + cc + t) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+          *reinterpret_cast<float4*>(z + lm_off(k, cc + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
       }
       if (!seg_end) {
 #pragma unroll
@@ -430,12 +438,7 @@ seg_scan_kernel(SegScanArgs a, int replay) {
         const int i = 32 * (quarter - 2) + lane, t = j * kC + i;
         float y[32];
         tmem_ld32(taddr(tD, 32 * quarter, cc), y);
-        if (a.out == 1) {
-          float* dst = a.o0 + (bh * a.NTp * kC + t) * TV + cc;
-#pragma unroll
-          for (int u = 0; u < 32; u += 4)
-            *reinterpret_cast<float4*>(dst + u) = make_float4(y[u], y[u + 1], y[u + 2], y[u + 3]);
-        } else if (t < a.T) {
+        if (t < a.T) {
           uint4* dst = reinterpret_cast<uint4*>(
               reinterpret_cast<uint16_t*>(a.o) + ((int64_t(b) * a.T + t) * a.H + h) * TV + cc);
 #pragma unroll
@@ -466,7 +469,10 @@ seg_scan_kernel(SegScanArgs a, int replay) {
 // ---------------------------------------------------------------------------
 // seg_combine: grid (H, B), 256 threads. The state entering each segment of
 // one level: S_{s+1} = M_s S_s + Z_s with M_s and S_s each split into two
-// bf16 halves (three MMAs: hi.hi + hi.lo + lo.hi).
+// bf16 halves (three MMAs: hi.hi + hi.lo + lo.hi) accumulating onto Z_s in
+// TMEM. M_{s+1} streams into the second of two shared-memory buffers and
+// Z_{s+1} into the second of two TMEM accumulators while step s's MMAs run,
+// so a step's critical path is its MMAs and the read-out of S_{s+1}.
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kSegThreads, 1)
@@ -474,7 +480,7 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
                    int nseg, int32_t* status) {
   if (seg_gate_closed(status)) return;
   extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ uint64_t bar_ld, bar_mma;
+  __shared__ uint64_t bar_ld[2], bar_mma;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -482,22 +488,26 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
   const int h = blockIdx.x, b = blockIdx.y;
   const int64_t bh = int64_t(b) * H + h;
   const int k = 32 * quarter + lane;
-  bf16* Ahi = reinterpret_cast<bf16*>(sm);
-  bf16* Alo = Ahi + TK * TV;
-  bf16* Shi = Alo + TK * TV;
+  // Two M buffers (hi, lo), then the state's hi / lo B operands.
+  bf16* Shi = reinterpret_cast<bf16*>(sm + 4 * kStateBytes);
   bf16* Slo = Shi + TK * TV;
   const char* mz0 = mz + bh * (nseg - 1) * int64_t(kMzBytes);
+  const int nsteps = nseg - 1;
 
-  if (warp == 0) tmem_alloc(&tbase, 128);
+  if (warp == 0) tmem_alloc(&tbase, 256);
+  auto load_m = [&](int s) {
+    uint64_t* bar = &bar_ld[s & 1];
+    mbar_arrive_expect_tx(bar, 2 * kStateBytes);
+    bulk_g2s(sm + (s & 1) * 2 * kStateBytes, mz0 + s * int64_t(kMzBytes), 2 * kStateBytes, bar);
+  };
   if (tid == 0) {
-    mbar_init(&bar_ld, 1);
+    mbar_init(&bar_ld[0], 1);
+    mbar_init(&bar_ld[1], 1);
     mbar_init(&bar_mma, 1);
     fence_mbar_init();
     abort_flag = 0;
-    mbar_arrive_expect_tx(&bar_ld, 2 * kStateBytes);
-    bulk_g2s(Ahi, mz0, 2 * kStateBytes, &bar_ld);
+    load_m(0);
   }
-  // S_0: the level's initial state (or zero) as hi / lo B operands.
   auto put_state = [&](const float* x, int cc) {
 #pragma unroll
     for (int c = 0; c < 32; c += 8) {
@@ -511,6 +521,26 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
       *reinterpret_cast<uint4*>(Slo + mnmajor_off(k, cc + c, TK)) = pack8(lo);
     }
   };
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tb = tbase;
+  // Z_s of a step into accumulator s & 1.
+  auto put_z = [&](int s) {
+    const float* z = reinterpret_cast<const float*>(mz0 + s * int64_t(kMzBytes) + 2 * kStateBytes);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int cc = c0 + 32 * hh;
+      float x[32];
+#pragma unroll
+      for (int t = 0; t < 32; t += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(z + lm_off(k, cc + t));
+        x[t] = v.x; x[t + 1] = v.y; x[t + 2] = v.z; x[t + 3] = v.w;
+      }
+      tmem_st32(taddr(tb + 128 * (s & 1), 32 * quarter, cc), x);
+    }
+  };
+  // S_0: the level's initial state (or zero).
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
     const int cc = c0 + 32 * hh;
@@ -519,49 +549,32 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
     for (int t = 0; t < 32; ++t) x[t] = init ? init[((bh * L + level) * TK + k) * TV + cc + t] : 0.f;
     put_state(x, cc);
   }
+  if (nsteps > 0) put_z(0);
+  tmem_wait_st();
+  fence_proxy_async();
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  const uint32_t tD = tbase;
   const uint32_t id = idesc_f16(128, 128, true, false, true);
-  uint32_t ph_ld = 0, ph_mma = 0;
-  for (int s = 0; s + 1 < nseg; ++s) {
-    // Z_s as the accumulator's starting value.
-    const float* z = reinterpret_cast<const float*>(mz0 + s * int64_t(kMzBytes) + 2 * kStateBytes);
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int cc = c0 + 32 * hh;
-      float x[32];
-#pragma unroll
-      for (int t = 0; t < 32; t += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(z + k * TV + cc + t);
-        x[t] = v.x; x[t + 1] = v.y; x[t + 2] = v.z; x[t + 3] = v.w;
-      }
-      tmem_st32(taddr(tD, 32 * quarter, cc), x);
-    }
-    tmem_wait_st();
-    fence_proxy_async();
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
+  uint32_t ph_mma = 0;
+  for (int s = 0; s < nsteps; ++s) {
+    const uint32_t tD = tb + 128 * (s & 1);
     if (tid == 0) {
-      if (!mbar_wait(&bar_ld, ph_ld)) abort_flag = 1;
+      // (Buffer (s + 1) & 1 was last read by step s - 1's MMAs, complete.)
+      if (s + 1 < nsteps) load_m(s + 1);
+      if (!mbar_wait(&bar_ld[s & 1], (s >> 1) & 1)) abort_flag = 1;
       fence_after_sync();
-      mma_tile(tD, smem_u32(Ahi), smem_u32(Shi), TK, id, true);
-      mma_tile(tD, smem_u32(Ahi), smem_u32(Slo), TK, id, true);
-      mma_tile(tD, smem_u32(Alo), smem_u32(Shi), TK, id, true);
+      const uint8_t* mb = sm + (s & 1) * 2 * kStateBytes;
+      mma_tile(tD, smem_u32(mb), smem_u32(Shi), TK, id, true);
+      mma_tile(tD, smem_u32(mb), smem_u32(Slo), TK, id, true);
+      mma_tile(tD, smem_u32(mb + kStateBytes), smem_u32(Shi), TK, id, true);
       mma_commit(&bar_mma);
     }
-    ph_ld ^= 1;
     __syncwarp();
+    if (s + 1 < nsteps) put_z(s + 1);
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
-    // M_s is spent: the next segment's streams in while S_{s+1} is written.
-    if (tid == 0 && s + 2 < nseg) {
-      mbar_arrive_expect_tx(&bar_ld, 2 * kStateBytes);
-      bulk_g2s(Ahi, mz0 + (s + 1) * int64_t(kMzBytes), 2 * kStateBytes, &bar_ld);
-    }
     float* dst = starts + (bh * nseg + s + 1) * TK * TV;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -570,9 +583,10 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
       tmem_ld32(taddr(tD, 32 * quarter, cc), x);
 #pragma unroll
       for (int t = 0; t < 32; t += 4)
-        *reinterpret_cast<float4*>(dst + k * TV + cc + t) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+        *reinterpret_cast<float4*>(dst + lm_off(k, cc + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
       put_state(x, cc);
     }
+    tmem_wait_st();
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
@@ -582,7 +596,7 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
   if (abort_flag && tid == 0 && status) atomicOr(status, NGDN2_STATUS_WAIT_TIMEOUT);
   fence_before_sync();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 128);
+  if (warp == 0) tmem_dealloc(tbase, 256);
 }
 
 // ---------------------------------------------------------------------------
@@ -897,22 +911,31 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
 }
 
 // ---------------------------------------------------------------------------
-// seg_read: grid (NT, H, B), 256 threads. o = o0 + sum_l mix_l scale
-// (q_l . S_l) for one chunk, S_l the state entering the chunk's group of
-// level l (chunk.py:129-156, naive.py:382-390); up to kReadLevels levels per
-// round, each in its own TMEM accumulator (lanes 64..127, as in the fused
-// scan's reads).
+// seg_read: grid (ceil(NT / unit), H, B), 256 threads. Adds the upper
+// levels' reads sum_{l >= 1} mix_l scale (q_l . S_l) to the level-0 output
+// that level 0's replay left in o (chunk.py:129-156, naive.py:382-390). A CTA
+// takes a unit of up to four chunks; the unit size divides every upper
+// level's firing interval, so its chunks read the same state of each level
+// (the one entering their group). Level by level, the state and the unit's
+// query tiles (TMA, 128-byte swizzle) arrive in one of two shared-memory
+// stages, the next level's load overlapping this level's work; the query
+// rows are scaled by mix_l scale in place; then one M = 128 MMA per chunk
+// (the tile in the tile's lower half, as in the fused scan's reads)
+// accumulates into that chunk's TMEM accumulator, so the levels sum on the
+// tensor cores and the epilogue adds one accumulator per chunk to o.
 // ---------------------------------------------------------------------------
 
+constexpr int kReadUnit = 4;
+constexpr int kReadStage = kStateBytes + kReadUnit * TILE_QK;
+
 struct ReadArgs {
-  int B, T, H, L, NT;
+  int B, T, H, L, NT, unit;
   int firing[NGDN2_MAX_LEVELS];
   const bf16* E[NGDN2_MAX_LEVELS];
   int nE[NGDN2_MAX_LEVELS];
   QView q;
   TokView mix;
   float scale;
-  const float* o0;
   void* o;
   int dtype;
   int hl_mode;
@@ -923,116 +946,117 @@ __global__ void __launch_bounds__(kReadThreads, 1)
 seg_read_kernel(ReadArgs a, const __grid_constant__ CUtensorMap qmap) {
   if (seg_gate_closed(a.status)) return;
   extern __shared__ __align__(1024) uint8_t sm_raw[];
-  __shared__ uint64_t bar_ld, bar_mma;
+  __shared__ uint64_t bar_ld[2], bar_mma[NGDN2_MAX_LEVELS];
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, c0 = 64 * (warp >> 2);
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int n0 = blockIdx.x * a.unit;
+  const int nc = min(a.unit, a.NT - n0);
   const int64_t bh = int64_t(b) * a.H + h;
   uint8_t* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
-  // Per level slot: the 64 KB ahead of each query tile hold its state (the
-  // M = 128 read tile's upper half, whose lanes are never read, lands there).
-  uint8_t* QT = sm + kReadLevels * kStateBytes;
   const bool q_tma = a.hl_mode != 2;
-  const bool q_conv = !q_tma || a.q.dt != NGDN2_BF16;
+  const int nlev = a.L - 1;
 
   if (warp == 0) tmem_alloc(&tbase, 512);
+  // Level l's state (the one entering the unit's group) and query tiles
+  // into stage st.
+  auto issue = [&](int l, int st) {
+    uint8_t* base = sm + st * kReadStage;
+    uint64_t* bar = &bar_ld[st];
+    mbar_arrive_expect_tx(bar, uint32_t(kStateBytes + (q_tma ? nc * TILE_QK : 0)));
+    bulk_g2s(base, a.E[l] + (bh * a.nE[l] + n0 / a.firing[l]) * (TK * TV), kStateBytes, bar);
+    if (q_tma)
+      for (int c = 0; c < nc; ++c)
+        tma_load_4d(base + kStateBytes + c * TILE_QK, &qmap, 0, b * a.T + (n0 + c) * kC, 0,
+                    a.hl_mode ? l * a.H + h : h * a.L + l, bar);
+  };
   if (tid == 0) {
-    mbar_init(&bar_ld, 1);
-    mbar_init(&bar_mma, 1);
+    mbar_init(&bar_ld[0], 1);
+    mbar_init(&bar_ld[1], 1);
+    for (int l = 0; l < NGDN2_MAX_LEVELS; ++l) mbar_init(&bar_mma[l], 1);
     fence_mbar_init();
     abort_flag = 0;
+    issue(1, 0);
+    if (nlev > 1) issue(2, 1);
   }
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tb = tbase;
-  const int i = 32 * (quarter - 2) + lane;   // output row of threads in lane quarters 2, 3
-  const int t = n * kC + i;
-  float acc[64];
-#pragma unroll
-  for (int u = 0; u < 64; ++u) acc[u] = 0.f;
   const uint32_t id = idesc_f16(128, 128, true, false, true);
-  uint32_t ph_ld = 0, ph_mma = 0;
-  for (int l0 = 1; l0 < a.L; l0 += kReadLevels) {
-    const int nl = min(kReadLevels, a.L - l0);
-    if (tid == 0) {
-      uint32_t bytes = uint32_t(nl) * kStateBytes + (q_tma ? uint32_t(nl) * TILE_QK : 0u);
-      mbar_arrive_expect_tx(&bar_ld, bytes);
-      for (int r = 0; r < nl; ++r) {
-        const int l = l0 + r;
-        const bf16* st = a.E[l] + (bh * a.nE[l] + n / a.firing[l]) * (TK * TV);
-        bulk_g2s(sm + r * kStateBytes, st, kStateBytes, &bar_ld);
-        if (q_tma)
-          tma_load_4d(QT + r * TILE_QK, &qmap, 0, b * a.T + n * kC, 0,
-                      a.hl_mode ? l * a.H + h : h * a.L + l, &bar_ld);
-      }
-    }
-    if (!mbar_wait(&bar_ld, ph_ld)) abort_flag = 1;
-    ph_ld ^= 1;
-    if (q_conv) {
-      // fp16 q (or q without a tensor map): bf16 tiles in the swizzled layout.
-      const int r = tid & 63, g4 = tid >> 6;
-      for (int lr = 0; lr < nl; ++lr) {
-        const int l = l0 + lr;
-        uint8_t* tile = QT + lr * TILE_QK;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint4* q8 = reinterpret_cast<uint4*>(tile + sw128_off(r, 8 * (g4 + 4 * u)));
+  uint32_t ph_ld[2] = {0u, 0u};
+  for (int li = 0; li < nlev; ++li) {
+    const int l = li + 1, st = li & 1;
+    uint8_t* base = sm + st * kReadStage;
+    if (!mbar_wait(&bar_ld[st], ph_ld[st])) abort_flag = 1;
+    ph_ld[st] ^= 1;
+    // Row r of chunk c scaled by mix_l scale (zero past T), as bf16 (fp16 q
+    // converted; q without a tensor map read here with plain loads).
+    {
+      const int r = tid & 63, c = tid >> 6;
+      if (c < nc) {
+        const int t = (n0 + c) * kC + r;
+        const float m =
+            t < a.T ? load_elem(a.mix.p, a.mix.off(b, t, h, l), a.mix.dt) * a.scale : 0.f;
+        uint8_t* tile = base + kStateBytes + c * TILE_QK;
+#pragma unroll 4
+        for (int u = 0; u < 16; ++u) {
+          uint4* q8 = reinterpret_cast<uint4*>(tile + sw128_off(r, 8 * u));
+          const uint4 raw =
+              q_tma ? *q8
+                    : t < a.T ? raw8_at(a.q.p, a.q.dt, a.q.off(b, t, h, l, 8 * u), a.q.sd)
+                              : make_uint4(0u, 0u, 0u, 0u);
           float f[8];
-          const uint4 raw = q_tma ? *q8
-                            : n * kC + r < a.T ? raw8_at(a.q.p, a.q.dt,
-                                                         a.q.off(b, n * kC + r, h, l, 8 * (g4 + 4 * u)), a.q.sd)
-                                               : make_uint4(0, 0, 0, 0);
           unpack8(raw, a.q.dt, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] *= m;
           *q8 = pack8(f);
         }
       }
-      fence_proxy_async();
     }
+    fence_proxy_async();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     if (tid == 0) {
-      for (int r = 0; r < nl; ++r)
-        mma_tile_sw128_lo(tb + 128 * r, smem_u32(QT + r * TILE_QK), smem_u32(sm + r * kStateBytes), id,
-                          false);
-      mma_commit(&bar_mma);
-    }
-    __syncwarp();
-    if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
-    ph_mma ^= 1;
-    fence_after_sync();
-    if (quarter >= 2) {
-      for (int r = 0; r < nl; ++r) {
-        const int l = l0 + r;
-        float m = 0.f;
-        if (t < a.T) m = load_elem(a.mix.p, a.mix.off(b, t, h, l), a.mix.dt) * a.scale;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float y[32];
-          tmem_ld32(taddr(tb + 128 * r, 32 * quarter, c0 + 32 * hh), y);
-#pragma unroll
-          for (int u = 0; u < 32; ++u) acc[32 * hh + u] = fmaf(m, y[u], acc[32 * hh + u]);
-        }
+      for (int c = 0; c < nc; ++c)
+        mma_tile_sw128_lo(tb + 128 * c, smem_u32(base + kStateBytes + c * TILE_QK),
+                          smem_u32(base), id, li > 0);
+      mma_commit(&bar_mma[li]);
+      // Once these MMAs have read the stage, the level after next streams in.
+      if (li + 2 < nlev) {
+        if (!mbar_wait(&bar_mma[li], 0)) abort_flag = 1;
+        issue(l + 2, st);
       }
     }
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    if (abort_flag) break;
+    __syncwarp();
   }
-  if (quarter >= 2 && t < a.T) {
-    const float* src = a.o0 + (bh * a.NT * kC + t) * TV + c0;
-    uint16_t* dst = reinterpret_cast<uint16_t*>(a.o) + ((int64_t(b) * a.T + t) * a.H + h) * TV + c0;
+  // MMAs complete in issue order: the last level's barrier covers them all.
+  if (nlev > 0 && !mbar_wait(&bar_mma[nlev - 1], 0)) abort_flag = 1;
+  fence_after_sync();
+  if (quarter >= 2) {
+    const int i = 32 * (quarter - 2) + lane;
+    for (int c = 0; c < nc; ++c) {
+      const int t = (n0 + c) * kC + i;
 #pragma unroll
-    for (int u = 0; u < 64; u += 8) {
-      const float4 p0 = *reinterpret_cast<const float4*>(src + u);
-      const float4 p1 = *reinterpret_cast<const float4*>(src + u + 4);
-      float y[8] = {p0.x + acc[u], p0.y + acc[u + 1], p0.z + acc[u + 2], p0.w + acc[u + 3],
-                    p1.x + acc[u + 4], p1.y + acc[u + 5], p1.z + acc[u + 6], p1.w + acc[u + 7]};
-      *reinterpret_cast<uint4*>(dst + u) = a.dtype == NGDN2_BF16 ? pack8(y) : pack8h(y);
+      for (int hh = 0; hh < 2; ++hh) {
+        float y[32];
+        tmem_ld32(taddr(tb + 128 * c, 32 * quarter, c0 + 32 * hh), y);
+        if (t < a.T) {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) +
+                                                ((int64_t(b) * a.T + t) * a.H + h) * TV + c0 + 32 * hh);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float f[8];
+            unpack8(dst[u], a.dtype, f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] += y[8 * u + e];
+            dst[u] = a.dtype == NGDN2_BF16 ? pack8(f) : pack8h(f);
+          }
+        }
+      }
     }
   }
   if (abort_flag && tid == 0 && a.status) atomicOr(a.status, NGDN2_STATUS_WAIT_TIMEOUT);
@@ -1092,7 +1116,6 @@ static cudaError_t scan_level(const FwdParams& p, const SegLayout& lay, char* ws
   a.L = p.L;
   a.H = p.H;
   a.T = p.T;
-  a.NTp = p.NT;
   a.nsteps = level_steps(p, l);
   a.seglen = lay.seglen[l];
   a.nseg = lay.nseg[l];
@@ -1107,8 +1130,7 @@ static cudaError_t scan_level(const FwdParams& p, const SegLayout& lay, char* ws
   const int rows = level_rows(p, l);
   if (l == 0) {
     a.recs = ws + lay.tc.chunks_off;
-    a.out = p.L > 1 ? 1 : 2;
-    a.o0 = reinterpret_cast<float*>(ws + lay.o0_off);
+    a.out = 1;
     a.o = p.o;
     a.dtype = p.dtype;
   } else {
@@ -1123,7 +1145,7 @@ static cudaError_t scan_level(const FwdParams& p, const SegLayout& lay, char* ws
     err = rows == 64 ? launch_scan<64>(c, true, 2 * (a.nseg - 1), p.B, stream)
                      : launch_scan<128>(c, true, 2 * (a.nseg - 1), p.B, stream);
     if (err != cudaSuccess) return err;
-    const int smem = 4 * kStateBytes;
+    const int smem = 6 * kStateBytes;
     err = cudaFuncSetAttribute(seg_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
     seg_combine_kernel<<<dim3(p.H, p.B), kSegThreads, smem, stream>>>(
@@ -1164,11 +1186,21 @@ static cudaError_t probe_level(const FwdParams& p, const SegLayout& lay, char* w
   return cudaGetLastError();
 }
 
+// Chunks per read CTA: the largest of 4, 2, 1 dividing every upper level's
+// firing interval (so a unit's chunks share each level's group).
+static int read_unit(const FwdParams& p) {
+  int u = kReadUnit;
+  for (int l = 1; l < p.L; ++l)
+    while (u > 1 && p.firing[l] % u) u >>= 1;
+  return u;
+}
+
 static cudaError_t read_levels(const FwdParams& p, const SegLayout& lay, char* ws,
                                cudaStream_t stream) {
   ReadArgs a;
   memset(&a, 0, sizeof(a));
   a.B = p.B; a.T = p.T; a.H = p.H; a.L = p.L; a.NT = p.NT;
+  a.unit = read_unit(p);
   for (int l = 1; l < p.L; ++l) {
     a.firing[l] = p.firing[l];
     a.E[l] = reinterpret_cast<const bf16*>(ws + lay.E_off[l]);
@@ -1177,17 +1209,17 @@ static cudaError_t read_levels(const FwdParams& p, const SegLayout& lay, char* w
   a.q = p.q;
   a.mix = p.mix;
   a.scale = p.scale;
-  a.o0 = reinterpret_cast<const float*>(ws + lay.o0_off);
   a.o = p.o;
   a.dtype = p.dtype;
   a.status = p.status;
   CUtensorMap qmap;
   if (!tc_make_q_map(p, &qmap, &a.hl_mode)) return cudaErrorInvalidValue;
-  const int smem = kReadLevels * (kStateBytes + TILE_QK) + 1024;
+  const int smem = 2 * kReadStage + 1024;
   cudaError_t err =
       cudaFuncSetAttribute(seg_read_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
-  seg_read_kernel<<<dim3(p.NT, p.H, p.B), kReadThreads, smem, stream>>>(a, qmap);
+  seg_read_kernel<<<dim3((p.NT + a.unit - 1) / a.unit, p.H, p.B), kReadThreads, smem, stream>>>(
+      a, qmap);
   return cudaGetLastError();
 }
 

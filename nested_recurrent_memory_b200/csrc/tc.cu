@@ -131,37 +131,56 @@ __device__ __forceinline__ int kgroup_elems(int J) {
 }
 
 
-__global__ void __launch_bounds__(kPrepThreads, 2)
-prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ PrepMaps maps) {
-  if (gate_closed(p)) return;
-  extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ uint64_t bar;
-  __shared__ uint32_t tbase;
+// A chunk's raw inputs: raw(i, d0) is the raw 16 bytes of columns
+// d0 .. d0 + 7 of this thread's row of q_0, k, b, v or w (i = 0..4), loaded
+// through the load/store unit with the tensors' own strides; graw / gf32 the
+// same for g. Rows past T read as zeros.
+struct GlobalInputs {
+  const FwdParams* p;
+  int b, h, t;
+  bool valid;
+  __device__ static GlobalInputs make(const FwdParams& p, int b, int h, int t, bool valid) {
+    return GlobalInputs{&p, b, h, t, valid};
+  }
+  __device__ __forceinline__ uint4 raw(int i, int d0) const {
+    if (!valid) return make_uint4(0, 0, 0, 0);
+    switch (i) {
+      case 0: return raw8_at(p->q.p, p->q.dt, p->q.off(b, t, h, 0, d0), p->q.sd);
+      case 1: return raw8_at(p->k.p, p->k.dt, p->k.off(b, t, h, d0), p->k.sd);
+      case 2: return raw8_at(p->b.p, p->b.dt, p->b.off(b, t, h, d0), p->b.sd);
+      case 3: return raw8_at(p->v.p, p->v.dt, p->v.off(b, t, h, d0), p->v.sd);
+      default: return raw8_at(p->w.p, p->w.dt, p->w.off(b, t, h, d0), p->w.sd);
+    }
+  }
+  __device__ __forceinline__ uint4 graw(int d0) const {
+    return valid ? raw8_at(p->g.p, p->g.dt, p->g.off(b, t, h, d0), p->g.sd) : make_uint4(0, 0, 0, 0);
+  }
+  __device__ __forceinline__ void gf32(int d0, float* out) const {
+    if (valid) {
+      load8(p->g, b, t, h, d0, out);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) out[u] = 0.f;
+    }
+  }
+};
+
+// One chunk (n of head h, batch row b) of the prep: the operands, the two
+// MMAs and the inverse, writing the chunk's record (see the kernel below).
+// ``bar`` is the MMA mbarrier (two phases per chunk), ``tb`` 256 TMEM
+// columns.
+__device__ __forceinline__ void prep_chunk(const FwdParams& p, const TcLayout& lay, char* ws,
+                                           uint8_t* sm, int b, int h, int n, uint64_t& bar,
+                                           uint32_t tb) {
   __shared__ float mixs[1][kC];             // mix_0 * scale per row
   __shared__ __align__(16) float rho[5][TK];  // G[16J + 7] for J = 0..3, then G[63]
   // [0]: e^(G_63 - rho_3); [J]: e^(rho_J - rho_(J-1)), J = 1..3; [4 + I]: e^(rho_I)
   __shared__ __align__(16) float rat[8][TK];
   float* Tt = reinterpret_cast<float*>(sm + P_TT);
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = n * kC;
   char* rec = ws + lay.chunks_off + ((int64_t(b) * p.H + h) * p.NT + n) * lay.rec.size;
 
-  // One L2 prefetch per input tensor of this chunk's rows: the column
-  // chunks that the loads below fetch one at a time then come from L2.
-  if (tid < 6 && (maps.valid >> tid & 1u)) tc::tma_prefetch_l2_3d(&maps.m[tid], 0, b * p.T + t0, h);
-  // g is the first input the kernel waits on. Blocks start in index order as
-  // slots free up, so the block two waves ahead (this index + two CTAs per
-  // SM) takes this slot about one CTA lifetime from now: its g rows are
-  // pulled into L2 as well, so that its first wait sees L2 latency.
-  if (tid == 32 && (maps.valid & 2u)) {
-    uint32_t nsm;
-    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
-    const int64_t lin2 = n + int64_t(p.NT) * (h + int64_t(p.H) * b) + 2 * int64_t(nsm);
-    const int64_t b2 = lin2 / (int64_t(p.NT) * p.H);
-    if (b2 < p.B)
-      tc::tma_prefetch_l2_3d(&maps.m[1], 0, int(b2 * p.T + (lin2 % p.NT) * kC), int(lin2 / p.NT % p.H));
-  }
   // Phase A mapping: warp w owns rows 8w .. 8w+7; lane = 8 * c4 + r8 holds
   // row 8w + r8 and the 8-column chunks c4, c4 + 4, c4 + 8, c4 + 12. A warp
   // load then touches 8 rows x 64 contiguous bytes, and the 16-byte shared
@@ -171,21 +190,14 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   const bool valid = t < p.T;
   bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
   bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
+  const GlobalInputs in = GlobalInputs::make(p, b, h, t, valid);
 
   // Raw 16-byte chunks of q_0, k, b, v, w for one column chunk; each
   // chunk's loads are issued one chunk ahead of their use.
   auto fetch = [&](int ci, uint4* raw) {
     const int d0 = 8 * (c4 + 4 * ci);
-    if (valid) {
-      raw[0] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, 0, d0), p.q.sd);
-      raw[1] = raw8_at(p.k.p, p.k.dt, p.k.off(b, t, h, d0), p.k.sd);
-      raw[2] = raw8_at(p.b.p, p.b.dt, p.b.off(b, t, h, d0), p.b.sd);
-      raw[3] = raw8_at(p.v.p, p.v.dt, p.v.off(b, t, h, d0), p.v.sd);
-      raw[4] = raw8_at(p.w.p, p.w.dt, p.w.off(b, t, h, d0), p.w.sd);
-    } else {
 #pragma unroll
-      for (int i = 0; i < 5; ++i) raw[i] = make_uint4(0, 0, 0, 0);
-    }
+    for (int i = 0; i < 5; ++i) raw[i] = in.raw(i, d0);
   };
   uint4 cur[5], nxt[5];
 
@@ -200,14 +212,8 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
 #pragma unroll
   for (int ci = 0; ci < 4; ++ci) {
     const int d0 = 8 * (c4 + 4 * ci);
-    if (g16) {
-      graw[ci] = valid ? raw8_at(p.g.p, p.g.dt, p.g.off(b, t, h, d0), p.g.sd) : make_uint4(0, 0, 0, 0);
-    } else if (valid) {
-      load8(p.g, b, t, h, d0, G[ci]);
-    } else {
-#pragma unroll
-      for (int u = 0; u < 8; ++u) G[ci][u] = 0.f;
-    }
+    if (g16) graw[ci] = in.graw(d0);
+    else in.gf32(d0, G[ci]);
   }
   fetch(0, cur);
   uint32_t mix_bits = 0;
@@ -215,11 +221,6 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
     const int64_t o = p.mix.off(b, t0 + tid, h, 0);
     mix_bits = p.mix.dt == NGDN2_F32 ? __float_as_uint(reinterpret_cast<const float*>(p.mix.p)[o])
                                      : uint32_t(reinterpret_cast<const uint16_t*>(p.mix.p)[o]);
-  }
-  if (warp == 0) tmem_alloc(&tbase, kPrepCols);
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
   }
   if (g16) {
 #pragma unroll
@@ -280,7 +281,6 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
     for (int I2 = 0; I2 < 4; ++I2) rat[4 + I2][tid] = __expf(rho[I2][tid]);
   }
   __syncthreads();
-  const uint32_t tb = tbase;
 
   // A2. Operands. Row block I of queries uses rho_I so that
   //       Q_I[i] . K^(I)[j] = q_i . k_j e^(G_i - G_j)
@@ -625,7 +625,44 @@ prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ Prep
   }
   fence_before_sync();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tb, kPrepCols);
+}
+
+// prep_tc: grid (NT, H, B), 256 threads, two CTAs per SM; one chunk per CTA
+// with its inputs loaded by the load/store unit (any strides).
+__global__ void __launch_bounds__(kPrepThreads, 2)
+prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ PrepMaps maps) {
+  if (gate_closed(p)) return;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tbase;
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kC;
+  // One L2 prefetch per input tensor of this chunk's rows: the column
+  // chunks that the loads fetch one at a time then come from L2.
+  if (tid < 6 && (maps.valid >> tid & 1u)) tc::tma_prefetch_l2_3d(&maps.m[tid], 0, b * p.T + t0, h);
+  // g is the first input the kernel waits on. Blocks start in index order as
+  // slots free up, so the block two waves ahead (this index + two CTAs per
+  // SM) takes this slot about one CTA lifetime from now: its g rows are
+  // pulled into L2 as well, so that its first wait sees L2 latency.
+  if (tid == 32 && (maps.valid & 2u)) {
+    uint32_t nsm;
+    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+    const int64_t lin2 = n + int64_t(p.NT) * (h + int64_t(p.H) * b) + 2 * int64_t(nsm);
+    const int64_t b2 = lin2 / (int64_t(p.NT) * p.H);
+    if (b2 < p.B)
+      tc::tma_prefetch_l2_3d(&maps.m[1], 0, int(b2 * p.T + (lin2 % p.NT) * kC), int(lin2 / p.NT % p.H));
+  }
+  if (warp == 0) tmem_alloc(&tbase, kPrepCols);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  prep_chunk(p, lay, ws, sm, b, h, n, bar, tbase);
+  if (warp == 0) tmem_dealloc(tbase, kPrepCols);
 }
 
 }  // namespace
