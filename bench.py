@@ -215,25 +215,75 @@ class ClockSampler:
 # CPU baseline: the oracle on a bounded sample
 # ---------------------------------------------------------------------------
 
-def cpu_sample_run(w, heads, seed=0):
-    """One bounded sample: one batch row, ``heads`` heads, the full T, in
-    fp32 through the oracle. Returns (seconds, token-heads processed)."""
+REF_ROOT = ROOT / "baseline" / "_ref"
+
+
+def reference_naive():
+    """The reference's own CPU implementation of the path,
+    ``naive_chunk_nested_gdn2`` (nested_gdn2/ops/naive.py:226-420), from the
+    unmodified install in baseline/_ref, or None when it is not installed.
+    Its parent packages are stubs: the package ``__init__`` registers the HF
+    model, which imports a newer flash-linear-attention than this image
+    has; the op modules themselves need torch only."""
+    import types
+    naive_py = REF_ROOT / "nested_gdn2" / "ops" / "naive.py"
+    if not naive_py.exists():
+        return None
+    sys.dont_write_bytecode = True
+    for name, sub in (("nested_gdn2", ""), ("nested_gdn2.ops", "ops")):
+        if name not in sys.modules:
+            mod = types.ModuleType(name)
+            mod.__path__ = [str(REF_ROOT / "nested_gdn2" / sub) if sub else str(REF_ROOT / "nested_gdn2")]
+            sys.modules[name] = mod
+    try:
+        from nested_gdn2.ops.naive import naive_chunk_nested_gdn2
+    except Exception:
+        return None
+    return naive_chunk_nested_gdn2
+
+
+def cpu_sample_run(w, heads, seed=0, T=None):
+    """One bounded sample: one batch row, ``heads`` heads, the first ``T``
+    tokens (default the full T), in fp32 on the host cores: the reference's
+    own naive_chunk_nested_gdn2 with torch using every host thread when it
+    is installed, else the numpy restatement in oracle/. Returns (seconds,
+    token-heads processed, kind)."""
     import numpy as np
     import torch
 
-    import oracle  # CPU baseline leg only
     from nested_recurrent_memory_b200.synthetic import config_inputs
 
-    inp = config_inputs(1, w["T"], heads, w["K"], w["V"], w["L"], w["m"], w["firing"],
+    T = T or w["T"]
+    inp = config_inputs(1, T, heads, w["K"], w["V"], w["L"], w["m"], w["firing"],
                         dtype=torch.float32, seed=seed)
     L = inp.pop("L")
+    ref = reference_naive()
+    if ref is not None:
+        torch.set_num_threads(os.cpu_count() or 1)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            ref(**inp, L=L, output_final_state=True)
+        return time.perf_counter() - t0, T * heads, "reference"
+    import oracle  # CPU baseline leg only (the reference is not installed)
     a = {k: (v.numpy() if torch.is_tensor(v) else v) for k, v in inp.items()}
     t0 = time.perf_counter()
     oracle.chunk_forward(**a, L=L, output_final_state=True, dtype=np.float32)
-    return time.perf_counter() - t0, w["T"] * heads
+    return time.perf_counter() - t0, T * heads, "port"
 
 
-def cpu_threads():
+def cpu_sample_shape(w):
+    """Heads and tokens of one CPU sample: about 2-10 s of host work (the
+    reference's naive op holds a [heads, T / 64, 64, 64, K] decay tensor,
+    so long sequences are sampled by a prefix)."""
+    if w["T"] > 16384:
+        return 1, 16384
+    return 4, w["T"]
+
+
+def cpu_threads(kind="port"):
+    if kind == "reference":
+        import torch
+        return torch.get_num_threads()
     try:
         from threadpoolctl import threadpool_info
         n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
@@ -249,26 +299,29 @@ def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    heads = 4
+    heads, T = cpu_sample_shape(w)
     for _ in range(args.warmup):
-        cpu_sample_run(w, heads)
+        cpu_sample_run(w, heads, T=T)
     secs = []
+    kind = "port"
     for i in range(args.steps):
-        s, th = cpu_sample_run(w, heads, seed=i)
+        s, th, kind = cpu_sample_run(w, heads, seed=i, T=T)
         secs.append(s)
     total = sum(secs)
     # token-heads/s divided by H: tokens of the configuration per second
-    value = args.steps * w["T"] * heads / w["H"] / total
-    sample = (f"per step: 1 of {w['B']} batch rows, {heads} of {w['H']} heads, T={w['T']}, "
-              "fp32 numpy oracle (restated reference naive_chunk_nested_gdn2)")
+    value = args.steps * T * heads / w["H"] / total
+    what = ("the reference's naive_chunk_nested_gdn2 (baseline/_ref, unmodified), torch fp32"
+            if kind == "reference" else
+            "fp32 numpy oracle (restated reference naive_chunk_nested_gdn2)")
+    sample = f"per step: 1 of {w['B']} batch rows, {heads} of {w['H']} heads, T={T}, {what}"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(args, w),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_threads(),
-                         "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_threads(kind),
+                         "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -515,13 +568,15 @@ def run_ours(args, w):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        heads = 2 if w["T"] > 16384 else 16
-        secs, th = cpu_sample_run(w, heads)
-        cpu = {"value": th / w["H"] / secs, "unit": "tokens/s", "cores": cpu_threads(),
-               "kind": "port",
-               "sample": (f"1 of {w['B']} batch rows, {heads} of {w['H']} heads, T={w['T']} "
-                          f"({secs:.1f} s), fp32 numpy oracle (restated reference "
-                          "naive_chunk_nested_gdn2)")}
+        heads, T = cpu_sample_shape(w)
+        secs, th, kind = cpu_sample_run(w, heads, T=T)
+        what = ("the reference's naive_chunk_nested_gdn2 (baseline/_ref, unmodified), torch fp32"
+                if kind == "reference" else
+                "fp32 numpy oracle (restated reference naive_chunk_nested_gdn2)")
+        cpu = {"value": th / w["H"] / secs, "unit": "tokens/s", "cores": cpu_threads(kind),
+               "kind": kind,
+               "sample": (f"1 of {w['B']} batch rows, {heads} of {w['H']} heads, T={T} "
+                          f"({secs:.1f} s), {what}")}
 
     if rank == 0:
         line = {
