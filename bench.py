@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling runs on a smaller case)")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="override the number of heads (profiling runs on a smaller case)")
     ap.add_argument("--model", action="store_true",
                     help="time the full-model forward harness (BASELINE config 4: 12-layer "
                          "NestedGDN-2 LM, B=32 sharded over the GPUs, T=4096); prints its own line")
@@ -785,6 +787,8 @@ def main():
     w = workload(args.config)
     if args.batch is not None:
         w["B"] = args.batch
+    if args.heads is not None:
+        w["H"] = args.heads
     if args.decode:
         run_decode(args, w)
     elif args.backward:

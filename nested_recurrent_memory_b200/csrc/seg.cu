@@ -142,7 +142,6 @@ inline SegLayout seg_layout(const FwdParams& p) {
   memset(&s, 0, sizeof(s));
   const int64_t bh = int64_t(p.B) * p.H;
   s.tc.rec = TcRecord::make(1);
-  s.tc.params32_off = 0;
   s.tc.ptc_off = 0;
   int64_t off = int64_t(p.L > 1 ? p.L - 1 : 0) * p.H * PT_SIZE;
   s.tc.chunks_off = align256(off);

@@ -15,12 +15,14 @@
 //   scan_tc  -- one CTA per (b, h). The level-0 state S0 lives in TMEM
 //               (fp32, lanes = key index) for the whole sequence, a bf16
 //               copy of every level's state sits in shared memory as the
-//               MMA B operand. Per chunk: one bulk copy brings the record in,
-//               MMA1 forms W.S0 and the multi-level read sum_l Q_l.S_l, the
-//               epilogue forms v_new = U - W.S0 while other warps decay S0 in
-//               TMEM, MMA2 adds A_qk.v_new to the output and K_tail^T.v_new to
-//               S0. Promotions of levels >= 1 run at their firings on CUDA
-//               cores in fp32 against the fp32 master states.
+//               MMA B operand. Per chunk: bulk copies bring the record in,
+//               MMA1 forms W.S0 and the level-0 read, the upper levels' reads
+//               q_l.S_l run during E1 (v_new = U - W.S0), MMA2 adds
+//               A_qk.v_new to the output and K_tail^T.v_new to S0, and E2
+//               mixes the levels per row. Promotions of levels >= 1 run at
+//               their firings as tcgen05 MMA round trips (promote_tc for the
+//               learned arm, promote_merge_tc for the merge arm) against fp32
+//               master states.
 //
 // Reference: level 0 follows nested_gdn2/ops/naive.py:329-392 (chunk form of
 // fla's GDN-2, chunk.py:236-248), reads and mix naive.py:382-390, promotion
@@ -30,14 +32,12 @@
 #include <string.h>
 #include <cudaTypedefs.h>
 
-#include "promote_simt.cuh"
 #include "tc_api.cuh"
 #include "tc_common.cuh"
 #include "tc_ptx.cuh"
 
 namespace ngdn2 {
 
-cudaError_t launch_convert_params(const FwdParams& p, cudaStream_t stream);
 
 namespace {
 
@@ -131,56 +131,37 @@ __device__ __forceinline__ int kgroup_elems(int J) {
 }
 
 
-// A chunk's raw inputs: raw(i, d0) is the raw 16 bytes of columns
-// d0 .. d0 + 7 of this thread's row of q_0, k, b, v or w (i = 0..4), loaded
-// through the load/store unit with the tensors' own strides; graw / gf32 the
-// same for g. Rows past T read as zeros.
-struct GlobalInputs {
-  const FwdParams* p;
-  int b, h, t;
-  bool valid;
-  __device__ static GlobalInputs make(const FwdParams& p, int b, int h, int t, bool valid) {
-    return GlobalInputs{&p, b, h, t, valid};
-  }
-  __device__ __forceinline__ uint4 raw(int i, int d0) const {
-    if (!valid) return make_uint4(0, 0, 0, 0);
-    switch (i) {
-      case 0: return raw8_at(p->q.p, p->q.dt, p->q.off(b, t, h, 0, d0), p->q.sd);
-      case 1: return raw8_at(p->k.p, p->k.dt, p->k.off(b, t, h, d0), p->k.sd);
-      case 2: return raw8_at(p->b.p, p->b.dt, p->b.off(b, t, h, d0), p->b.sd);
-      case 3: return raw8_at(p->v.p, p->v.dt, p->v.off(b, t, h, d0), p->v.sd);
-      default: return raw8_at(p->w.p, p->w.dt, p->w.off(b, t, h, d0), p->w.sd);
-    }
-  }
-  __device__ __forceinline__ uint4 graw(int d0) const {
-    return valid ? raw8_at(p->g.p, p->g.dt, p->g.off(b, t, h, d0), p->g.sd) : make_uint4(0, 0, 0, 0);
-  }
-  __device__ __forceinline__ void gf32(int d0, float* out) const {
-    if (valid) {
-      load8(p->g, b, t, h, d0, out);
-    } else {
-#pragma unroll
-      for (int u = 0; u < 8; ++u) out[u] = 0.f;
-    }
-  }
-};
-
-// One chunk (n of head h, batch row b) of the prep: the operands, the two
-// MMAs and the inverse, writing the chunk's record (see the kernel below).
-// ``bar`` is the MMA mbarrier (two phases per chunk), ``tb`` 256 TMEM
-// columns.
-__device__ __forceinline__ void prep_chunk(const FwdParams& p, const TcLayout& lay, char* ws,
-                                           uint8_t* sm, int b, int h, int n, uint64_t& bar,
-                                           uint32_t tb) {
+__global__ void __launch_bounds__(kPrepThreads, 2)
+prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ PrepMaps maps) {
+  if (gate_closed(p)) return;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tbase;
   __shared__ float mixs[1][kC];             // mix_0 * scale per row
   __shared__ __align__(16) float rho[5][TK];  // G[16J + 7] for J = 0..3, then G[63]
   // [0]: e^(G_63 - rho_3); [J]: e^(rho_J - rho_(J-1)), J = 1..3; [4 + I]: e^(rho_I)
   __shared__ __align__(16) float rat[8][TK];
   float* Tt = reinterpret_cast<float*>(sm + P_TT);
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = n * kC;
   char* rec = ws + lay.chunks_off + ((int64_t(b) * p.H + h) * p.NT + n) * lay.rec.size;
 
+  // One L2 prefetch per input tensor of this chunk's rows: the column
+  // chunks that the loads below fetch one at a time then come from L2.
+  if (tid < 6 && (maps.valid >> tid & 1u)) tc::tma_prefetch_l2_3d(&maps.m[tid], 0, b * p.T + t0, h);
+  // g is the first input the kernel waits on. Blocks start in index order as
+  // slots free up, so the block two waves ahead (this index + two CTAs per
+  // SM) takes this slot about one CTA lifetime from now: its g rows are
+  // pulled into L2 as well, so that its first wait sees L2 latency.
+  if (tid == 32 && (maps.valid & 2u)) {
+    uint32_t nsm;
+    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+    const int64_t lin2 = n + int64_t(p.NT) * (h + int64_t(p.H) * b) + 2 * int64_t(nsm);
+    const int64_t b2 = lin2 / (int64_t(p.NT) * p.H);
+    if (b2 < p.B)
+      tc::tma_prefetch_l2_3d(&maps.m[1], 0, int(b2 * p.T + (lin2 % p.NT) * kC), int(lin2 / p.NT % p.H));
+  }
   // Phase A mapping: warp w owns rows 8w .. 8w+7; lane = 8 * c4 + r8 holds
   // row 8w + r8 and the 8-column chunks c4, c4 + 4, c4 + 8, c4 + 12. A warp
   // load then touches 8 rows x 64 contiguous bytes, and the 16-byte shared
@@ -190,14 +171,21 @@ __device__ __forceinline__ void prep_chunk(const FwdParams& p, const TcLayout& l
   const bool valid = t < p.T;
   bf16* Qg = reinterpret_cast<bf16*>(rec + lay.rec.Q);
   bf16* Ktg = reinterpret_cast<bf16*>(rec + lay.rec.Kt);
-  const GlobalInputs in = GlobalInputs::make(p, b, h, t, valid);
 
   // Raw 16-byte chunks of q_0, k, b, v, w for one column chunk; each
   // chunk's loads are issued one chunk ahead of their use.
   auto fetch = [&](int ci, uint4* raw) {
     const int d0 = 8 * (c4 + 4 * ci);
+    if (valid) {
+      raw[0] = raw8_at(p.q.p, p.q.dt, p.q.off(b, t, h, 0, d0), p.q.sd);
+      raw[1] = raw8_at(p.k.p, p.k.dt, p.k.off(b, t, h, d0), p.k.sd);
+      raw[2] = raw8_at(p.b.p, p.b.dt, p.b.off(b, t, h, d0), p.b.sd);
+      raw[3] = raw8_at(p.v.p, p.v.dt, p.v.off(b, t, h, d0), p.v.sd);
+      raw[4] = raw8_at(p.w.p, p.w.dt, p.w.off(b, t, h, d0), p.w.sd);
+    } else {
 #pragma unroll
-    for (int i = 0; i < 5; ++i) raw[i] = in.raw(i, d0);
+      for (int i = 0; i < 5; ++i) raw[i] = make_uint4(0, 0, 0, 0);
+    }
   };
   uint4 cur[5], nxt[5];
 
@@ -212,8 +200,14 @@ __device__ __forceinline__ void prep_chunk(const FwdParams& p, const TcLayout& l
 #pragma unroll
   for (int ci = 0; ci < 4; ++ci) {
     const int d0 = 8 * (c4 + 4 * ci);
-    if (g16) graw[ci] = in.graw(d0);
-    else in.gf32(d0, G[ci]);
+    if (g16) {
+      graw[ci] = valid ? raw8_at(p.g.p, p.g.dt, p.g.off(b, t, h, d0), p.g.sd) : make_uint4(0, 0, 0, 0);
+    } else if (valid) {
+      load8(p.g, b, t, h, d0, G[ci]);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) G[ci][u] = 0.f;
+    }
   }
   fetch(0, cur);
   uint32_t mix_bits = 0;
@@ -221,6 +215,11 @@ __device__ __forceinline__ void prep_chunk(const FwdParams& p, const TcLayout& l
     const int64_t o = p.mix.off(b, t0 + tid, h, 0);
     mix_bits = p.mix.dt == NGDN2_F32 ? __float_as_uint(reinterpret_cast<const float*>(p.mix.p)[o])
                                      : uint32_t(reinterpret_cast<const uint16_t*>(p.mix.p)[o]);
+  }
+  if (warp == 0) tmem_alloc(&tbase, kPrepCols);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
   }
   if (g16) {
 #pragma unroll
@@ -281,6 +280,7 @@ __device__ __forceinline__ void prep_chunk(const FwdParams& p, const TcLayout& l
     for (int I2 = 0; I2 < 4; ++I2) rat[4 + I2][tid] = __expf(rho[I2][tid]);
   }
   __syncthreads();
+  const uint32_t tb = tbase;
 
   // A2. Operands. Row block I of queries uses rho_I so that
   //       Q_I[i] . K^(I)[j] = q_i . k_j e^(G_i - G_j)
@@ -625,44 +625,7 @@ __device__ __forceinline__ void prep_chunk(const FwdParams& p, const TcLayout& l
   }
   fence_before_sync();
   __syncthreads();
-}
-
-// prep_tc: grid (NT, H, B), 256 threads, two CTAs per SM; one chunk per CTA
-// with its inputs loaded by the load/store unit (any strides).
-__global__ void __launch_bounds__(kPrepThreads, 2)
-prep_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ PrepMaps maps) {
-  if (gate_closed(p)) return;
-  extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ uint64_t bar;
-  __shared__ uint32_t tbase;
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int t0 = n * kC;
-  // One L2 prefetch per input tensor of this chunk's rows: the column
-  // chunks that the loads fetch one at a time then come from L2.
-  if (tid < 6 && (maps.valid >> tid & 1u)) tc::tma_prefetch_l2_3d(&maps.m[tid], 0, b * p.T + t0, h);
-  // g is the first input the kernel waits on. Blocks start in index order as
-  // slots free up, so the block two waves ahead (this index + two CTAs per
-  // SM) takes this slot about one CTA lifetime from now: its g rows are
-  // pulled into L2 as well, so that its first wait sees L2 latency.
-  if (tid == 32 && (maps.valid & 2u)) {
-    uint32_t nsm;
-    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
-    const int64_t lin2 = n + int64_t(p.NT) * (h + int64_t(p.H) * b) + 2 * int64_t(nsm);
-    const int64_t b2 = lin2 / (int64_t(p.NT) * p.H);
-    if (b2 < p.B)
-      tc::tma_prefetch_l2_3d(&maps.m[1], 0, int(b2 * p.T + (lin2 % p.NT) * kC), int(lin2 / p.NT % p.H));
-  }
-  if (warp == 0) tmem_alloc(&tbase, kPrepCols);
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
-  fence_before_sync();
-  __syncthreads();
-  fence_after_sync();
-  prep_chunk(p, lay, ws, sm, b, h, n, bar, tbase);
-  if (warp == 0) tmem_dealloc(tbase, kPrepCols);
+  if (warp == 0) tmem_dealloc(tb, kPrepCols);
 }
 
 }  // namespace
@@ -686,7 +649,7 @@ constexpr int kPromoScratch = 98304;
 // upper levels' query tiles (L - 1), the v_new tile and the CUDA-core
 // promotion's GEMM staging; promotions reuse everything after the states.
 __host__ __device__ inline int64_t scan_tc_smem(int L, const TcRecord& rec) {
-  const int64_t tail = rec.load_bytes + int64_t(L - 1) * TILE_QK + TILE_QK + kGemmSmemFloats * 4;
+  const int64_t tail = rec.load_bytes + int64_t(L - 1) * TILE_QK + TILE_QK;
   return int64_t(L) * TILE_S + (tail > kPromoScratch ? tail : kPromoScratch) + 1024;
 }
 
@@ -1016,6 +979,137 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   fence_after_sync();
 }
 
+// Merge promotion of level l - 1 into level l on the tensor cores
+// (probe.py:105-136 with the gates of :34-66, naive.py:7-39): the values are
+// the rows of S_{l-1} and the keys the identity, so the gram matrix is
+// diag(b[k][k]) and the update is row by row,
+//     S_l[k] <- (1 - b[k][k]) e^(g_k) S_l[k] + S_{l-1}[k] * w[k],
+// with w = sigmoid(S_{l-1} . W_w), b = sigmoid(S_{l-1} . W_b - 4) and
+// g = mean_k(-softplus(S_{l-1} . W_g - 4)). The three gate GEMMs run as two
+// M = 128, N = 256 MMAs ([W_w | W_g] and [W_k^T | W_b]; the W_k^T half is
+// unused) on a bf16 copy of S_{l-1}; the update reads and writes the fp32
+// masters in final_state. Same TMEM columns and scratch as promote_tc.
+__device__ void promote_merge_tc(const FwdParams& p, const TcLayout& lay, const char* ws, int h,
+                                 int l, uint32_t tb, bf16* Sbf, uint8_t* X, float* Sg,
+                                 uint64_t* bar_ld, uint64_t* bar_mma, uint32_t& ph_ld,
+                                 uint32_t& ph_mma, float* egp, float* red, int* abort_flag) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, c0 = 32 * (warp >> 2);
+  const int row = 32 * quarter + lane;  // pair index = key index
+  const char* pt = ws + lay.ptc_off + (int64_t(l - 1) * p.H + h) * PT_SIZE;
+  bf16* XW = reinterpret_cast<bf16*>(X);
+  bf16* XQ = reinterpret_cast<bf16*>(X + 65536);
+  const uint32_t tV = tb + 128, tG = tb + 256;
+  const uint32_t id_gate = idesc_f16(128, 256, true, false, false);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_ld, 65536u);
+    bulk_g2s(XW, pt + PT_W2B, 65536u, bar_ld);
+  }
+  // V' = S_{l-1} as a K-major A operand: the bf16 copy's 16-byte pieces
+  // (8 values of one row) reordered from the MN-major B layout.
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(Sbf + (l - 1) * TK * TV);
+    uint4* dst = reinterpret_cast<uint4*>(XQ);
+    for (int e = tid; e < TK * TV / 8; e += kScanThreads) {
+      const int e8 = e & 7, kg = (e >> 3) & 15, vg = e >> 7;
+      dst[((kg * 16 + vg) << 3) + e8] = src[e];
+    }
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  if (!mbar_wait(bar_ld, ph_ld)) *abort_flag = 1;
+  ph_ld ^= 1;
+  if (tid == 0) {
+    fence_after_sync();
+    mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    mma_commit(bar_mma);
+  }
+  __syncwarp();
+  if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
+  ph_mma ^= 1;
+  fence_after_sync();
+  // w = sigmoid(w_logit) into TMEM; -softplus(g_logit - 4) per pair into the
+  // (spent) [W_w | W_g] buffer, columns XOR-swizzled by row.
+  float* gpart = reinterpret_cast<float*>(X);
+  {
+    float a[32];
+    tmem_ld32(taddr(tG, 32 * quarter, c0), a);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) a[u] = sigmoidf_(a[u] + kWLogitInit);
+    tmem_st32(taddr(tV, 32 * quarter, c0), a);
+    tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), a);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -softplusf_(a[u] + kGLogitInit);
+  }
+  tmem_wait_st();
+  __syncthreads();
+  {
+    const int k = tid & 127, qq = tid >> 7;
+    float sum = 0.f;
+    for (int r = qq * 32; r < qq * 32 + 32; ++r) sum += gpart[r * 128 + (k ^ (r & 31))];
+    red[qq * 128 + k] = sum;
+  }
+  __syncthreads();
+  if (tid < 128) egp[tid] = expf((red[tid] + red[128 + tid] + red[256 + tid] + red[384 + tid]) / 128.f);
+  fence_proxy_async();
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_ld, 65536u);
+    bulk_g2s(XW, pt + PT_W2A, 65536u, bar_ld);
+  }
+  if (!mbar_wait(bar_ld, ph_ld)) *abort_flag = 1;
+  ph_ld ^= 1;
+  if (tid == 0) {
+    fence_after_sync();
+    mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+    mma_commit(bar_mma);
+  }
+  __syncwarp();
+  if (!mbar_wait(bar_mma, ph_mma)) *abort_flag = 1;
+  ph_mma ^= 1;
+  fence_after_sync();
+  // b[k][k] from the warps whose 32 columns hold row k's diagonal.
+  if ((warp >> 2) == quarter) {
+    float a[32];
+    tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), a);
+    float d = 0.f;
+#pragma unroll
+    for (int u = 0; u < 32; ++u)
+      if (u == lane) d = a[u];
+    red[row] = sigmoidf_(d + kBLogitInit);
+  }
+  __syncthreads();
+  {
+    const int k = row;
+    const float e = egp[k], keep = 1.f - red[k];
+    float w[32];
+    tmem_ld32(taddr(tV, 32 * quarter, c0), w);
+    float* Sl = Sg + int64_t(l) * TK * TV + k * TV + c0;
+    const float* Sb = Sg + int64_t(l - 1) * TK * TV + k * TV + c0;
+    float x[32];
+#pragma unroll
+    for (int t = 0; t < 32; t += 4) {
+      const float4 sl = *reinterpret_cast<const float4*>(Sl + t);
+      const float4 sb = *reinterpret_cast<const float4*>(Sb + t);
+      x[t] = keep * e * sl.x + sb.x * w[t];
+      x[t + 1] = keep * e * sl.y + sb.y * w[t + 1];
+      x[t + 2] = keep * e * sl.z + sb.z * w[t + 2];
+      x[t + 3] = keep * e * sl.w + sb.w * w[t + 3];
+    }
+#pragma unroll
+    for (int t = 0; t < 32; t += 4)
+      *reinterpret_cast<float4*>(Sl + t) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+#pragma unroll
+    for (int c = 0; c < 32; c += 8)
+      *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, c0 + c, TK)) = pack8(x + c);
+  }
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+}
+
 // qmap views q as 4-D [64 channels, (b, t) tokens, 2 channel halves,
 // (head, level) pairs] with 128-byte swizzle: one (64, 64, 2, 1) box is a
 // [64 tokens x 128] K-major MMA operand in the swizzled layout (sw128_off).
@@ -1045,12 +1139,10 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
   uint8_t* Rec = sm + int64_t(L) * TILE_S;
   uint8_t* QT = Rec + lay.rec.load_bytes;  // upper-level query tiles (sw128_off)
   bf16* Vn = reinterpret_cast<bf16*>(QT + int64_t(L - 1) * TILE_QK);
-  float* gsm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Vn) + TILE_QK);
   float* Sg = p.fin + bh * L * TK * TV;
-  float* sc = p.scan + bh * p.ss.size;
   const bool learned = p.promotion != NGDN2_PROMOTION_MERGE;
   // Learned promotions keep the upper levels' fp32 masters transposed in
-  // the workspace; merge promotions (CUDA cores) use final_state as is.
+  // the workspace; merge promotions (row by row) use final_state as is.
   float* Mt = reinterpret_cast<float*>(ws + lay.mast_off) + bh * (L > 1 ? L - 1 : 0) * TK * TV;
   const char* rec0 = ws + lay.chunks_off + bh * p.NT * lay.rec.size;
 
@@ -1433,10 +1525,8 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
       for (int l = 1; l < L; ++l) {
         if (!(fire_mask >> l & 1u)) continue;
         if (!learned) {
-          promote_simt<false>(p, b, h, l, Sg, sc, gsm);
-          refresh_copy(Sbf + l * TK * TV, Sg + l * TK * TV);
-          fence_proxy_async();
-          __syncthreads();
+          promote_merge_tc(p, lay, ws, h, l, tb, Sbf, Rec, Sg, &bar_ld, &bar_mma, ph_ld, ph_mma,
+                           egp, red, &abort_flag);
         } else {
           promote_tc(p, lay, ws, h, l, tb, Sbf, Rec, Mt, &bar_ld, &bar_mma, ph_ld, ph_mma, egp,
                      red, &abort_flag, early && l == first);
@@ -1567,15 +1657,8 @@ static void make_prep_maps(const FwdParams& p, PrepMaps* pm) {
 
 size_t tc_workspace_bytes(const FwdParams& p) { return size_t(tc_layout(p).total); }
 
-// The fp32 parameter copy feeds only the CUDA-core promotion, which the
-// tensor-core scan runs for the merge arm; learned promotions read the bf16
-// layouts of tc_params.
-static bool tc_needs_params32(const FwdParams& p) {
-  return p.L > 1 && p.promotion == NGDN2_PROMOTION_MERGE;
-}
-
 int num_launches_tc(const FwdParams& p) {
-  return (tc_needs_params32(p) ? 1 : 0) + (p.L > 1 ? 1 : 0) + (p.NT > 0 ? 1 : 0) + 1;
+  return (p.L > 1 ? 1 : 0) + (p.NT > 0 ? 1 : 0) + 1;
 }
 
 cudaError_t launch_tc_params(const FwdParams& p, const TcLayout& lay, char* ws,
@@ -1606,12 +1689,9 @@ bool tc_make_q_map(const FwdParams& p, CUtensorMap* m, int* hl_mode) {
 cudaError_t launch_fwd_tc(FwdParams p, void* workspace, int stage, cudaStream_t stream) {
   const TcLayout lay = tc_layout(p);
   char* ws = static_cast<char*>(workspace);
-  p.params32 = reinterpret_cast<float*>(ws + lay.params32_off);
-  p.scan = reinterpret_cast<float*>(ws + lay.scan_off);
   p.chunks = nullptr;
   cudaError_t err;
   if (stage == 0 || stage == 1) {
-    if (tc_needs_params32(p) && (err = launch_convert_params(p, stream)) != cudaSuccess) return err;
     if ((err = launch_tc_params(p, lay, ws, stream)) != cudaSuccess) return err;
     if ((err = launch_tc_prep(p, lay, ws, stream)) != cudaSuccess) return err;
   }

@@ -50,22 +50,21 @@ constexpr int64_t PT_W2A = 32768;
 constexpr int64_t PT_W2B = PT_W2A + 65536;
 constexpr int64_t PT_SIZE = PT_W2B + 65536;
 
+// Workspace of the fused family: the promotion operands (bf16, per level
+// and head), the chunk records, and the learned arm's fp32 masters of the
+// upper levels (transposed [V][K], per (b, h)).
 struct TcLayout {
   TcRecord rec;
-  int64_t params32_off, ptc_off, chunks_off, scan_off, mast_off, total;
+  int64_t ptc_off, chunks_off, mast_off, total;
 };
 
 __host__ __device__ inline TcLayout tc_layout(const FwdParams& p) {
   TcLayout t;
   t.rec = TcRecord::make(p.L);
-  t.params32_off = 0;
-  t.ptc_off = (p.pl.size * 4 + 255) & ~int64_t(255);
+  t.ptc_off = 0;
   t.chunks_off = t.ptc_off + int64_t(p.L > 1 ? p.L - 1 : 0) * p.H * PT_SIZE;
-  t.scan_off = t.chunks_off + int64_t(p.B) * p.H * p.NT * t.rec.size;
-  t.scan_off = (t.scan_off + 255) & ~int64_t(255);
-  t.mast_off = t.scan_off + int64_t(p.B) * p.H * p.ss.size * 4;
+  t.mast_off = t.chunks_off + int64_t(p.B) * p.H * p.NT * t.rec.size;
   t.mast_off = (t.mast_off + 255) & ~int64_t(255);
-  // fp32 masters of levels >= 1, transposed [V][K], per (b, h)
   t.total = t.mast_off + int64_t(p.B) * p.H * (p.L > 1 ? p.L - 1 : 0) * TK * TV * 4;
   return t;
 }
