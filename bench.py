@@ -56,6 +56,8 @@ def parse_args():
                     help="override the per-GPU batch (profiling runs on a smaller case)")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the number of heads (profiling runs on a smaller case)")
+    ap.add_argument("--seq", type=int, default=None,
+                    help="override the sequence length T (profiling runs on a smaller case)")
     ap.add_argument("--model", action="store_true",
                     help="time the full-model forward harness (BASELINE config 4: 12-layer "
                          "NestedGDN-2 LM, B=32 sharded over the GPUs, T=4096); prints its own line")
@@ -789,6 +791,8 @@ def main():
         w["B"] = args.batch
     if args.heads is not None:
         w["H"] = args.heads
+    if args.seq is not None:
+        w["T"] = args.seq
     if args.decode:
         run_decode(args, w)
     elif args.backward:
