@@ -111,20 +111,33 @@ inline int level_steps(const FwdParams& p, int l) {
   return l == 0 ? p.NT : p.NT / p.firing[l];
 }
 
-// Segments of a level: enough to fill the GPU with (batch, head, segment)
-// CTAs, about sqrt(3 steps) so the sequential combine (one short step per
-// segment) and the segment scans (about three times longer per step) stay
-// balanced, and at least four steps per segment.
+// Segments of a level, from a cost model of the three stages (per-step
+// times measured on B200, microseconds): the compose runs 2 (segments - 1)
+// CTAs per (batch, head) and the replay one per segment, each stepping
+// through its segment's length (in ceil(CTAs / slots) waves, slots = 2 CTAs
+// per SM for 64-row steps, 1 for 128); the combine steps once per segment
+// in sequence. The count minimising compose + combine + replay is taken,
+// with at least four steps per segment.
 inline int level_nseg(const FwdParams& p, int l) {
   const int steps = level_steps(p, l);
-  const int bh = p.B * p.H;
-  const int per_sm = level_rows(p, l) == 64 ? 2 : 1;
-  int n = (kSMs * per_sm) / (bh > 0 ? bh : 1);
-  int bal = 1;
-  while ((bal + 1) * (bal + 1) <= 3 * steps) ++bal;
-  if (bal < n) n = bal;
-  if (steps / 4 < n) n = steps / 4;
-  return n < 1 ? 1 : n;
+  const int bh = p.B * p.H > 0 ? p.B * p.H : 1;
+  const bool r64 = level_rows(p, l) == 64;
+  const int slots = kSMs * (r64 ? 2 : 1);
+  const double t_compose = r64 ? 2.9 : 4.4, t_replay = r64 ? 5.3 : 3.4, t_combine = 2.6;
+  int best = 1;
+  double best_t = 1e30;
+  for (int n = 1; n <= (steps / 4 > 1 ? steps / 4 : 1); ++n) {
+    const int len = (steps + n - 1) / n;
+    const int64_t wc = (int64_t(2) * bh * (n - 1) + slots - 1) / slots;
+    const int64_t wr = (int64_t(bh) * n + slots - 1) / slots;
+    const double t = double(wc) * len * t_compose + double(n - 1) * t_combine +
+                     double(wr) * len * t_replay;
+    if (t < best_t) {
+      best_t = t;
+      best = n;
+    }
+  }
+  return best;
 }
 
 struct SegLayout {
