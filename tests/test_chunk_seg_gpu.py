@@ -146,3 +146,43 @@ def test_no_wait_timeouts_at_occupancy():
             ref = (o.clone(), s.clone())
         else:
             assert torch.equal(o, ref[0]) and torch.equal(s, ref[1])
+
+
+def test_query_layouts_and_fp16_agree():
+    """The upper-level read kernel takes q through a tensor map in either
+    (head, level) order -- [B, T, H, L, K] or the layer's transposed
+    [B, T, L, H, K] view -- or, for a q whose rows do not collapse (a view
+    cut from a longer sequence), with plain loads. Same values, same bits
+    out. fp16 inputs (converted to bf16 tiles in the read kernel) meet the
+    oracle at the same bar."""
+    inp = config_inputs(1, 1024, 2, 128, 128, 4, 128, (1, 2, 4, 8), dtype=torch.bfloat16, seed=40,
+                        gate_proj_std=128 ** -0.5)
+    inp.pop("L")
+    d = _dev(inp)
+    q = d["q"]
+    longer = torch.zeros(1, 1100, *q.shape[2:], dtype=q.dtype, device="cuda")
+    longer[:, :1024] = q
+    outs = []
+    for qq in (q, q.transpose(2, 3).contiguous().transpose(2, 3), longer[:, :1024]):
+        call = FwdCall(**dict(d, q=qq), L=4, path="tc_seg")
+        outs.append([t.clone() for t in call.launch()])
+        call.check()
+    for o, s in outs[1:]:
+        assert torch.equal(o, outs[0][0]) and torch.equal(s, outs[0][1])
+    half = config_inputs(1, 1024, 2, 128, 128, 4, 128, (1, 2, 4, 8), dtype=torch.float16, seed=40,
+                         gate_proj_std=128 ** -0.5)
+    half.pop("L")
+    _check(half, 4, label="fp16 L4")
+
+
+def test_broadcast_gates_match_dense():
+    """Stride-0 broadcast gates (b, w, g views of per-token scalars) give the
+    same bits as the materialised tensors."""
+    kw = dict(dtype=torch.bfloat16, seed=41)
+    dense = config_inputs(1, 2048, 2, 128, 128, 3, 64, (1, 4, 16), **kw)
+    bcast = config_inputs(1, 2048, 2, 128, 128, 3, 64, (1, 4, 16), dense_gates=False, **kw)
+    dense.pop("L")
+    bcast.pop("L")
+    o1, s1 = _run(dense, 3)
+    o2, s2 = _run(bcast, 3)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
