@@ -22,9 +22,10 @@
 //   compose  -- per segment of consecutive steps, in parallel: the
 //               segment's transition S_end = M S_start + Z (M from the
 //               identity with Y = 0, Z from zero; one CTA each);
-//   combine  -- per (batch, head), sequentially over segments: the state
-//               entering each segment, M in two bf16 halves (hi + lo) times
-//               the state in two halves, so the chain keeps ~16 bits;
+//   combine  -- per (batch, head) and quarter of the value columns,
+//               sequentially over segments: the state entering each
+//               segment, M in two bf16 halves (hi + lo) times the state in
+//               two halves, so the chain keeps ~16 bits;
 //   replay   -- per segment, in parallel: the recurrence from the true start
 //               state, emitting the states that later stages read (bf16, in
 //               the MMA operand layout) and the final state (fp32).
@@ -123,7 +124,7 @@ inline int level_nseg(const FwdParams& p, int l) {
   const int bh = p.B * p.H > 0 ? p.B * p.H : 1;
   const bool r64 = level_rows(p, l) == 64;
   const int slots = kSMs * (r64 ? 2 : 1);
-  const double t_compose = r64 ? 2.9 : 4.4, t_replay = r64 ? 5.3 : 3.4, t_combine = 2.6;
+  const double t_compose = r64 ? 2.9 : 4.4, t_replay = r64 ? 5.3 : 3.4, t_combine = 1.4;
   int best = 1;
   double best_t = 1e30;
   for (int n = 1; n <= (steps / 4 > 1 ? steps / 4 : 1); ++n) {
@@ -479,136 +480,168 @@ seg_scan_kernel(SegScanArgs a, int replay) {
 }
 
 // ---------------------------------------------------------------------------
-// seg_combine: grid (H, B), 256 threads. The state entering each segment of
-// one level: S_{s+1} = M_s S_s + Z_s with M_s and S_s each split into two
-// bf16 halves (three MMAs: hi.hi + hi.lo + lo.hi) accumulating onto Z_s in
-// TMEM. M_{s+1} streams into the second of two shared-memory buffers and
-// Z_{s+1} into the second of two TMEM accumulators while step s's MMAs run,
-// so a step's critical path is its MMAs and the read-out of S_{s+1}.
+// seg_combine: grid (kCombineSplit, H, B), 128 threads. The state entering
+// each segment of one level: S_{s+1} = M_s S_s + Z_s. The value columns of
+// S evolve independently under the same M_s, so each CTA owns
+// kCombineCols of them. M_s and the slice of S_s are each split into two
+// bf16 halves, and three products keep ~16 bits: M_hi . [S_hi | S_lo] as
+// one N = 64 product (M_hi read from shared memory once) and M_lo . S_hi
+// (N = 32), fp32 in TMEM; the epilogue sums the three with Z_s. The MMAs'
+// operand reads from shared memory bound a step, so there are as few as
+// that allows (16). M_s streams into shared memory kCombineBufs - 1 steps
+// ahead of use; each thread loads its row of the slice of Z_{s+1} into
+// registers during step s. Thread 32q + i owns row k = 32q + i.
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(kSegThreads, 1)
+constexpr int kCombineSplit = 4;
+constexpr int kCombineCols = TV / kCombineSplit;   // 32
+constexpr int kCombineThreads = 128;
+constexpr int kCombineBufs = 3;
+constexpr int kCombineSliceBytes = TK * kCombineCols * 2;
+constexpr int kCombineSmem = kCombineBufs * 2 * kStateBytes + 2 * kCombineSliceBytes;
+
+__global__ void __launch_bounds__(kCombineThreads, 1)
 seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int level, int H,
                    int nseg, int32_t* status) {
   if (seg_gate_closed(status)) return;
   extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ uint64_t bar_ld[2], bar_mma;
+  __shared__ uint64_t bar_ld[kCombineBufs], bar_mma;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, c0 = 64 * (warp >> 2);
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, quarter = tid >> 5;
+  const int v0 = blockIdx.x * kCombineCols, h = blockIdx.y, b = blockIdx.z;
   const int64_t bh = int64_t(b) * H + h;
-  const int k = 32 * quarter + lane;
-  // Two M buffers (hi, lo), then the state's hi / lo B operands.
-  bf16* Shi = reinterpret_cast<bf16*>(sm + 4 * kStateBytes);
-  bf16* Slo = Shi + TK * TV;
+  const int k = tid;
+  // M buffers (hi, lo each), then the slice's hi and lo halves as one N = 64
+  // MN-major B operand (hi in its rows 0..31, lo in 32..63).
+  bf16* Shi = reinterpret_cast<bf16*>(sm + kCombineBufs * 2 * kStateBytes);
+  bf16* Slo = Shi + TK * kCombineCols;
   const char* mz0 = mz + bh * (nseg - 1) * int64_t(kMzBytes);
   const int nsteps = nseg - 1;
 
-  if (warp == 0) tmem_alloc(&tbase, 256);
+  if (quarter == 0) tmem_alloc(&tbase, 128);
+  int issued = 0;  // (thread 0) M loads issued
   auto load_m = [&](int s) {
-    uint64_t* bar = &bar_ld[s & 1];
+    ++issued;
+    uint64_t* bar = &bar_ld[s % kCombineBufs];
     mbar_arrive_expect_tx(bar, 2 * kStateBytes);
-    bulk_g2s(sm + (s & 1) * 2 * kStateBytes, mz0 + s * int64_t(kMzBytes), 2 * kStateBytes, bar);
+    bulk_g2s(sm + (s % kCombineBufs) * 2 * kStateBytes, mz0 + s * int64_t(kMzBytes),
+             2 * kStateBytes, bar);
   };
   if (tid == 0) {
-    mbar_init(&bar_ld[0], 1);
-    mbar_init(&bar_ld[1], 1);
+    for (int i = 0; i < kCombineBufs; ++i) mbar_init(&bar_ld[i], 1);
     mbar_init(&bar_mma, 1);
     fence_mbar_init();
     abort_flag = 0;
-    load_m(0);
+    for (int s = 0; s < kCombineBufs - 1 && s < nsteps; ++s) load_m(s);
   }
-  auto put_state = [&](const float* x, int cc) {
+  auto put_state = [&](const float* x) {
 #pragma unroll
-    for (int c = 0; c < 32; c += 8) {
+    for (int c = 0; c < kCombineCols; c += 8) {
       float hi[8], lo[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         hi[t] = __bfloat162float(__float2bfloat16_rn(x[c + t]));
         lo[t] = x[c + t] - hi[t];
       }
-      *reinterpret_cast<uint4*>(Shi + mnmajor_off(k, cc + c, TK)) = pack8(hi);
-      *reinterpret_cast<uint4*>(Slo + mnmajor_off(k, cc + c, TK)) = pack8(lo);
+      *reinterpret_cast<uint4*>(Shi + mnmajor_off(k, c, TK)) = pack8(hi);
+      *reinterpret_cast<uint4*>(Slo + mnmajor_off(k, c, TK)) = pack8(lo);
     }
   };
-  fence_before_sync();
-  __syncthreads();
-  fence_after_sync();
-  const uint32_t tb = tbase;
-  // Z_s of a step into accumulator s & 1.
-  auto put_z = [&](int s) {
+  // Row k of the slice of Z_s.
+  auto fetch_z = [&](int s, float4* z4) {
     const float* z = reinterpret_cast<const float*>(mz0 + s * int64_t(kMzBytes) + 2 * kStateBytes);
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int cc = c0 + 32 * hh;
-      float x[32];
-#pragma unroll
-      for (int t = 0; t < 32; t += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(z + lm_off(k, cc + t));
-        x[t] = v.x; x[t + 1] = v.y; x[t + 2] = v.z; x[t + 3] = v.w;
-      }
-      tmem_st32(taddr(tb + 128 * (s & 1), 32 * quarter, cc), x);
-    }
+    for (int t = 0; t < kCombineCols / 4; ++t)
+      z4[t] = *reinterpret_cast<const float4*>(z + lm_off(k, v0 + 4 * t));
   };
+  float4 zc[kCombineCols / 4], zn[kCombineCols / 4];
   // S_0: the level's initial state (or zero).
+  {
+    float x[kCombineCols];
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int cc = c0 + 32 * hh;
-    float x[32];
-#pragma unroll
-    for (int t = 0; t < 32; ++t) x[t] = init ? init[((bh * L + level) * TK + k) * TV + cc + t] : 0.f;
-    put_state(x, cc);
+    for (int t = 0; t < kCombineCols; ++t)
+      x[t] = init ? init[((bh * L + level) * TK + k) * TV + v0 + t] : 0.f;
+    put_state(x);
   }
-  if (nsteps > 0) put_z(0);
-  tmem_wait_st();
+  if (nsteps > 0) fetch_z(0, zc);
   fence_proxy_async();
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  const uint32_t id = idesc_f16(128, 128, true, false, true);
+  const uint32_t tb = tbase;
+  // TMEM: [hi.hi | hi.lo] in columns 0..63, lo.hi in 64..95.
+  const uint32_t id64 = idesc_f16(128, 2 * kCombineCols, true, false, true);
+  const uint32_t id32 = idesc_f16(128, kCombineCols, true, false, true);
+  // Descriptors of K step 0; K step kk adds 256 bytes (16 in the address field).
+  const uint64_t d_s = desc_tile(smem_u32(Shi), TK, 0);
+  const uint64_t d_m0 = desc_tile(smem_u32(sm), TK, 0);
   uint32_t ph_mma = 0;
+  int landed = 0;  // (thread 0) M loads waited for
   for (int s = 0; s < nsteps; ++s) {
-    const uint32_t tD = tb + 128 * (s & 1);
     if (tid == 0) {
-      // (Buffer (s + 1) & 1 was last read by step s - 1's MMAs, complete.)
-      if (s + 1 < nsteps) load_m(s + 1);
-      if (!mbar_wait(&bar_ld[s & 1], (s >> 1) & 1)) abort_flag = 1;
-      fence_after_sync();
-      const uint8_t* mb = sm + (s & 1) * 2 * kStateBytes;
-      mma_tile(tD, smem_u32(mb), smem_u32(Shi), TK, id, true);
-      mma_tile(tD, smem_u32(mb), smem_u32(Slo), TK, id, true);
-      mma_tile(tD, smem_u32(mb + kStateBytes), smem_u32(Shi), TK, id, true);
+      // (Buffer (s - 1) mod kCombineBufs was last read by step s - 1's
+      // MMAs, complete.)
+      if (s + kCombineBufs - 1 < nsteps) load_m(s + kCombineBufs - 1);
+      if (mbar_wait(&bar_ld[s % kCombineBufs], (s / kCombineBufs) & 1)) {
+        ++landed;
+        fence_after_sync();
+        const uint64_t d_hi = d_m0 + uint64_t((s % kCombineBufs) * 2 * kStateBytes) / 16;
+        const uint64_t d_lo = d_hi + kStateBytes / 16;
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          mma_f16(tb, d_hi + 16 * kk, d_s + 16 * kk, id64, kk > 0 ? 1u : 0u);
+          mma_f16(tb + 2 * kCombineCols, d_lo + 16 * kk, d_s + 16 * kk, id32, kk > 0 ? 1u : 0u);
+        }
+      } else {
+        abort_flag = 1;
+      }
+      // (With no MMA issued the commit arrives at once.)
       mma_commit(&bar_mma);
     }
     __syncwarp();
-    if (s + 1 < nsteps) put_z(s + 1);
+    if (s + 1 < nsteps) fetch_z(s + 1, zn);
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
+    float x[kCombineCols];
+    {
+      uint32_t r0[kCombineCols], r1[kCombineCols], r2[kCombineCols];
+      tmem_ld32_nowait(taddr(tb, 32 * quarter, 0), r0);
+      tmem_ld32_nowait(taddr(tb + kCombineCols, 32 * quarter, 0), r1);
+      tmem_ld32_nowait(taddr(tb + 2 * kCombineCols, 32 * quarter, 0), r2);
+      tmem_wait_ld();
+#pragma unroll
+      for (int t = 0; t < kCombineCols / 4; ++t) {
+        const float z[4] = {zc[t].x, zc[t].y, zc[t].z, zc[t].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          x[4 * t + e] = (__uint_as_float(r0[4 * t + e]) + z[e]) +
+                         (__uint_as_float(r1[4 * t + e]) + __uint_as_float(r2[4 * t + e]));
+      }
+    }
+    put_state(x);  // (the next step's operand first: it is on the chain)
     float* dst = starts + (bh * nseg + s + 1) * TK * TV;
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int cc = c0 + 32 * hh;
-      float x[32];
-      tmem_ld32(taddr(tD, 32 * quarter, cc), x);
+    for (int t = 0; t < kCombineCols; t += 4)
+      *reinterpret_cast<float4*>(dst + lm_off(k, v0 + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
 #pragma unroll
-      for (int t = 0; t < 32; t += 4)
-        *reinterpret_cast<float4*>(dst + lm_off(k, cc + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
-      put_state(x, cc);
-    }
-    tmem_wait_st();
+    for (int t = 0; t < kCombineCols / 4; ++t) zc[t] = zn[t];
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     if (abort_flag) break;
   }
-  if (abort_flag && tid == 0 && status) atomicOr(status, NGDN2_STATUS_WAIT_TIMEOUT);
+  if (abort_flag && tid == 0) {
+    // Copies still in flight land before the CTA's shared memory is released.
+    for (int c = landed; c < issued; ++c)
+      if (!mbar_wait(&bar_ld[c % kCombineBufs], (c / kCombineBufs) & 1)) break;
+    if (status) atomicOr(status, NGDN2_STATUS_WAIT_TIMEOUT);
+  }
   fence_before_sync();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 256);
+  if (quarter == 0) tmem_dealloc(tbase, 128);
 }
 
 // ---------------------------------------------------------------------------
@@ -923,18 +956,21 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
 }
 
 // ---------------------------------------------------------------------------
-// seg_read: grid (ceil(NT / unit), H, B), 256 threads. Adds the upper
-// levels' reads sum_{l >= 1} mix_l scale (q_l . S_l) to the level-0 output
-// that level 0's replay left in o (chunk.py:129-156, naive.py:382-390). A CTA
-// takes a unit of up to four chunks; the unit size divides every upper
-// level's firing interval, so its chunks read the same state of each level
-// (the one entering their group). Level by level, the state and the unit's
-// query tiles (TMA, 128-byte swizzle) arrive in one of two shared-memory
-// stages, the next level's load overlapping this level's work; the query
-// rows are scaled by mix_l scale in place; then one M = 128 MMA per chunk
-// (the tile in the tile's lower half, as in the fused scan's reads)
-// accumulates into that chunk's TMEM accumulator, so the levels sum on the
-// tensor cores and the epilogue adds one accumulator per chunk to o.
+// seg_read: persistent, one CTA per SM, 8 consumer warps + 1 producer warp.
+// Adds the upper levels' reads sum_{l >= 1} mix_l scale (q_l . S_l) to the
+// level-0 output that level 0's replay left in o (chunk.py:129-156,
+// naive.py:382-390). A job is a unit of up to four chunks of one (batch,
+// head); the unit size divides every upper level's firing interval, so its
+// chunks read the same state of each level (the one entering their group).
+// A CTA walks its jobs (blockIdx.x, + gridDim.x, ...) level by level: the
+// producer streams each (job, level) item's state and query tiles (TMA,
+// 128-byte swizzle) into one of two shared-memory stages as soon as the MMAs
+// of the stage's previous item have read it, across job boundaries; the
+// consumers scale the query rows by mix_l scale in place, one thread issues
+// one M = 128 MMA per chunk (the tile in the tile's lower half, as in the
+// fused scan's reads) accumulating into that chunk's TMEM accumulator, so
+// the levels sum on the tensor cores, and the epilogue adds one accumulator
+// per chunk to o while the next job's first items load.
 // ---------------------------------------------------------------------------
 
 constexpr int kReadUnit = 4;
@@ -954,127 +990,170 @@ struct ReadArgs {
   int32_t* status;
 };
 
-__global__ void __launch_bounds__(kReadThreads, 1)
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kReadThreads) : "memory");
+}
+
+__global__ void __launch_bounds__(kReadThreads + 32, 1)
 seg_read_kernel(ReadArgs a, const __grid_constant__ CUtensorMap qmap) {
   if (seg_gate_closed(a.status)) return;
   extern __shared__ __align__(1024) uint8_t sm_raw[];
-  __shared__ uint64_t bar_ld[2], bar_mma[NGDN2_MAX_LEVELS];
+  __shared__ uint64_t bar_full[2], bar_free[2], bar_done, bar_fin;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, c0 = 64 * (warp >> 2);
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int n0 = blockIdx.x * a.unit;
-  const int nc = min(a.unit, a.NT - n0);
-  const int64_t bh = int64_t(b) * a.H + h;
+  const int quarter = warp & 3, c0 = 64 * ((warp >> 2) & 1);
   uint8_t* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
   const bool q_tma = a.hl_mode != 2;
   const int nlev = a.L - 1;
+  const int units = (a.NT + a.unit - 1) / a.unit;
+  const int64_t njobs = int64_t(a.B) * a.H * units;
+  // This CTA's jobs: blockIdx.x, + gridDim.x, ...; items = (job, level).
+  const int64_t my_jobs =
+      njobs > blockIdx.x ? (njobs - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t nitems = my_jobs * nlev;
 
   if (warp == 0) tmem_alloc(&tbase, 512);
-  // Level l's state (the one entering the unit's group) and query tiles
-  // into stage st.
-  auto issue = [&](int l, int st) {
-    uint8_t* base = sm + st * kReadStage;
-    uint64_t* bar = &bar_ld[st];
-    mbar_arrive_expect_tx(bar, uint32_t(kStateBytes + (q_tma ? nc * TILE_QK : 0)));
-    bulk_g2s(base, a.E[l] + (bh * a.nE[l] + n0 / a.firing[l]) * (TK * TV), kStateBytes, bar);
-    if (q_tma)
-      for (int c = 0; c < nc; ++c)
-        tma_load_4d(base + kStateBytes + c * TILE_QK, &qmap, 0, b * a.T + (n0 + c) * kC, 0,
-                    a.hl_mode ? l * a.H + h : h * a.L + l, bar);
-  };
   if (tid == 0) {
-    mbar_init(&bar_ld[0], 1);
-    mbar_init(&bar_ld[1], 1);
-    for (int l = 0; l < NGDN2_MAX_LEVELS; ++l) mbar_init(&bar_mma[l], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_free[i], 1);
+    }
+    mbar_init(&bar_done, 1);
+    mbar_init(&bar_fin, 1);
     fence_mbar_init();
     abort_flag = 0;
-    issue(1, 0);
-    if (nlev > 1) issue(2, 1);
   }
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tb = tbase;
-  const uint32_t id = idesc_f16(128, 128, true, false, true);
-  uint32_t ph_ld[2] = {0u, 0u};
-  for (int li = 0; li < nlev; ++li) {
-    const int l = li + 1, st = li & 1;
-    uint8_t* base = sm + st * kReadStage;
-    if (!mbar_wait(&bar_ld[st], ph_ld[st])) abort_flag = 1;
-    ph_ld[st] ^= 1;
-    // Row r of chunk c scaled by mix_l scale (zero past T), as bf16 (fp16 q
-    // converted; q without a tensor map read here with plain loads).
-    {
-      const int r = tid & 63, c = tid >> 6;
-      if (c < nc) {
-        const int t = (n0 + c) * kC + r;
-        const float m =
-            t < a.T ? load_elem(a.mix.p, a.mix.off(b, t, h, l), a.mix.dt) * a.scale : 0.f;
-        uint8_t* tile = base + kStateBytes + c * TILE_QK;
-#pragma unroll 4
-        for (int u = 0; u < 16; ++u) {
-          uint4* q8 = reinterpret_cast<uint4*>(tile + sw128_off(r, 8 * u));
-          const uint4 raw =
-              q_tma ? *q8
-                    : t < a.T ? raw8_at(a.q.p, a.q.dt, a.q.off(b, t, h, l, 8 * u), a.q.sd)
-                              : make_uint4(0u, 0u, 0u, 0u);
-          float f[8];
-          unpack8(raw, a.q.dt, f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] *= m;
-          *q8 = pack8(f);
+
+  if (warp == kReadThreads / 32) {
+    // Producer warp: item it's state and query tiles into stage it & 1, once
+    // the MMAs of item it - 2 (the stage's previous use) have read it.
+    if (lane == 0) {
+      int64_t it = 0;
+      for (; it < nitems; ++it) {
+        const int st = int(it & 1);
+        if (it >= 2 && !mbar_wait(&bar_free[st], uint32_t(((it - 2) >> 1) & 1))) {
+          abort_flag = 1;
+          break;
         }
+        if (*reinterpret_cast<volatile int*>(&abort_flag)) break;
+        const int64_t job = blockIdx.x + (it / nlev) * gridDim.x;
+        const int l = int(it % nlev) + 1;
+        const int64_t bh = job / units;
+        const int b = int(bh / a.H), h = int(bh % a.H);
+        const int n0 = int(job % units) * a.unit;
+        const int nc = min(a.unit, a.NT - n0);
+        uint8_t* base = sm + st * kReadStage;
+        uint64_t* bar = &bar_full[st];
+        mbar_arrive_expect_tx(bar, uint32_t(kStateBytes + (q_tma ? nc * TILE_QK : 0)));
+        bulk_g2s(base, a.E[l] + (bh * a.nE[l] + n0 / a.firing[l]) * (TK * TV), kStateBytes, bar);
+        if (q_tma)
+          for (int c = 0; c < nc; ++c)
+            tma_load_4d(base + kStateBytes + c * TILE_QK, &qmap, 0, b * a.T + (n0 + c) * kC, 0,
+                        a.hl_mode ? l * a.H + h : h * a.L + l, bar);
       }
+      // Copies still in flight land before the CTA's shared memory is
+      // released (each stage has at most one outstanding).
+      for (int64_t j = it - 2 > 0 ? it - 2 : 0; j < it; ++j)
+        if (!mbar_wait(&bar_full[j & 1], uint32_t((j >> 1) & 1))) break;
     }
-    fence_proxy_async();
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    if (tid == 0) {
-      for (int c = 0; c < nc; ++c)
-        mma_tile_sw128_lo(tb + 128 * c, smem_u32(base + kStateBytes + c * TILE_QK),
-                          smem_u32(base), id, li > 0);
-      mma_commit(&bar_mma[li]);
-      // Once these MMAs have read the stage, the level after next streams in.
-      if (li + 2 < nlev) {
-        if (!mbar_wait(&bar_mma[li], 0)) abort_flag = 1;
-        issue(l + 2, st);
+  } else {
+    const uint32_t id = idesc_f16(128, 128, true, false, true);
+    for (int64_t jj = 0; jj < my_jobs; ++jj) {
+      const int64_t job = blockIdx.x + jj * gridDim.x;
+      const int64_t bh = job / units;
+      const int b = int(bh / a.H), h = int(bh % a.H);
+      const int n0 = int(job % units) * a.unit;
+      const int nc = min(a.unit, a.NT - n0);
+      for (int li = 0; li < nlev; ++li) {
+        const int64_t it = jj * nlev + li;
+        const int l = li + 1, st = int(it & 1);
+        uint8_t* base = sm + st * kReadStage;
+        if (!mbar_wait(&bar_full[st], uint32_t((it >> 1) & 1))) abort_flag = 1;
+        // Row r of chunk c scaled by mix_l scale (zero past T), as bf16 (fp16
+        // q converted; q without a tensor map read here with plain loads).
+        {
+          const int r = tid & 63, c = tid >> 6;
+          if (c < nc) {
+            const int t = (n0 + c) * kC + r;
+            const float m =
+                t < a.T ? load_elem(a.mix.p, a.mix.off(b, t, h, l), a.mix.dt) * a.scale : 0.f;
+            uint8_t* tile = base + kStateBytes + c * TILE_QK;
+#pragma unroll 4
+            for (int u = 0; u < 16; ++u) {
+              uint4* q8 = reinterpret_cast<uint4*>(tile + sw128_off(r, 8 * u));
+              const uint4 raw =
+                  q_tma ? *q8
+                        : t < a.T ? raw8_at(a.q.p, a.q.dt, a.q.off(b, t, h, l, 8 * u), a.q.sd)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+              float f[8];
+              unpack8(raw, a.q.dt, f);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] *= m;
+              *q8 = pack8(f);
+            }
+          }
+        }
+        fence_proxy_async();
+        fence_before_sync();
+        consumers_sync();
+        fence_after_sync();
+        if (tid == 0) {
+          for (int c = 0; c < nc; ++c)
+            mma_tile_sw128_lo(tb + 128 * c, smem_u32(base + kStateBytes + c * TILE_QK),
+                              smem_u32(base), id, li > 0);
+          mma_commit(&bar_free[st]);
+          if (li == nlev - 1) mma_commit(&bar_done);
+        }
+        __syncwarp();
       }
-    }
-    __syncwarp();
-  }
-  // MMAs complete in issue order: the last level's barrier covers them all.
-  if (nlev > 0 && !mbar_wait(&bar_mma[nlev - 1], 0)) abort_flag = 1;
-  fence_after_sync();
-  if (quarter >= 2) {
-    const int i = 32 * (quarter - 2) + lane;
-    for (int c = 0; c < nc; ++c) {
-      const int t = (n0 + c) * kC + i;
+      // The job's MMAs complete; its accumulators go to o.
+      if (!mbar_wait(&bar_done, uint32_t(jj & 1))) abort_flag = 1;
+      fence_after_sync();
+      if (quarter >= 2) {
+        const int i = 32 * (quarter - 2) + lane;
+        for (int c = 0; c < nc; ++c) {
+          const int t = (n0 + c) * kC + i;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float y[32];
-        tmem_ld32(taddr(tb + 128 * c, 32 * quarter, c0 + 32 * hh), y);
-        if (t < a.T) {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) +
-                                                ((int64_t(b) * a.T + t) * a.H + h) * TV + c0 + 32 * hh);
+          for (int hh = 0; hh < 2; ++hh) {
+            float y[32];
+            tmem_ld32(taddr(tb + 128 * c, 32 * quarter, c0 + 32 * hh), y);
+            if (t < a.T) {
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) +
+                                                    ((int64_t(b) * a.T + t) * a.H + h) * TV +
+                                                    c0 + 32 * hh);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float f[8];
-            unpack8(dst[u], a.dtype, f);
+              for (int u = 0; u < 4; ++u) {
+                float f[8];
+                unpack8(dst[u], a.dtype, f);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] += y[8 * u + e];
-            dst[u] = a.dtype == NGDN2_BF16 ? pack8(f) : pack8h(f);
+                for (int e = 0; e < 8; ++e) f[e] += y[8 * u + e];
+                dst[u] = a.dtype == NGDN2_BF16 ? pack8(f) : pack8h(f);
+              }
+            }
           }
         }
       }
+      // The next job's MMAs overwrite the accumulators read above.
+      fence_before_sync();
+      consumers_sync();
+      fence_after_sync();
+      if (*reinterpret_cast<volatile int*>(&abort_flag)) break;
+    }
+    if (tid == 0) {
+      // Every MMA issued has completed before TMEM is released.
+      mma_commit(&bar_fin);
+      if (!mbar_wait(&bar_fin, 0)) abort_flag = 1;
     }
   }
-  if (abort_flag && tid == 0 && a.status) atomicOr(a.status, NGDN2_STATUS_WAIT_TIMEOUT);
   fence_before_sync();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tb, 512);
+  if (abort_flag && tid == 0 && a.status) atomicOr(a.status, NGDN2_STATUS_WAIT_TIMEOUT);
+  if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
 }  // namespace
@@ -1157,10 +1236,10 @@ static cudaError_t scan_level(const FwdParams& p, const SegLayout& lay, char* ws
     err = rows == 64 ? launch_scan<64>(c, true, 2 * (a.nseg - 1), p.B, stream)
                      : launch_scan<128>(c, true, 2 * (a.nseg - 1), p.B, stream);
     if (err != cudaSuccess) return err;
-    const int smem = 6 * kStateBytes;
-    err = cudaFuncSetAttribute(seg_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    err = cudaFuncSetAttribute(seg_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kCombineSmem);
     if (err != cudaSuccess) return err;
-    seg_combine_kernel<<<dim3(p.H, p.B), kSegThreads, smem, stream>>>(
+    seg_combine_kernel<<<dim3(kCombineSplit, p.H, p.B), kCombineThreads, kCombineSmem, stream>>>(
         a.mz, p.init, reinterpret_cast<float*>(ws + lay.start_off[l]), p.L, l, p.H, a.nseg,
         p.status);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
@@ -1230,8 +1309,10 @@ static cudaError_t read_levels(const FwdParams& p, const SegLayout& lay, char* w
   cudaError_t err =
       cudaFuncSetAttribute(seg_read_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
-  seg_read_kernel<<<dim3((p.NT + a.unit - 1) / a.unit, p.H, p.B), kReadThreads, smem, stream>>>(
-      a, qmap);
+  // Persistent: one CTA per SM (or per job, when fewer) walks its jobs.
+  const int64_t njobs = int64_t(p.B) * p.H * ((p.NT + a.unit - 1) / a.unit);
+  const int grid = int(njobs < kSMs ? njobs : kSMs);
+  seg_read_kernel<<<grid, kReadThreads + 32, smem, stream>>>(a, qmap);
   return cudaGetLastError();
 }
 
