@@ -1111,28 +1111,47 @@ seg_read_kernel(ReadArgs a, const __grid_constant__ CUtensorMap qmap) {
         }
         __syncwarp();
       }
-      // The job's MMAs complete; its accumulators go to o.
+      // The job's MMAs complete; its accumulators go to o. Row i's 64
+      // columns of o for chunk c + 1 are loaded while chunk c is formed (the
+      // first chunk's before the wait), so the loads' latency overlaps.
+      const int i = 32 * (quarter - 2) + lane;
+      auto o_row = [&](int c) {
+        const int t = (n0 + c) * kC + i;
+        return t < a.T ? reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) +
+                                                  ((int64_t(b) * a.T + t) * a.H + h) * TV + c0)
+                       : nullptr;
+      };
+      uint4 ob[2][8];
+      if (quarter >= 2) {
+        const uint4* src = o_row(0);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ob[0][u] = src ? src[u] : make_uint4(0u, 0u, 0u, 0u);
+      }
       if (!mbar_wait(&bar_done, uint32_t(jj & 1))) abort_flag = 1;
       fence_after_sync();
       if (quarter >= 2) {
-        const int i = 32 * (quarter - 2) + lane;
-        for (int c = 0; c < nc; ++c) {
-          const int t = (n0 + c) * kC + i;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            float y[32];
-            tmem_ld32(taddr(tb + 128 * c, 32 * quarter, c0 + 32 * hh), y);
-            if (t < a.T) {
-              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) +
-                                                    ((int64_t(b) * a.T + t) * a.H + h) * TV +
-                                                    c0 + 32 * hh);
+        for (int c = 0; c < kReadUnit; ++c) {
+          if (c < nc) {
+            if (c + 1 < nc) {
+              const uint4* src = o_row(c + 1);
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                float f[8];
-                unpack8(dst[u], a.dtype, f);
+              for (int u = 0; u < 8; ++u) ob[(c + 1) & 1][u] = src ? src[u] : make_uint4(0u, 0u, 0u, 0u);
+            }
+            uint4* dst = o_row(c);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] += y[8 * u + e];
-                dst[u] = a.dtype == NGDN2_BF16 ? pack8(f) : pack8h(f);
+            for (int hh = 0; hh < 2; ++hh) {
+              float y[32];
+              tmem_ld32(taddr(tb + 128 * c, 32 * quarter, c0 + 32 * hh), y);
+              if (dst) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  float f[8];
+                  unpack8(ob[c & 1][4 * hh + u], a.dtype, f);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) f[e] += y[8 * u + e];
+                  dst[4 * hh + u] = a.dtype == NGDN2_BF16 ? pack8(f) : pack8h(f);
+                }
               }
             }
           }
