@@ -124,7 +124,7 @@ inline int level_nseg(const FwdParams& p, int l) {
   const int bh = p.B * p.H > 0 ? p.B * p.H : 1;
   const bool r64 = level_rows(p, l) == 64;
   const int slots = kSMs * (r64 ? 2 : 1);
-  const double t_compose = r64 ? 2.9 : 4.4, t_replay = r64 ? 5.3 : 3.4, t_combine = 1.4;
+  const double t_compose = r64 ? 2.9 : 4.4, t_replay = r64 ? 5.3 : 3.4, t_combine = 1.3;
   int best = 1;
   double best_t = 1e30;
   for (int n = 1; n <= (steps / 4 > 1 ? steps / 4 : 1); ++n) {
@@ -480,22 +480,27 @@ seg_scan_kernel(SegScanArgs a, int replay) {
 }
 
 // ---------------------------------------------------------------------------
-// seg_combine: grid (kCombineSplit, H, B), 128 threads. The state entering
+// seg_combine: grid (kCombineSplit, H, B), 256 threads. The state entering
 // each segment of one level: S_{s+1} = M_s S_s + Z_s. The value columns of
 // S evolve independently under the same M_s, so each CTA owns
 // kCombineCols of them. M_s and the slice of S_s are each split into two
 // bf16 halves, and three products keep ~16 bits: M_hi . [S_hi | S_lo] as
-// one N = 64 product (M_hi read from shared memory once) and M_lo . S_hi
-// (N = 32), fp32 in TMEM; the epilogue sums the three with Z_s. The MMAs'
-// operand reads from shared memory bound a step, so there are as few as
-// that allows (16). M_s streams into shared memory kCombineBufs - 1 steps
-// ahead of use; each thread loads its row of the slice of Z_{s+1} into
-// registers during step s. Thread 32q + i owns row k = 32q + i.
+// one N = 32 product (M_hi read from shared memory once) and M_lo . S_hi
+// (N = 16), fp32 in TMEM; the epilogue sums the three with Z_s. Each MMA
+// instruction takes about 50 cycles whatever its N or operand source, so a
+// step issues as few as the split allows (16), and the columns are split
+// eight ways to shorten the epilogue. M_s streams into shared memory
+// kCombineBufs - 1 steps ahead of use (the next copy is issued after the
+// step's MMAs). Warp w owns row k = 32 (w & 3) + i (its TMEM lane quarter)
+// and 8 of the 16 columns (w >> 2). Off the chain, while a step's MMAs run,
+// each thread stores the previous step's state to the segment starts and
+// loads its part of Z_{s+1}.
 // ---------------------------------------------------------------------------
 
-constexpr int kCombineSplit = 4;
-constexpr int kCombineCols = TV / kCombineSplit;   // 32
-constexpr int kCombineThreads = 128;
+constexpr int kCombineSplit = 8;
+constexpr int kCombineCols = TV / kCombineSplit;   // 16
+constexpr int kCombineThreads = 256;
+constexpr int kCombineHalf = kCombineCols / 2;    // columns per thread
 constexpr int kCombineBufs = 3;
 constexpr int kCombineSliceBytes = TK * kCombineCols * 2;
 constexpr int kCombineSmem = kCombineBufs * 2 * kStateBytes + 2 * kCombineSliceBytes;
@@ -508,18 +513,19 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
   __shared__ uint64_t bar_ld[kCombineBufs], bar_mma;
   __shared__ uint32_t tbase;
   __shared__ int abort_flag;
-  const int tid = threadIdx.x, quarter = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, quarter = warp & 3;
+  const int cq = kCombineHalf * (warp >> 2);   // this thread's columns within the slice
   const int v0 = blockIdx.x * kCombineCols, h = blockIdx.y, b = blockIdx.z;
   const int64_t bh = int64_t(b) * H + h;
-  const int k = tid;
-  // M buffers (hi, lo each), then the slice's hi and lo halves as one N = 64
-  // MN-major B operand (hi in its rows 0..31, lo in 32..63).
+  const int k = 32 * quarter + (tid & 31);
+  // M buffers (hi, lo each), then the slice's hi and lo halves as one N = 32
+  // MN-major B operand (hi in its rows 0..15, lo in 16..31).
   bf16* Shi = reinterpret_cast<bf16*>(sm + kCombineBufs * 2 * kStateBytes);
   bf16* Slo = Shi + TK * kCombineCols;
   const char* mz0 = mz + bh * (nseg - 1) * int64_t(kMzBytes);
   const int nsteps = nseg - 1;
 
-  if (quarter == 0) tmem_alloc(&tbase, 128);
+  if (warp == 0) tmem_alloc(&tbase, 64);
   int issued = 0;  // (thread 0) M loads issued
   auto load_m = [&](int s) {
     ++issued;
@@ -536,43 +542,45 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
     for (int s = 0; s < kCombineBufs - 1 && s < nsteps; ++s) load_m(s);
   }
   auto put_state = [&](const float* x) {
+    float hi[kCombineHalf], lo[kCombineHalf];
 #pragma unroll
-    for (int c = 0; c < kCombineCols; c += 8) {
-      float hi[8], lo[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        hi[t] = __bfloat162float(__float2bfloat16_rn(x[c + t]));
-        lo[t] = x[c + t] - hi[t];
-      }
-      *reinterpret_cast<uint4*>(Shi + mnmajor_off(k, c, TK)) = pack8(hi);
-      *reinterpret_cast<uint4*>(Slo + mnmajor_off(k, c, TK)) = pack8(lo);
+    for (int t = 0; t < kCombineHalf; ++t) {
+      hi[t] = __bfloat162float(__float2bfloat16_rn(x[t]));
+      lo[t] = x[t] - hi[t];
     }
+    *reinterpret_cast<uint4*>(Shi + mnmajor_off(k, cq, TK)) = pack8(hi);
+    *reinterpret_cast<uint4*>(Slo + mnmajor_off(k, cq, TK)) = pack8(lo);
   };
-  // Row k of the slice of Z_s.
+  // This thread's part of row k of the slice of Z_s.
   auto fetch_z = [&](int s, float4* z4) {
     const float* z = reinterpret_cast<const float*>(mz0 + s * int64_t(kMzBytes) + 2 * kStateBytes);
 #pragma unroll
-    for (int t = 0; t < kCombineCols / 4; ++t)
-      z4[t] = *reinterpret_cast<const float4*>(z + lm_off(k, v0 + 4 * t));
+    for (int t = 0; t < kCombineHalf / 4; ++t)
+      z4[t] = *reinterpret_cast<const float4*>(z + lm_off(k, v0 + cq + 4 * t));
   };
-  float4 zc[kCombineCols / 4], zn[kCombineCols / 4];
-  // S_0: the level's initial state (or zero).
-  {
-    float x[kCombineCols];
+  auto store_start = [&](int s, const float* x) {
+    float* dst = starts + (bh * nseg + s) * TK * TV;
 #pragma unroll
-    for (int t = 0; t < kCombineCols; ++t)
-      x[t] = init ? init[((bh * L + level) * TK + k) * TV + v0 + t] : 0.f;
-    put_state(x);
-  }
+    for (int t = 0; t < kCombineHalf; t += 4)
+      *reinterpret_cast<float4*>(dst + lm_off(k, v0 + cq + t)) =
+          make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+  };
+  float4 zc[kCombineHalf / 4], zn[kCombineHalf / 4];
+  float x[kCombineHalf];
+  // S_0: the level's initial state (or zero).
+#pragma unroll
+  for (int t = 0; t < kCombineHalf; ++t)
+    x[t] = init ? init[((bh * L + level) * TK + k) * TV + v0 + cq + t] : 0.f;
+  put_state(x);
   if (nsteps > 0) fetch_z(0, zc);
   fence_proxy_async();
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tb = tbase;
-  // TMEM: [hi.hi | hi.lo] in columns 0..63, lo.hi in 64..95.
-  const uint32_t id64 = idesc_f16(128, 2 * kCombineCols, true, false, true);
-  const uint32_t id32 = idesc_f16(128, kCombineCols, true, false, true);
+  // TMEM: [hi.hi | hi.lo] in columns 0..31, lo.hi in 32..47.
+  const uint32_t id_hh = idesc_f16(128, 2 * kCombineCols, true, false, true);
+  const uint32_t id_lh = idesc_f16(128, kCombineCols, true, false, true);
   // Descriptors of K step 0; K step kk adds 256 bytes (16 in the address field).
   const uint64_t d_s = desc_tile(smem_u32(Shi), TK, 0);
   const uint64_t d_m0 = desc_tile(smem_u32(sm), TK, 0);
@@ -580,9 +588,6 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
   int landed = 0;  // (thread 0) M loads waited for
   for (int s = 0; s < nsteps; ++s) {
     if (tid == 0) {
-      // (Buffer (s - 1) mod kCombineBufs was last read by step s - 1's
-      // MMAs, complete.)
-      if (s + kCombineBufs - 1 < nsteps) load_m(s + kCombineBufs - 1);
       if (mbar_wait(&bar_ld[s % kCombineBufs], (s / kCombineBufs) & 1)) {
         ++landed;
         fence_after_sync();
@@ -590,29 +595,36 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
         const uint64_t d_lo = d_hi + kStateBytes / 16;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk) {
-          mma_f16(tb, d_hi + 16 * kk, d_s + 16 * kk, id64, kk > 0 ? 1u : 0u);
-          mma_f16(tb + 2 * kCombineCols, d_lo + 16 * kk, d_s + 16 * kk, id32, kk > 0 ? 1u : 0u);
+          mma_f16(tb, d_hi + 16 * kk, d_s + 16 * kk, id_hh, kk > 0 ? 1u : 0u);
+          mma_f16(tb + 2 * kCombineCols, d_lo + 16 * kk, d_s + 16 * kk, id_lh, kk > 0 ? 1u : 0u);
         }
       } else {
         abort_flag = 1;
       }
       // (With no MMA issued the commit arrives at once.)
       mma_commit(&bar_mma);
+      // (Buffer (s - 1) mod kCombineBufs was last read by step s - 1's
+      // MMAs, complete.)
+      if (s + kCombineBufs - 1 < nsteps) load_m(s + kCombineBufs - 1);
     }
     __syncwarp();
+    // Off the chain: S_s (s >= 1) to the segment starts, Z_{s+1} in.
+    if (s > 0) store_start(s, x);
     if (s + 1 < nsteps) fetch_z(s + 1, zn);
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
-    float x[kCombineCols];
     {
-      uint32_t r0[kCombineCols], r1[kCombineCols], r2[kCombineCols];
-      tmem_ld32_nowait(taddr(tb, 32 * quarter, 0), r0);
-      tmem_ld32_nowait(taddr(tb + kCombineCols, 32 * quarter, 0), r1);
-      tmem_ld32_nowait(taddr(tb + 2 * kCombineCols, 32 * quarter, 0), r2);
+      uint32_t r0[kCombineHalf], r1[kCombineHalf], r2[kCombineHalf];
+      tmem_ld8_nowait(taddr(tb, 32 * quarter, cq), r0);
+      tmem_ld8_nowait(taddr(tb + kCombineCols, 32 * quarter, cq), r1);
+      tmem_ld8_nowait(taddr(tb + 2 * kCombineCols, 32 * quarter, cq), r2);
       tmem_wait_ld();
+      tmem_regs_after_wait8(r0);
+      tmem_regs_after_wait8(r1);
+      tmem_regs_after_wait8(r2);
 #pragma unroll
-      for (int t = 0; t < kCombineCols / 4; ++t) {
+      for (int t = 0; t < kCombineHalf / 4; ++t) {
         const float z[4] = {zc[t].x, zc[t].y, zc[t].z, zc[t].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e)
@@ -620,19 +632,16 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
                          (__uint_as_float(r1[4 * t + e]) + __uint_as_float(r2[4 * t + e]));
       }
     }
-    put_state(x);  // (the next step's operand first: it is on the chain)
-    float* dst = starts + (bh * nseg + s + 1) * TK * TV;
+    put_state(x);
 #pragma unroll
-    for (int t = 0; t < kCombineCols; t += 4)
-      *reinterpret_cast<float4*>(dst + lm_off(k, v0 + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
-#pragma unroll
-    for (int t = 0; t < kCombineCols / 4; ++t) zc[t] = zn[t];
+    for (int t = 0; t < kCombineHalf / 4; ++t) zc[t] = zn[t];
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     if (abort_flag) break;
   }
+  if (nsteps > 0 && !abort_flag) store_start(nsteps, x);
   if (abort_flag && tid == 0) {
     // Copies still in flight land before the CTA's shared memory is released.
     for (int c = landed; c < issued; ++c)
@@ -641,7 +650,7 @@ seg_combine_kernel(const char* mz, const float* init, float* starts, int L, int 
   }
   fence_before_sync();
   __syncthreads();
-  if (quarter == 0) tmem_dealloc(tbase, 128);
+  if (warp == 0) tmem_dealloc(tbase, 64);
 }
 
 // ---------------------------------------------------------------------------
