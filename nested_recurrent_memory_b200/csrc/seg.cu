@@ -670,8 +670,12 @@ struct ProbeArgs {
   int32_t* status;
 };
 
-constexpr int kProbeScratch = 98304;
-constexpr int kGpartOffP = 65536 + 16384;
+// Probe scratch after the state: [W_w | W_g] (64 KB), the bank then V' (up
+// to 32 KB), [W_k^T | W_b] (64 KB). Both weight blocks arrive with the
+// first copies, so the second gate product waits on no load; the gate
+// partials (fp16) go over the state once P1 has read it.
+constexpr int kProbeW2A = 65536 + 32768;
+constexpr int kProbeScratch = kProbeW2A + 65536;
 
 __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a) {
   if (seg_gate_closed(a.status)) return;
@@ -690,6 +694,7 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
   uint8_t* X = sm + kStateBytes;
   bf16* XW = reinterpret_cast<bf16*>(X);
   bf16* XQ = reinterpret_cast<bf16*>(X + 65536);
+  bf16* XW2 = reinterpret_cast<bf16*>(X + kProbeW2A);
   const char* pt = a.ptc + int64_t(h) * PT_SIZE;
   // The level below's state after its firings up to this one
   // (chunk.py:39-55): group ((i + 1) f_l) // f_{l-1} of the level below.
@@ -703,10 +708,11 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
     mbar_init(&bar_mma, 1);
     fence_mbar_init();
     abort_flag = 0;
-    const uint32_t bytes = kStateBytes + 65536 + (a.learned ? mp * 256 : 0);
+    const uint32_t bytes = kStateBytes + 2 * 65536 + (a.learned ? mp * 256 : 0);
     mbar_arrive_expect_tx(&bar_ld, bytes);
     bulk_g2s(Sbf, S_src, kStateBytes, &bar_ld);
     bulk_g2s(XW, pt + PT_W2B, 65536u, &bar_ld);
+    bulk_g2s(XW2, pt + PT_W2A, 65536u, &bar_ld);
     if (a.learned) bulk_g2s(XQ, pt + PT_QB, uint32_t(mp * 256), &bar_ld);
   }
   fence_before_sync();
@@ -774,14 +780,9 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
   if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
   ph_mma ^= 1;
   fence_after_sync();
-  if (split && tid == 0) {
-    mbar_arrive_expect_tx(&bar_ld, 65536u);
-    bulk_g2s(XW, pt + PT_W2A, 65536u, &bar_ld);
-  }
   // w = sigmoid(w_logit) into v * w (TMEM); -softplus(g_logit - 4) per pair
-  // into shared memory (probe.py:63-65).
-  float* gpart = reinterpret_cast<float*>(X);
-  uint32_t* gpart16 = reinterpret_cast<uint32_t*>(X + kGpartOffP);
+  // into shared memory as fp16 pairs (probe.py:63-65), over the state.
+  uint32_t* gpart16 = reinterpret_cast<uint32_t*>(Sbf);
   {
     float av[32], vp[32];
     if (split) {
@@ -819,8 +820,11 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
       tmem_st32(taddr(tV, 32 * quarter, c0), vp);
       tmem_ld32(taddr(tG, 32 * quarter, 128 + c0), av);
 #pragma unroll
-      for (int u = 0; u < 32; ++u)
-        gpart[row * 128 + ((c0 + u) ^ (row & 31))] = -softplus_fast(av[u] + kGLogitInit);
+      for (int u = 0; u < 32; u += 2) {
+        const __half2 g2 = __floats2half2_rn(-softplus_fast(av[u] + kGLogitInit),
+                                             -softplus_fast(av[u + 1] + kGLogitInit));
+        gpart16[row * 64 + (((c0 + u) >> 1) ^ (row & 31))] = *reinterpret_cast<const uint32_t*>(&g2);
+      }
     }
   }
   tmem_wait_st();
@@ -828,12 +832,8 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
   {
     const int kk = tid & 127, qq = tid >> 7, r0 = qq * (nq >> 2), r1 = r0 + (nq >> 2);
     float sum = 0.f;
-    if (split) {
-      const __half* g16 = reinterpret_cast<const __half*>(gpart16);
-      for (int r = r0; r < r1; ++r) sum += __half2float(g16[2 * (r * 64 + ((kk >> 1) ^ (r & 31))) + (kk & 1)]);
-    } else {
-      for (int r = r0; r < r1; ++r) sum += gpart[r * 128 + (kk ^ (r & 31))];
-    }
+    const __half* g16 = reinterpret_cast<const __half*>(gpart16);
+    for (int r = r0; r < r1; ++r) sum += __half2float(g16[2 * (r * 64 + ((kk >> 1) ^ (r & 31))) + (kk & 1)]);
     red[qq * 128 + kk] = sum;
   }
   __syncthreads();
@@ -841,20 +841,14 @@ __global__ void __launch_bounds__(kProbeThreads, 1) seg_probe_kernel(ProbeArgs a
     egp[tid] = expf((red[tid] + red[128 + tid] + red[256 + tid] + red[384 + tid]) / float(nq));
   fence_proxy_async();
   __syncthreads();
-  if (tid == 0 && !split) {
-    mbar_arrive_expect_tx(&bar_ld, 65536u);
-    bulk_g2s(XW, pt + PT_W2A, 65536u, &bar_ld);
-  }
-  if (!mbar_wait(&bar_ld, ph_ld)) abort_flag = 1;
-  ph_ld ^= 1;
   // P2a: [u | b_logit] = V' . [W_k^T | W_b] (probe.py:60, :99)
   if (tid == 0) {
     fence_after_sync();
     if (split) {
-      mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_half, false);
-      mma_tile(tG + (16u << 16), smem_u32(XQ), smem_u32(XW + 128 * 128), TV, id_half, false);
+      mma_tile(tG, smem_u32(XQ), smem_u32(XW2), TV, id_half, false);
+      mma_tile(tG + (16u << 16), smem_u32(XQ), smem_u32(XW2 + 128 * 128), TV, id_half, false);
     } else {
-      mma_tile(tG, smem_u32(XQ), smem_u32(XW), TV, id_gate, false);
+      mma_tile(tG, smem_u32(XQ), smem_u32(XW2), TV, id_gate, false);
     }
     mma_commit(&bar_mma);
   }
