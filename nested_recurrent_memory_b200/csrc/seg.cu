@@ -355,23 +355,26 @@ seg_scan_kernel(SegScanArgs a, int replay) {
     fence_after_sync();
     // E1: Yv = Y - R . X -> bf16 MN-major B operand [Kd = ROWS][N = V].
     if (e1) {
+      // Both column halves in one TMEM round trip.
+      uint32_t raw[64];
+      tmem_ld32_nowait(taddr(tD, 32 * quarter, c0), raw);
+      tmem_ld32_nowait(taddr(tD, 32 * quarter, c0 + 32), raw + 32);
+      tmem_wait_ld();
+      tmem_regs_after_wait32(raw);
+      tmem_regs_after_wait32(raw + 32);
+      const float* x = reinterpret_cast<const float*>(raw);
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float x[32];
-        tmem_ld32(taddr(tD, 32 * quarter, c0 + 32 * hh), x);
+      for (int c = 0; c < 8; ++c) {
+        float y[8];
+        if (mode == 0) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float y[8];
-          if (mode == 0) {
+          for (int t = 0; t < 8; ++t) y[t] = -x[8 * c + t];
+        } else {
+          unpack8(yraw[c], NGDN2_BF16, y);
 #pragma unroll
-            for (int t = 0; t < 8; ++t) y[t] = -x[8 * c + t];
-          } else {
-            unpack8(yraw[4 * hh + c], NGDN2_BF16, y);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) y[t] -= x[8 * c + t];
-          }
-          *reinterpret_cast<uint4*>(Yv + mnmajor_off(k, c0 + 32 * hh + 8 * c, ROWS)) = pack8(y);
+          for (int t = 0; t < 8; ++t) y[t] -= x[8 * c + t];
         }
+        *reinterpret_cast<uint4*>(Yv + mnmajor_off(k, c0 + 8 * c, ROWS)) = pack8(y);
       }
     }
     fence_proxy_async();
@@ -405,18 +408,22 @@ seg_scan_kernel(SegScanArgs a, int replay) {
     // TMEM state scaled by the next step's d. Level 0's output rows (lanes
     // 64..127 of tD) go out as well.
     const bool seg_end = j + 1 == j1;
+    {
+      // Both column halves of the state in one TMEM round trip.
+      uint32_t raw[64];
+      tmem_ld32_nowait(taddr(tX, 32 * quarter, c0), raw);
+      tmem_ld32_nowait(taddr(tX, 32 * quarter, c0 + 32), raw + 32);
+      tmem_wait_ld();
+      tmem_regs_after_wait32(raw);
+      tmem_regs_after_wait32(raw + 32);
+      float* x = reinterpret_cast<float*>(raw);
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int cc = c0 + 32 * hh;
-      float x[32];
-      tmem_ld32(taddr(tX, 32 * quarter, cc), x);
-#pragma unroll
-      for (int c = 0; c < 32; c += 8)
-        *reinterpret_cast<uint4*>(Xb + mnmajor_off(k, cc + c, TK)) = pack8(x + c);
+      for (int c = 0; c < 64; c += 8)
+        *reinterpret_cast<uint4*>(Xb + mnmajor_off(k, c0 + c, TK)) = pack8(x + c);
       if (seg_end && last_seg) {
 #pragma unroll
-        for (int t = 0; t < 32; t += 4)
-          *reinterpret_cast<float4*>(a.fin + ((bh * a.L + a.level) * TK + k) * TV + cc + t) =
+        for (int t = 0; t < 64; t += 4)
+          *reinterpret_cast<float4*>(a.fin + ((bh * a.L + a.level) * TK + k) * TV + c0 + t) =
               make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
       }
       if (seg_end && mode == 0) {
@@ -424,39 +431,46 @@ seg_scan_kernel(SegScanArgs a, int replay) {
         bf16* mh = reinterpret_cast<bf16*>(a.mz + (bh * (a.nseg - 1) + s) * int64_t(kMzBytes));
         bf16* ml = mh + TK * TV;
 #pragma unroll
-        for (int c = 0; c < 32; c += 8) {
+        for (int c = 0; c < 64; c += 8) {
           float hi[8], lo[8];
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
             hi[t] = __bfloat162float(__float2bfloat16_rn(x[c + t]));
             lo[t] = x[c + t] - hi[t];
           }
-          *reinterpret_cast<uint4*>(mh + kmajor_off(k, cc + c, TK)) = pack8(hi);
-          *reinterpret_cast<uint4*>(ml + kmajor_off(k, cc + c, TK)) = pack8(lo);
+          *reinterpret_cast<uint4*>(mh + kmajor_off(k, c0 + c, TK)) = pack8(hi);
+          *reinterpret_cast<uint4*>(ml + kmajor_off(k, c0 + c, TK)) = pack8(lo);
         }
       }
       if (seg_end && mode == 1) {
         float* z = reinterpret_cast<float*>(a.mz + (bh * (a.nseg - 1) + s) * int64_t(kMzBytes) +
                                             2 * kStateBytes);
 #pragma unroll
-        for (int t = 0; t < 32; t += 4)
-          *reinterpret_cast<float4*>(z + lm_off(k, cc + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
+        for (int t = 0; t < 64; t += 4)
+          *reinterpret_cast<float4*>(z + lm_off(k, c0 + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
       }
       if (!seg_end) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) x[t] *= dnext;
-        tmem_st32(taddr(tX, 32 * quarter, cc), x);
+        for (int t = 0; t < 64; ++t) x[t] *= dnext;
+        tmem_st32(taddr(tX, 32 * quarter, c0), x);
+        tmem_st32(taddr(tX, 32 * quarter, c0 + 32), x + 32);
       }
-      if (out && quarter >= 2) {
-        const int i = 32 * (quarter - 2) + lane, t = j * kC + i;
-        float y[32];
-        tmem_ld32(taddr(tD, 32 * quarter, cc), y);
-        if (t < a.T) {
-          uint4* dst = reinterpret_cast<uint4*>(
-              reinterpret_cast<uint16_t*>(a.o) + ((int64_t(b) * a.T + t) * a.H + h) * TV + cc);
+    }
+    if (out && quarter >= 2) {
+      // Level 0's output rows, both column halves in one round trip.
+      const int i = 32 * (quarter - 2) + lane, t = j * kC + i;
+      uint32_t raw[64];
+      tmem_ld32_nowait(taddr(tD, 32 * quarter, c0), raw);
+      tmem_ld32_nowait(taddr(tD, 32 * quarter, c0 + 32), raw + 32);
+      tmem_wait_ld();
+      tmem_regs_after_wait32(raw);
+      tmem_regs_after_wait32(raw + 32);
+      const float* y = reinterpret_cast<const float*>(raw);
+      if (t < a.T) {
+        uint4* dst = reinterpret_cast<uint4*>(
+            reinterpret_cast<uint16_t*>(a.o) + ((int64_t(b) * a.T + t) * a.H + h) * TV + c0);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) dst[u] = a.dtype == NGDN2_BF16 ? pack8(y + 8 * u) : pack8h(y + 8 * u);
-        }
+        for (int u = 0; u < 8; ++u) dst[u] = a.dtype == NGDN2_BF16 ? pack8(y + 8 * u) : pack8h(y + 8 * u);
       }
     }
     tmem_wait_st();
