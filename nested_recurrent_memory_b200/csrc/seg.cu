@@ -184,10 +184,7 @@ inline SegLayout seg_layout(const FwdParams& p) {
 }
 
 // fp32 [K][V] states kept between kernels (segment transitions Z, segment
-// start states) in a lane-major layout: element (k, v) at
-// ((v / 4) * K + k) * 4 + v % 4, so the 32 lanes of a warp that own rows
-// k .. k + 31 access 512 contiguous bytes per float4 instead of 32 rows.
-__device__ __forceinline__ int lm_off(int k, int v) { return ((v >> 2) * TK + k) * 4 + (v & 3); }
+// start states) use the lane-major layout of lm_off (tc_common.cuh).
 
 __device__ __forceinline__ bool seg_gate_closed(const int32_t* status) {
   return status && (*reinterpret_cast<const volatile int32_t*>(status) & NGDN2_STATUS_GATE_TIMEOUT);

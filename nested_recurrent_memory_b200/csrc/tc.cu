@@ -692,8 +692,8 @@ constexpr int kGpartOff = 65536 + 16384;
 // fp32 accumulators in TMEM columns 128..511 (the chunk accumulators are
 // free between chunks); bf16 operands in ``X`` (the record buffer, reloaded
 // after the promotion). The fp32 master of S_l is in global memory,
-// transposed ([V][K]) so that lane-per-key TMEM traffic reads and writes it
-// in coalesced 128-byte rows. With 64 pairs the gate products go to the two
+// lane-major (lm_off) so that lane-per-key TMEM traffic reads and writes it
+// as float4 runs of 512 contiguous bytes a warp. With 64 pairs the gate products go to the two
 // half-lane groups of the same TMEM columns so every lane has work.
 // 512 threads: warp w reads TMEM lane quarter (w & 3), columns 32 * (w >> 2).
 __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* ws, int h, int l,
@@ -706,7 +706,7 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   const char* pt = ws + lay.ptc_off + (int64_t(l - 1) * p.H + h) * PT_SIZE;
   bf16* XW = reinterpret_cast<bf16*>(X);
   bf16* XQ = reinterpret_cast<bf16*>(X + 65536);
-  float* Sl = Mt + int64_t(l - 1) * TK * TV;  // fp32 master of level l, [V][K]
+  float* Sl = Mt + int64_t(l - 1) * TK * TV;  // fp32 master of level l, lane-major (lm_off)
   const uint32_t tV = tb + 128, tG = tb + 256, tS = tb + 384;
   const int row = (mp == 128) ? 32 * quarter + lane : (lane < 16 ? 16 * quarter + lane : -1);
   const bool split = mp == 64;
@@ -928,9 +928,17 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
   {
     const int k = 32 * quarter + lane;
     const float e = egp[k];
+    float4 sl4[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) sl4[t] = *reinterpret_cast<const float4*>(Sl + lm_off(k, c0 + 4 * t));
     float x[32];
 #pragma unroll
-    for (int t = 0; t < 32; ++t) x[t] = Sl[(c0 + t) * TK + k] * e;
+    for (int t = 0; t < 8; ++t) {
+      x[4 * t] = sl4[t].x * e;
+      x[4 * t + 1] = sl4[t].y * e;
+      x[4 * t + 2] = sl4[t].z * e;
+      x[4 * t + 3] = sl4[t].w * e;
+    }
     tmem_st32(taddr(tS, 32 * quarter, c0), x);
     tmem_wait_st();
   }
@@ -968,7 +976,8 @@ __device__ void promote_tc(const FwdParams& p, const TcLayout& lay, const char* 
     float x[32];
     tmem_ld32(taddr(tS, 32 * quarter, c0), x);
 #pragma unroll
-    for (int t = 0; t < 32; ++t) Sl[(c0 + t) * TK + k] = x[t];
+    for (int t = 0; t < 32; t += 4)
+      *reinterpret_cast<float4*>(Sl + lm_off(k, c0 + t)) = make_float4(x[t], x[t + 1], x[t + 2], x[t + 3]);
 #pragma unroll
     for (int c = 0; c < 32; c += 8)
       *reinterpret_cast<uint4*>(Sbf + l * TK * TV + mnmajor_off(k, c0 + c, TK)) = pack8(x + c);
@@ -1141,7 +1150,7 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
   bf16* Vn = reinterpret_cast<bf16*>(QT + int64_t(L - 1) * TILE_QK);
   float* Sg = p.fin + bh * L * TK * TV;
   const bool learned = p.promotion != NGDN2_PROMOTION_MERGE;
-  // Learned promotions keep the upper levels' fp32 masters transposed in
+  // Learned promotions keep the upper levels' fp32 masters lane-major in
   // the workspace; merge promotions (row by row) use final_state as is.
   float* Mt = reinterpret_cast<float*>(ws + lay.mast_off) + bh * (L > 1 ? L - 1 : 0) * TK * TV;
   const char* rec0 = ws + lay.chunks_off + bh * p.NT * lay.rec.size;
@@ -1160,8 +1169,8 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     Sg[e] = p.init ? p.init[bh * L * TK * TV + e] : 0.f;
   if (learned) {
     for (int64_t e = tid; e < int64_t(L - 1) * TK * TV; e += kScanThreads) {
-      const int64_t l1 = e / (TK * TV), r2 = e % (TK * TV), v = r2 / TK, k = r2 % TK;
-      Mt[e] = p.init ? p.init[bh * L * TK * TV + (l1 + 1) * TK * TV + k * TV + v] : 0.f;
+      const int64_t l1 = e / (TK * TV), r2 = e % (TK * TV), k = r2 / TV, v = r2 % TV;
+      Mt[l1 * TK * TV + lm_off(int(k), int(v))] = p.init ? p.init[bh * L * TK * TV + (l1 + 1) * TK * TV + r2] : 0.f;
     }
   }
   fence_before_sync();
@@ -1545,12 +1554,12 @@ scan_tc_kernel(FwdParams p, TcLayout lay, char* ws, const __grid_constant__ CUte
     }
   }
   if (abort_flag && tid == 0) set_status(p, NGDN2_STATUS_WAIT_TIMEOUT);
-  // Upper levels' final states from the transposed masters.
+  // Upper levels' final states from the lane-major masters.
   if (learned) {
     __syncthreads();
     for (int64_t e = tid; e < int64_t(L - 1) * TK * TV; e += kScanThreads) {
       const int64_t l1 = e / (TK * TV), r2 = e % (TK * TV), k = r2 / TV, v = r2 % TV;
-      Sg[(l1 + 1) * TK * TV + r2] = Mt[l1 * TK * TV + v * TK + k];
+      Sg[(l1 + 1) * TK * TV + r2] = Mt[l1 * TK * TV + lm_off(int(k), int(v))];
     }
   }
   fence_before_sync();

@@ -52,7 +52,7 @@ constexpr int64_t PT_SIZE = PT_W2B + 65536;
 
 // Workspace of the fused family: the promotion operands (bf16, per level
 // and head), the chunk records, and the learned arm's fp32 masters of the
-// upper levels (transposed [V][K], per (b, h)).
+// upper levels (lane-major, lm_off, per (b, h)).
 struct TcLayout {
   TcRecord rec;
   int64_t ptc_off, chunks_off, mast_off, total;
@@ -193,6 +193,13 @@ struct PrepMaps {
   CUtensorMap m[6];
   unsigned valid;
 };
+
+// fp32 [K][V] states kept in global memory in a lane-major layout: element
+// (k, v) at ((v / 4) * K + k) * 4 + v % 4, so the 32 lanes of a warp that own
+// rows k .. k + 31 access 512 contiguous bytes per float4.
+__host__ __device__ __forceinline__ int lm_off(int k, int v) {
+  return ((v >> 2) * TK + k) * 4 + (v & 3);
+}
 
 }  // namespace tcx
 }  // namespace ngdn2
