@@ -335,6 +335,22 @@ seg_scan_kernel(SegScanArgs a, int replay) {
   const uint32_t id_r = idesc_f16(128, 128, true, false, true);    // R . Xb (K-major A)
   const uint32_t id_p = idesc_f16(128, 128, true, true, true);     // P^T . Yv (MN-major A)
   uint32_t ph_a = 0, ph_b = 0, ph_mma = 0;
+  // Level 0's output rows of a step are staged in Yv (free once MMA2 has
+  // read it) as bf16 / fp16 rows with 16-byte chunks XOR-swizzled by row,
+  // and copied out by all threads, a row per 16 lanes, during the next
+  // step's MMA1 (or after the last step).
+  uint8_t* Ys = reinterpret_cast<uint8_t*>(Yv);
+  auto flush_out = [&](int jj) {
+#pragma unroll
+    for (int r = 0; r < kC * 16 / kSegThreads; ++r) {
+      const int e = tid + kSegThreads * r, row = e >> 4, ch = e & 15, t = jj * kC + row;
+      if (t < a.T)
+        reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) +
+                                 ((int64_t(b) * a.T + t) * a.H + h) * TV)[ch] =
+            *reinterpret_cast<const uint4*>(Ys + row * 256 + ((ch ^ (row & 15)) << 4));
+    }
+  };
+  int pend = -1;  // step whose output rows wait in Yv
   for (int j = j0; j < j1; ++j) {
     // MMA1: R . X (rows of R in lanes 0 .. ROWS - 1; for level 0 with its
     // output, the read queries Q follow W, so Q . X lands in lanes 64..127).
@@ -347,6 +363,12 @@ seg_scan_kernel(SegScanArgs a, int replay) {
     ph_a ^= 1;
     const float dnext = j + 1 < j1 ? fetch_d(j + 1) : 1.f;
     __syncwarp();
+    if (pend >= 0) {
+      // (E1 below overwrites Yv.)
+      flush_out(pend);
+      pend = -1;
+      __syncthreads();
+    }
     if (!mbar_wait(&bar_mma, ph_mma)) abort_flag = 1;
     ph_mma ^= 1;
     fence_after_sync();
@@ -463,13 +485,13 @@ seg_scan_kernel(SegScanArgs a, int replay) {
       tmem_regs_after_wait32(raw);
       tmem_regs_after_wait32(raw + 32);
       const float* y = reinterpret_cast<const float*>(raw);
-      if (t < a.T) {
-        uint4* dst = reinterpret_cast<uint4*>(
-            reinterpret_cast<uint16_t*>(a.o) + ((int64_t(b) * a.T + t) * a.H + h) * TV + c0);
+      (void)t;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) dst[u] = a.dtype == NGDN2_BF16 ? pack8(y + 8 * u) : pack8h(y + 8 * u);
-      }
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(Ys + i * 256 + ((((c0 >> 3) + u) ^ (i & 15)) << 4)) =
+            a.dtype == NGDN2_BF16 ? pack8(y + 8 * u) : pack8h(y + 8 * u);
     }
+    if (out) pend = j;
     tmem_wait_st();
     dcur = dnext;
     fence_proxy_async();
@@ -484,6 +506,7 @@ seg_scan_kernel(SegScanArgs a, int replay) {
       if (slot >= 0) copy_out(slot);
     }
   }
+  if (pend >= 0 && !abort_flag) flush_out(pend);
   if (abort_flag && tid == 0 && a.status) atomicOr(a.status, NGDN2_STATUS_WAIT_TIMEOUT);
   fence_before_sync();
   __syncthreads();
