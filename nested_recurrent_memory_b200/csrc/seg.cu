@@ -324,11 +324,16 @@ seg_scan_kernel(SegScanArgs a, int replay) {
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  // The state entering group 0 of an upper level is its start state.
+  // An emitted state goes out by one bulk copy from Xb (every thread's
+  // writes to it are fenced for the async proxy before the barrier that
+  // precedes this); thread 0 waits for the copy to have read Xb before the
+  // barrier after which Xb is rewritten (E1's). The state entering group 0
+  // of an upper level is its start state.
   auto copy_out = [&](int slot) {
-    const uint4* srcv = reinterpret_cast<const uint4*>(Xb);
-    uint4* dst = reinterpret_cast<uint4*>(a.E + (bh * a.nE + slot) * (TK * TV));
-    for (int e = tid; e < kStateBytes / 16; e += kSegThreads) dst[e] = srcv[e];
+    if (tid == 0) {
+      bulk_s2g(a.E + (bh * a.nE + slot) * (TK * TV), Xb, kStateBytes);
+      bulk_commit();
+    }
   };
   if (replay && a.emit_every == 0 && s == 0) copy_out(0);
 
@@ -396,6 +401,7 @@ seg_scan_kernel(SegScanArgs a, int replay) {
         *reinterpret_cast<uint4*>(Yv + mnmajor_off(k, c0 + 8 * c, ROWS)) = pack8(y);
       }
     }
+    if (tid == 0) bulk_wait_read0();  // (E2 below rewrites Xb)
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
@@ -507,6 +513,7 @@ seg_scan_kernel(SegScanArgs a, int replay) {
     }
   }
   if (pend >= 0 && !abort_flag) flush_out(pend);
+  if (tid == 0) bulk_wait0();
   if (abort_flag && tid == 0 && a.status) atomicOr(a.status, NGDN2_STATUS_WAIT_TIMEOUT);
   fence_before_sync();
   __syncthreads();
