@@ -1107,19 +1107,6 @@ seg_read_kernel(ReadArgs a, const __grid_constant__ CUtensorMap qmap) {
     }
   } else {
     const uint32_t id = idesc_f16(128, 128, true, false, true);
-    // mix_l scale of this thread's row (r = tid & 63 of chunk tid >> 6) for
-    // item it, loaded an item ahead of its use (zero past T or past the job).
-    auto mix_of = [&](int64_t it) {
-      const int64_t job = blockIdx.x + (it / nlev) * gridDim.x;
-      const int64_t bh = job / units;
-      const int n0 = int(job % units) * a.unit, c = tid >> 6;
-      const int t = (n0 + c) * kC + (tid & 63);
-      return c < min(a.unit, a.NT - n0) && t < a.T
-                 ? load_elem(a.mix.p, a.mix.off(int(bh / a.H), t, int(bh % a.H), int(it % nlev) + 1),
-                             a.mix.dt) * a.scale
-                 : 0.f;
-    };
-    float m_next = nitems > 0 ? mix_of(0) : 0.f;
     for (int64_t jj = 0; jj < my_jobs; ++jj) {
       const int64_t job = blockIdx.x + jj * gridDim.x;
       const int64_t bh = job / units;
@@ -1130,8 +1117,6 @@ seg_read_kernel(ReadArgs a, const __grid_constant__ CUtensorMap qmap) {
         const int64_t it = jj * nlev + li;
         const int l = li + 1, st = int(it & 1);
         uint8_t* base = sm + st * kReadStage;
-        const float m = m_next;
-        if (it + 1 < nitems) m_next = mix_of(it + 1);
         if (!mbar_wait(&bar_full[st], uint32_t((it >> 1) & 1))) abort_flag = 1;
         // Row r of chunk c scaled by mix_l scale (zero past T), as bf16 (fp16
         // q converted; q without a tensor map read here with plain loads).
@@ -1139,6 +1124,8 @@ seg_read_kernel(ReadArgs a, const __grid_constant__ CUtensorMap qmap) {
           const int r = tid & 63, c = tid >> 6;
           if (c < nc) {
             const int t = (n0 + c) * kC + r;
+            const float m =
+                t < a.T ? load_elem(a.mix.p, a.mix.off(b, t, h, l), a.mix.dt) * a.scale : 0.f;
             uint8_t* tile = base + kStateBytes + c * TILE_QK;
 #pragma unroll 4
             for (int u = 0; u < 16; ++u) {
