@@ -50,6 +50,11 @@ def parse_args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", default="config1")
     ap.add_argument("--path", choices=("auto", "simt", "tc", "tc_seg"), default="auto")
+    ap.add_argument("--gates", choices=("dense", "broadcast"), default="dense",
+                    help="b, w, g as materialised tensors (the canonical run) or as the "
+                         "stride-0 views of the per-token, per-head scalars the recipe defines "
+                         "(the broadcast fast path: the kernels read one scalar, and e2e uploads "
+                         "only the scalars)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--batch", type=int, default=None,
@@ -100,7 +105,10 @@ def alg_counts(w):
     for lvl in range(1, L):
         f = w["firing"][lvl]
         flop += 2 * K * V + (8 * m * K * V + 2 * m * V * (2 * K + V)) / (f * C)
-    nbytes = s * (L * K + K + V + K + K + V + L + V)
+    # q (L levels), k, v, g, b, w, mix, o; broadcast gates are one scalar
+    # per token and head each.
+    gates = 3 if w.get("gates") == "broadcast" else K + K + V
+    nbytes = s * (L * K + K + V + gates + L + V)
     nbytes += L * K * V * 4 / w["T"]
     nbytes += (L - 1) * (m * K + 3 * K * V + V * V) * s / w["T"]
     return flop, nbytes
@@ -386,6 +394,7 @@ def config_dict(args, w):
         "global_batch": gb, "seq_len": w["T"], "heads": w["H"],
         "parallelism": par,
         "l2": "inputs larger than L2 (no flush needed)",
+        "gates": getattr(args, "gates", "dense"),
     }
 
 
@@ -417,7 +426,7 @@ def run_ours(args, w):
     plan = shard(world, rank, w)
     inp = config_inputs(w["B"], w["T"], plan["H_local"], w["K"], w["V"], w["L"], w["m"],
                         w["firing"], dtype=w["dtype"], seed=plan["seed"], device=dev,
-                        gen_device=dev)
+                        gen_device=dev, dense_gates=args.gates == "dense")
     L = inp.pop("L")
     call = FwdCall(**inp, L=L, path=args.path)
     launches_per_step = call.num_launches
@@ -462,21 +471,30 @@ def run_ours(args, w):
     # e2e through the public API with pinned host buffers.
     e2e = None
     if not args.no_e2e:
-        host = {k: (v.cpu().pin_memory() if torch.is_tensor(v) and v.is_cuda else v)
+        from nested_recurrent_memory_b200.host import compact_view
+        # Pinned host copies; a broadcast (stride-0) input keeps only its
+        # distinct elements on the host and is uploaded as such.
+        host = {k: (compact_view(v).cpu().pin_memory().expand(v.shape)
+                    if torch.is_tensor(v) and v.is_cuda else v)
                 for k, v in inp.items()}
-        dev_bufs = {k: (torch.empty_like(v, device=dev) if torch.is_tensor(v) and v.is_pinned() else v)
+        dev_bufs = {k: (torch.empty(compact_view(v).shape, dtype=v.dtype, device=dev)
+                        if torch.is_tensor(v) and v.is_pinned() else v)
                     for k, v in host.items()}
-        h2d = sum(v.numel() * v.element_size() for v in host.values()
+        h2d = sum(compact_view(v).numel() * v.element_size() for v in host.values()
                   if torch.is_tensor(v) and v.is_pinned())
         o_host = torch.empty(call.o.shape, dtype=call.o.dtype).pin_memory()
         s_host = torch.empty(call.final.shape, dtype=call.final.dtype).pin_memory()
         d2h = o_host.numel() * o_host.element_size() + s_host.numel() * s_host.element_size()
 
         def e2e_step():
+            args_dev = {}
             for k, v in host.items():
                 if torch.is_tensor(v) and v.is_pinned():
-                    dev_bufs[k].copy_(v, non_blocking=True)
-            o, s = chunk_nested_gdn2(**dev_bufs, L=L, output_final_state=True)
+                    dev_bufs[k].copy_(compact_view(v), non_blocking=True)
+                    args_dev[k] = dev_bufs[k].expand(v.shape)
+                else:
+                    args_dev[k] = v
+            o, s = chunk_nested_gdn2(**args_dev, L=L, output_final_state=True)
             o_host.copy_(o, non_blocking=True)
             s_host.copy_(s, non_blocking=True)
 
@@ -527,12 +545,14 @@ def run_ours(args, w):
     # q's level-0 slice, k, v, g, b, w and mix; the scan reads the upper
     # levels' queries and the weights and writes o and the final states.
     s_el = 2 if str(w["dtype"]).endswith(("bfloat16", "float16")) else 4
-    prep_bytes = s_el * (4 * w["K"] + 2 * w["V"] + w["L"]) * token_heads
+    gate_el = 3 if w.get("gates") == "broadcast" else 2 * w["K"] + w["V"]
+    prep_bytes = s_el * (2 * w["K"] + w["V"] + gate_el + w["L"]) * token_heads
     kernel_bytes = {1: prep_bytes, 2: alg_bytes - prep_bytes}
     traffic = None
     kernel_traffic = {1: None, 2: None}
     tfile = ROOT / "profiles" / "traffic.json"
-    if tfile.exists():
+    # (The committed ncu traffic figures are for the dense-gate runs.)
+    if tfile.exists() and w.get("gates", "dense") == "dense":
         tj = json.loads(tfile.read_text())
         key = f"{args.config}:{call.path}"
         if key in tj:
@@ -793,6 +813,7 @@ def main():
         w["H"] = args.heads
     if args.seq is not None:
         w["T"] = args.seq
+    w["gates"] = args.gates
     if args.decode:
         run_decode(args, w)
     elif args.backward:

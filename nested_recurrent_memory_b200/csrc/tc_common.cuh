@@ -124,6 +124,13 @@ __device__ __forceinline__ void load8_raw(const void* p, int dt, int64_t o, int6
       return;
     }
   }
+  if (sd == 0) {
+    // A broadcast (stride-0) channel dimension: one element, eight times.
+    const float x = load_elem(p, o, dt);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = x;
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) out[i] = load_elem(p, o + i * sd, dt);
 }
@@ -139,6 +146,12 @@ __device__ __forceinline__ void load8(const TokView& tv, int b, int t, int h, in
 __device__ __forceinline__ uint4 raw8_at(const void* p, int dt, int64_t o, int64_t sd) {
   if (sd == 1 && (o & 7) == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0)
     return __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + o));
+  if (sd == 0) {
+    // A broadcast (stride-0) channel dimension: one element, eight times.
+    const uint32_t v = __ldg(reinterpret_cast<const uint16_t*>(p) + o);
+    const uint32_t w2 = v | (v << 16);
+    return make_uint4(w2, w2, w2, w2);
+  }
   uint4 r;
   uint16_t* h = reinterpret_cast<uint16_t*>(&r);
 #pragma unroll

@@ -14,6 +14,11 @@ batch and returns at once; ``result`` waits for a batch's outputs in host
 memory. Every batch still uploads all of its inputs and downloads its
 outputs: only the ordering across batches changes. The op itself is
 ``chunk_nested_gdn2``, unchanged.
+
+Inputs given as broadcast views (stride 0 along some dimensions, e.g. gates
+that are one scalar per token and head expanded over the head dimension,
+which the op reads as such) upload only their distinct elements and are
+expanded again on the device.
 """
 
 from __future__ import annotations
@@ -21,6 +26,15 @@ from __future__ import annotations
 import torch
 
 from .ops import chunk_nested_gdn2
+
+
+def compact_view(t: torch.Tensor) -> torch.Tensor:
+    """``t`` restricted to index 0 along its stride-0 dimensions: the
+    distinct elements of a broadcast view (``t`` itself when it has none)."""
+    if all(st != 0 or n <= 1 for st, n in zip(t.stride(), t.shape)):
+        return t
+    return t[tuple(slice(0, 1) if (st == 0 and n > 1) else slice(None)
+                   for st, n in zip(t.stride(), t.shape))]
 
 
 class HostPipeline:
@@ -33,7 +47,8 @@ class HostPipeline:
     Output buffers are pinned host tensors owned by the pipeline, one pair
     per in-flight slot; ``result(handle)`` returns them after the batch's
     download has finished, and they stay valid until that slot is reused
-    two submissions later.
+    two submissions later. An input that is a broadcast view of a pinned
+    tensor uploads only its distinct elements (``compact_view``).
     """
 
     def __init__(self, example: dict, device=None, **op_kwargs):
@@ -43,8 +58,9 @@ class HostPipeline:
                 raise ValueError(f"input {k!r} must be a pinned host tensor")
         self.names = list(example)
         self.op_kwargs = op_kwargs
-        self.slots = [{k: torch.empty_like(t, device=self.device) for k, t in example.items()}
-                      for _ in range(2)]
+        self.shapes = {k: t.shape for k, t in example.items()}
+        self.slots = [{k: torch.empty(compact_view(t).shape, dtype=t.dtype, device=self.device)
+                       for k, t in example.items()} for _ in range(2)]
         self.up, self.run, self.down = (torch.cuda.Stream(self.device) for _ in range(3))
         self.freed = [torch.cuda.Event() for _ in range(2)]      # slot inputs no longer read
         self.uploaded = [torch.cuda.Event() for _ in range(2)]
@@ -68,11 +84,12 @@ class HostPipeline:
             if self.count >= 2:
                 self.up.wait_event(self.freed[s])
             for k in self.names:
-                bufs[k].copy_(host_inputs[k], non_blocking=True)
+                bufs[k].copy_(compact_view(host_inputs[k]), non_blocking=True)
             self.uploaded[s].record(self.up)
         with torch.cuda.stream(self.run):
             self.run.wait_event(self.uploaded[s])
-            o, fs = chunk_nested_gdn2(**bufs, output_final_state=True, **self.op_kwargs)
+            args = {k: bufs[k].expand(self.shapes[k]) for k in self.names}
+            o, fs = chunk_nested_gdn2(**args, output_final_state=True, **self.op_kwargs)
             self.freed[s].record(self.run)
             self.computed[s].record(self.run)
         with torch.cuda.stream(self.down):
