@@ -1,10 +1,13 @@
 // One-token decode step (nested_gdn2/ops/naive.py:42-134,
 // naive_step_nested_gdn2), the path the layer takes past its chunked prefix
-// (nested_gdn2.py:218-224). One CTA per (b, h): level 0 takes the token's
-// delta-rule write, every level is read with the token's query and mixed
-// into o, then each level whose firing this token completes promotes,
-// bottom-up, per batch row. fp32 arithmetic on CUDA cores: a step touches
-// each state element once or twice, so it is bound by the state traffic.
+// (nested_gdn2.py:218-224). Level 0 takes the token's delta-rule write and
+// every level is read with the token's query and mixed into o: the value
+// columns are independent there, so a CTA takes one (b, h) and 16 or 32 of
+// its columns (more CTAs in flight over the state). Then, when this token
+// completes some row's firing, a second kernel (one CTA per (b, h))
+// promotes each firing level bottom-up on the new state. fp32 arithmetic on
+// CUDA cores: a step touches each state element once or twice, so it is
+// bound by the state traffic.
 
 #include <string.h>
 
@@ -21,18 +24,20 @@ namespace {
 
 constexpr int kStepThreads = 256;
 
+// Columns of V per CTA of the write / read kernel.
+__host__ __device__ inline int step_cols(int V) { return V % 32 == 0 ? 32 : 16; }
+
 // S' = e^g S - k (k b e^g)^T S + k (v w)^T for one pair (naive.py:7-39,
-// with N = 1), the reads sum_l mix_l scale q_l S_l (naive.py:111-113), then
-// the promotions (naive.py:115-132).
+// with N = 1) and the reads sum_l mix_l scale q_l S_l (naive.py:111-113),
+// for the columns [c0, c0 + step_cols(V)) of one (b, h).
 __global__ void __launch_bounds__(kStepThreads)
-step_kernel(FwdParams p, const int64_t* positions, int64_t position, int chunk,
-            const float* Sin, float* Sout) {
+step_kernel(FwdParams p, const float* Sin, float* Sout) {
   __shared__ float eg[128], kv[128], kbe[128], vw[128], mixv[NGDN2_MAX_LEVELS];
   __shared__ float sq[NGDN2_MAX_LEVELS][128];
   __shared__ float red[kStepThreads];
-  __shared__ float gsm[kGemmSmemFloats];
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
   const int K = p.K, V = p.V, L = p.L, tid = threadIdx.x;
+  const int Vs = step_cols(V), c0 = blockIdx.y * Vs;
   const int64_t lv = int64_t(K) * V;
   const float* S = Sin + int64_t(bh) * L * lv;
   float* So = Sout + int64_t(bh) * L * lv;
@@ -44,30 +49,28 @@ step_kernel(FwdParams p, const int64_t* positions, int64_t position, int chunk,
     kbe[d] = kk * p.b.at(b, 0, h, d) * e;
     for (int l = 0; l < L; ++l) sq[l][d] = p.scale * p.q.at(b, 0, h, l, d);
   }
-  for (int c = tid; c < V; c += blockDim.x) vw[c] = p.v.at(b, 0, h, c) * p.w.at(b, 0, h, c);
+  for (int cl = tid; cl < Vs; cl += blockDim.x)
+    vw[cl] = p.v.at(b, 0, h, c0 + cl) * p.w.at(b, 0, h, c0 + cl);
   if (tid < L) mixv[tid] = p.mix.at(b, 0, h, tid);
   __syncthreads();
 
-  // Thread (c, s): column c, rows s, s + sp, ... (sp slices of the rows).
-  const int sp = kStepThreads / V, c = tid % V, s = tid / V;
-  const bool act = s < sp;
+  // Thread (cl, s): column c0 + cl, rows s, s + sp, ... (sp slices).
+  const int sp = kStepThreads / Vs, cl = tid % Vs, s = tid / Vs, c = c0 + cl;
   auto reduce = [&](float part) {
     __syncthreads();
-    if (act) red[s * V + c] = part;
+    red[s * Vs + cl] = part;
     __syncthreads();
     float t = 0.f;
-    if (act)
-      for (int j = 0; j < sp; ++j) t += red[j * V + c];
+    for (int j = 0; j < sp; ++j) t += red[j * Vs + cl];
     return t;
   };
   // Level 0: d_c = sum_k (k b e^g)_k S[k][c], then the write and its read.
   float part = 0.f;
-  if (act)
-    for (int k = s; k < K; k += sp) part = fmaf(kbe[k], S[int64_t(k) * V + c], part);
+  for (int k = s; k < K; k += sp) part = fmaf(kbe[k], S[int64_t(k) * V + c], part);
   const float dc = reduce(part);
   part = 0.f;
-  if (act) {
-    const float u = vw[c] - dc;
+  {
+    const float u = vw[cl] - dc;
     for (int k = s; k < K; k += sp) {
       const float x = fmaf(eg[k], S[int64_t(k) * V + c], kv[k] * u);
       So[int64_t(k) * V + c] = x;
@@ -78,26 +81,32 @@ step_kernel(FwdParams p, const int64_t* positions, int64_t position, int chunk,
   // Upper levels: read (the state before any promotion of this token).
   for (int l = 1; l < L; ++l) {
     part = 0.f;
-    if (act) {
-      const float* Sl = S + l * lv;
-      float* Sol = So + l * lv;
-      for (int k = s; k < K; k += sp) {
-        const float x = Sl[int64_t(k) * V + c];
-        if (Sol != Sl) Sol[int64_t(k) * V + c] = x;
-        part = fmaf(sq[l][k], x, part);
-      }
+    const float* Sl = S + l * lv;
+    float* Sol = So + l * lv;
+    for (int k = s; k < K; k += sp) {
+      const float x = Sl[int64_t(k) * V + c];
+      if (Sol != Sl) Sol[int64_t(k) * V + c] = x;
+      part = fmaf(sq[l][k], x, part);
     }
     o = fmaf(mixv[l], reduce(part), o);
   }
-  if (act && s == 0) store_elem(p.o, int64_t(bh) * V + c, o, p.dtype);
+  if (s == 0) store_elem(p.o, int64_t(bh) * V + c, o, p.dtype);
+}
 
-  // Promotions of this row, bottom-up, on the new state (naive.py:115-132).
+// The promotions of a row whose token completes a firing, bottom-up, on
+// the new state (naive.py:115-132).
+__global__ void __launch_bounds__(kStepThreads)
+step_promote_kernel(FwdParams p, const int64_t* positions, int64_t position, int chunk,
+                    float* Sout) {
+  __shared__ float gsm[kGemmSmemFloats];
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  const int64_t lv = int64_t(p.K) * p.V;
+  float* So = Sout + int64_t(bh) * p.L * lv;
   const int64_t end = (positions ? positions[b] : position) + 1;
-  if (L < 2 || end % chunk != 0) return;
+  if (p.L < 2 || end % chunk != 0) return;
   const int64_t ch = end / chunk;
-  __syncthreads();
   float* sc = p.scan + int64_t(bh) * p.ss.size;
-  for (int l = 1; l < L; ++l) {
+  for (int l = 1; l < p.L; ++l) {
     if (ch % p.firing[l] != 0) continue;
     promote_simt(p, b, h, l, So, sc, gsm);
     __syncthreads();
@@ -211,10 +220,16 @@ NGDN2_API int ngdn2_step(const ngdn2_step_args* args, void* stream) {
       for (int l = 1; l < p.L; ++l) may_fire |= ch % p.firing[l] == 0;
     }
     if (may_fire && launch_convert_params(p, st) != cudaSuccess) return NGDN2_ERR_CUDA;
+    step_kernel<<<dim3(p.B * p.H, p.V / step_cols(p.V)), kStepThreads, 0, st>>>(
+        p, args->state_in, args->state_out);
+    if (cudaGetLastError() != cudaSuccess) return NGDN2_ERR_CUDA;
+    if (may_fire)
+      step_promote_kernel<<<p.B * p.H, kStepThreads, 0, st>>>(p, args->positions, args->position,
+                                                              args->chunk_size, args->state_out);
+    return cudaGetLastError() == cudaSuccess ? NGDN2_OK : NGDN2_ERR_CUDA;
   }
-  step_kernel<<<p.B * p.H, kStepThreads, 0, st>>>(p, args->positions, args->position,
-                                                   args->chunk_size, args->state_in,
-                                                   args->state_out);
+  step_kernel<<<dim3(p.B * p.H, p.V / step_cols(p.V)), kStepThreads, 0, st>>>(
+      p, args->state_in, args->state_out);
   return cudaGetLastError() == cudaSuccess ? NGDN2_OK : NGDN2_ERR_CUDA;
 }
 
