@@ -93,3 +93,19 @@ def test_host_pipeline_rejects_pageable_inputs_before_touching_cuda():
     from nested_recurrent_memory_b200 import HostPipeline
     with pytest.raises(ValueError, match="pinned"):
         HostPipeline({"q": torch.zeros(1, 64, 1, 2, 16)}, L=2)
+
+
+def test_compact_view_of_broadcast_inputs():
+    # The distinct elements of a stride-0 (broadcast) view, as HostPipeline
+    # and bench --gates broadcast upload them; a dense tensor is its own.
+    from nested_recurrent_memory_b200.host import compact_view
+    beta = torch.randn(2, 5, 3)
+    b = beta.unsqueeze(-1).expand(2, 5, 3, 64)
+    c = compact_view(b)
+    assert c.shape == (2, 5, 3, 1) and c.is_contiguous()
+    assert torch.equal(c.expand(b.shape), b)
+    dense = torch.randn(2, 5, 3, 64)
+    assert compact_view(dense) is dense
+    inp = config_inputs(1, 128, 2, 64, 64, 2, 16, (1, 2), dtype=torch.float32, dense_gates=False)
+    for k in ("b", "w", "g"):
+        assert compact_view(inp[k]).numel() == 128 * 2
