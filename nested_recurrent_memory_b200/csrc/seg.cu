@@ -124,7 +124,7 @@ inline int level_nseg(const FwdParams& p, int l) {
   const int bh = p.B * p.H > 0 ? p.B * p.H : 1;
   const bool r64 = level_rows(p, l) == 64;
   const int slots = kSMs * (r64 ? 2 : 1);
-  const double t_compose = r64 ? 2.9 : 4.4, t_replay = r64 ? 5.3 : 3.4, t_combine = 1.4;
+  const double t_compose = r64 ? 3.4 : 2.9, t_replay = r64 ? 5.1 : 3.1, t_combine = 1.4;
   int best = 1;
   double best_t = 1e30;
   for (int n = 1; n <= (steps / 4 > 1 ? steps / 4 : 1); ++n) {
