@@ -554,11 +554,17 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
              [&](int c, int k) { return S0[k * V + c]; }, gsm,
              [&](int i, int k, float a) { dRW[i * K + k] = -a; });
   for (int e = tid; e < kC * V; e += nth) dRU[e] = dvn[e];
-  // dG_last from S' = e^(G_last) S0: sum_v S0 dS' e^(G_last)
-  for (int k = tid; k < K; k += nth) {
-    float s = 0.f;
-    for (int c = 0; c < V; ++c) s = fmaf(S0[k * V + c], dSn[k * V + c], s);
-    dGl[k] = s * expf(Gs[(kC - 1) * KP + k]);
+  // dG_last from S' = e^(G_last) S0: sum_v S0 dS' e^(G_last); a warp per
+  // row, its lanes along the row (coalesced), then a shuffle reduction.
+  {
+    const int lane = tid & 31, warp = tid >> 5, nwarp = nth >> 5;
+    for (int k = warp; k < K; k += nwarp) {
+      float s = 0.f;
+      for (int c = lane; c < V; c += 32) s = fmaf(S0[k * V + c], dSn[k * V + c], s);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) dGl[k] = s * expf(Gs[(kC - 1) * KP + k]);
+    }
   }
   __syncthreads();
   // dR = (I + T)^-T dY: back substitution, one column of [dU | dW] per thread.
@@ -600,18 +606,26 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     const float gj = Gs[j * KP + d];
     const bool exact = npos[d] != 0;
     float acc = 0.f, accg = 0.f, ex = 1.f;
-    for (int i = j; i < kC; ++i) {
-      float x = 0.f;
-      if (exact) {
-        x = Gs[i * KP + d] - gj;
-        ex = expf(fminf(x, 0.f));
-      } else if (i > j) {
+    if (!exact) {
+      // (The same sums as below without the clamp: every exponent is <= 0,
+      // so both accumulate every term; one chain, fewer instructions.)
+      acc = As[j * 65 + j] * Qs[j * KP + d];
+      for (int i = j + 1; i < kC; ++i) {
         ex *= Eg[i * KP + d];
+        const float term = Dt[i * 65 + j] * Bs[i * KP + d] * Ks[i * KP + d] +
+                           As[i * 65 + j] * Qs[i * KP + d];
+        acc = fmaf(term, ex, acc);
       }
-      const float term = (i > j ? Dt[i * 65 + j] * Bs[i * KP + d] * Ks[i * KP + d] : 0.f) +
-                         As[i * 65 + j] * Qs[i * KP + d];
-      acc = fmaf(term, ex, acc);
-      if (x <= 0.f) accg = fmaf(term, ex, accg);
+      accg = acc;
+    } else {
+      for (int i = j; i < kC; ++i) {
+        const float x = Gs[i * KP + d] - gj;
+        ex = expf(fminf(x, 0.f));
+        const float term = (i > j ? Dt[i * 65 + j] * Bs[i * KP + d] * Ks[i * KP + d] : 0.f) +
+                           As[i * 65 + j] * Qs[i * KP + d];
+        acc = fmaf(term, ex, acc);
+        if (x <= 0.f) accg = fmaf(term, ex, accg);
+      }
     }
     dKTA[j * K + d] = acc;
     dGc[j * K + d] = -Ks[j * KP + d] * accg;
@@ -623,21 +637,29 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
     const float gi = Gs[i * KP + d];
     const bool exact = npos[d] != 0;
     float dbk = 0.f, dqs = 0.f, gbk = 0.f, gqs = 0.f, ex = 1.f;
-    for (int j = i; j >= 0; --j) {
-      float x = 0.f;
-      if (exact) {
-        x = gi - Gs[j * KP + d];
-        ex = expf(fminf(x, 0.f));
-      } else if (j < i) {
+    if (!exact) {
+      // (As in the column pass: no clamp, one pair of chains.)
+      dqs = As[i * 65 + i] * Ks[i * KP + d];
+      for (int j = i - 1; j >= 0; --j) {
         ex *= Eg[(j + 1) * KP + d];
+        const float kx = Ks[j * KP + d] * ex;
+        dbk = fmaf(Dt[i * 65 + j], kx, dbk);
+        dqs = fmaf(As[i * 65 + j], kx, dqs);
       }
-      const float kx = Ks[j * KP + d] * ex;
-      const float tt = j < i ? Dt[i * 65 + j] : 0.f, aa = As[i * 65 + j];
-      dbk = fmaf(tt, kx, dbk);
-      dqs = fmaf(aa, kx, dqs);
-      if (x <= 0.f) {
-        gbk = fmaf(tt, kx, gbk);
-        gqs = fmaf(aa, kx, gqs);
+      gbk = dbk;
+      gqs = dqs;
+    } else {
+      for (int j = i; j >= 0; --j) {
+        const float x = gi - Gs[j * KP + d];
+        ex = expf(fminf(x, 0.f));
+        const float kx = Ks[j * KP + d] * ex;
+        const float tt = j < i ? Dt[i * 65 + j] : 0.f, aa = As[i * 65 + j];
+        dbk = fmaf(tt, kx, dbk);
+        dqs = fmaf(aa, kx, dqs);
+        if (x <= 0.f) {
+          gbk = fmaf(tt, kx, gbk);
+          gqs = fmaf(aa, kx, gqs);
+        }
       }
     }
     const float q = Qs[i * KP + d], k = Ks[i * KP + d], bb = Bs[i * KP + d];
@@ -657,8 +679,10 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   if (tid < K) {
     float acc = dGl[tid];
     const float gl = Gs[(kC - 1) * KP + tid];
+#pragma unroll 8
     for (int i = 0; i < kC; ++i)
       acc += dKt[i * K + tid] * Ks[i * KP + tid] * expf(gl - Gs[i * KP + tid]);
+#pragma unroll 8
     for (int i = kC - 1; i >= 0; --i) {
       acc += dGc[i * K + tid];
       if (t0 + i < f.T) p.dg[orow(i, K) + tid] = acc;
