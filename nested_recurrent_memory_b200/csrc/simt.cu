@@ -10,8 +10,10 @@
 //            the decay-masked K.K^T and Q.K^T blocks, the unit-lower-
 //            triangular solve [U | W] = (I + A_kk)^-1 [w*v | k*b*e^G], the
 //            read queries with mix and scale folded in, k*e^(G_last - G)
-//            and e^(G_last). Decays use the reference's clamped exponent
-//            e^min(G_i - G_j, 0) element by element, exactly as the oracle.
+//            and e^(G_last). Decays follow the reference's clamped exponent
+//            e^min(G_i - G_j, 0): element by element where a log-decay is
+//            positive, as a row-factor x column-factor GEMM where none is
+//            (the clamp cannot bind there).
 //   scan  -- one CTA per (b, h), sequential over chunks: the state
 //            recurrence and output of level 0 (naive.py:376-392), the reads
 //            of levels >= 1 (naive.py:382-390) and, at each firing, the
@@ -85,27 +87,73 @@ __global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
   __syncthreads();
   // A_kk (strictly lower) and A_qk (lower, diagonal included) with the
   // clamped per-channel decay (naive.py:335-344, 354-358, 377-378).
-  for (int e = tid; e < kC * kC; e += blockDim.x) {
-    const int i = e / kC, j = e % kC;
-    float aq = 0.f, ak = 0.f;
-    if (j <= i) {
-      const float* gi = Gs + i * KP;
-      const float* gj = Gs + j * KP;
-      const float* qi = Qs + i * KP;
-      const float* bki = BKs + i * KP;
-      const float* kj = Ks + j * KP;
-      for (int d = 0; d < K; ++d) {
-        const float kd = kj[d] * expf(fminf(gi[d] - gj[d], 0.f));
-        aq = fmaf(qi[d], kd, aq);
-        ak = fmaf(bki[d], kd, ak);
+  //
+  // When every log-decay of the chunk is <= 0 (G non-increasing along the
+  // chunk on every channel) the clamp never binds for j <= i, and
+  // e^(G_i - G_j) = e^(G_i - G_0) e^(G_0 - G_j) splits into a row and a
+  // column factor: both blocks become one 128 x 64 x K GEMM over
+  // [q e^(G-G_0) ; b k e^(G-G_0)] and (k e^(G_0-G))^T, with 2 * 64 * K
+  // exponentials instead of one per (i, j, d). The split needs
+  // G_0 - G_63 <= 80 so that e^(G_0 - G_j) stays finite in fp32; other
+  // chunks (and K not a multiple of 16) take the exact per-element loop.
+  __shared__ int factored;
+  float* gsm = Aqk + kC * 65;  // block_gemm staging
+  if (tid == 0) factored = (K % 16) == 0;
+  __syncthreads();
+  if (tid < K) {
+    bool ok = Gs[tid] - Gs[(kC - 1) * KP + tid] <= 80.f;
+    for (int i = 1; i < kC; ++i) ok = ok && Gs[i * KP + tid] <= Gs[(i - 1) * KP + tid];
+    if (!ok) factored = 0;
+  }
+  __syncthreads();
+  float* ta = p.ck_ta ? p.ck_ta + ((int64_t(b) * p.H + h) * p.NT + n) * 2 * kC * kC : nullptr;
+  if (factored) {
+    block_gemm<false, true>(
+        2 * kC, kC, K,
+        [&](int r, int d) {
+          const int i = r < kC ? r : r - kC;
+          const float x = r < kC ? Qs[i * KP + d] : BKs[i * KP + d];
+          return x * expf(Gs[i * KP + d] - Gs[d]);
+        },
+        [&](int d, int j) { return Ks[j * KP + d] * expf(Gs[d] - Gs[j * KP + d]); }, gsm,
+        [&](int r, int j, float a) {
+          if (r < kC) {
+            Aqk[r * 65 + j] = j <= r ? a : 0.f;
+          } else {
+            const int i = r - kC;
+            Akk[i * 65 + j] = j < i ? a : 0.f;
+          }
+        });
+    __syncthreads();
+    if (ta) {
+      for (int e = tid; e < kC * kC; e += blockDim.x) {
+        const int i = e / kC, j = e % kC;
+        ta[e] = Akk[i * 65 + j];
+        ta[kC * kC + e] = Aqk[i * 65 + j] * p.scale;
       }
     }
-    Aqk[i * 65 + j] = aq;
-    Akk[i * 65 + j] = (j < i) ? ak : 0.f;
-    if (p.ck_ta) {
-      float* ta = p.ck_ta + ((int64_t(b) * p.H + h) * p.NT + n) * 2 * kC * kC;
-      ta[e] = (j < i) ? ak : 0.f;
-      ta[kC * kC + e] = aq * p.scale;
+  } else {
+    for (int e = tid; e < kC * kC; e += blockDim.x) {
+      const int i = e / kC, j = e % kC;
+      float aq = 0.f, ak = 0.f;
+      if (j <= i) {
+        const float* gi = Gs + i * KP;
+        const float* gj = Gs + j * KP;
+        const float* qi = Qs + i * KP;
+        const float* bki = BKs + i * KP;
+        const float* kj = Ks + j * KP;
+        for (int d = 0; d < K; ++d) {
+          const float kd = kj[d] * expf(fminf(gi[d] - gj[d], 0.f));
+          aq = fmaf(qi[d], kd, aq);
+          ak = fmaf(bki[d], kd, ak);
+        }
+      }
+      Aqk[i * 65 + j] = aq;
+      Akk[i * 65 + j] = (j < i) ? ak : 0.f;
+      if (ta) {
+        ta[e] = (j < i) ? ak : 0.f;
+        ta[kC * kC + e] = aq * p.scale;
+      }
     }
   }
   __syncthreads();
@@ -302,7 +350,9 @@ __global__ void __launch_bounds__(256) update_simt_kernel(UpdParams u) {
 // Host launchers
 // ---------------------------------------------------------------------------
 
-size_t prep_simt_smem(int K) { return sizeof(float) * (4 * kC * (K + 1) + 2 * kC * 65); }
+size_t prep_simt_smem(int K) {
+  return sizeof(float) * (4 * kC * (K + 1) + 2 * kC * 65 + kGemmSmemFloats);
+}
 
 cudaError_t launch_convert_params(const FwdParams& p, cudaStream_t stream) {
   if (p.L <= 1) return cudaSuccess;

@@ -105,6 +105,25 @@ def test_initial_state(promotion):
     assert rel_err(_np(s), rs) < FP32_REL
 
 
+@pytest.mark.parametrize("lift", [0.02, 0.1])
+def test_positive_log_decays_fp32(lift):
+    """Log-decays above zero on some channels: the chunk's cumulative decay is
+    no longer monotone there, so the CUDA-core path takes its exact
+    (per-element) intra-chunk branch for that chunk and the factorised one
+    elsewhere; both must match the oracle."""
+    inp = op_inputs(1, 256, 2, 64, 64, 2, 16, firing_intervals=(1, 2))
+    L = inp.pop("L")
+    g = inp["g"].clone()
+    g[:, 64:128, :, :8] = lift          # second chunk: positive on 8 channels
+    inp["g"] = g
+    o, s = chunk_nested_gdn2_fwd(**_to_dev(inp), L=L, output_final_state=True,
+                                 path="simt")
+    assert last_path() == "simt"
+    ro, rs = _oracle(inp, L)
+    assert rel_err(_np(o), ro) < FP32_REL
+    assert rel_err(_np(s), rs) < FP32_REL
+
+
 def test_l1_reduces_to_level_zero():
     inp = op_inputs(2, 256, 2, 64, 64, 1, 16, firing_intervals=(1,))
     L = inp.pop("L")
