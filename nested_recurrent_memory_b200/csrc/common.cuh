@@ -58,8 +58,11 @@ __device__ __forceinline__ float softplusf_(float x) {
 // loads each tile straight into shared memory when the previous one is
 // consumed (fewer live registers, for kernels at their register cap); operands are staged
 // through shared memory in 64x16 and 16x64 tiles (the next tile's elements
-// load into registers during the current tile's FMAs) and each thread owns a
-// 4x4 block of outputs. The block needs at least kGemmThreads threads (more
+// load into registers during the current tile's FMAs) and each thread owns
+// 4x4 outputs of the 64x64 tile at a stride of 16 (rows tm + 16 i, columns
+// tn + 16 j): a warp's operand reads then touch 2 (A) and 16 consecutive (B)
+// words, one shared-memory wavefront each, and its epilogue writes runs of
+// 16 consecutive columns. The block needs at least kGemmThreads threads (more
 // only join the barriers) and every thread must call it (it synchronises). M and N are arbitrary; Kd
 // must be a multiple of 16. ``smem`` holds kGemmSmemFloats floats.
 // ---------------------------------------------------------------------------
@@ -74,8 +77,8 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
   float* Bs = smem + 16 * kGemmLd;  // [16][65]
   const int tid = threadIdx.x;
   const bool act = tid < kGemmThreads;  // larger blocks: the rest only join the barriers
-  const int tm = (tid / 16) * 4;
-  const int tn = (tid % 16) * 4;
+  const int tm = tid / 16;
+  const int tn = tid % 16;
   constexpr int kPer = 64 * 16 / kGemmThreads;  // tile elements each thread stages
   for (int m0 = 0; m0 < M; m0 += 64) {
     for (int n0 = 0; n0 < N; n0 += 64) {
@@ -102,9 +105,9 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
             for (int kk = 0; kk < 16; ++kk) {
               float a[4], bb[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + i];
+              for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + 16 * i];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + j];
+              for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + 16 * j];
 #pragma unroll
               for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -146,9 +149,9 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
           for (int kk = 0; kk < 16; ++kk) {
             float a[4], bb[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + i];
+            for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + 16 * i];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + j];
+            for (int j = 0; j < 4; ++j) bb[j] = Bs[kk * kGemmLd + tn + 16 * j];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -163,7 +166,7 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
         for (int i = 0; i < 4; ++i)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            int gm = m0 + tm + i, gn = n0 + tn + j;
+            const int gm = m0 + tm + 16 * i, gn = n0 + tn + 16 * j;
             if (gm < M && gn < N) epi(gm, gn, acc[i][j]);
           }
       }
