@@ -95,43 +95,6 @@ struct BwdParams {
   LocalScratch ls;
 };
 
-// 8 consecutive elements from element offset o (element stride sd) as fp32:
-// one or two vector loads when contiguous and 16-byte aligned.
-__device__ __forceinline__ void load8_any(const void* base, int dt, int64_t o, int64_t sd,
-                                          float* out) {
-  if (sd == 1) {
-    if (dt != NGDN2_F32) {
-      const uint16_t* p16 = reinterpret_cast<const uint16_t*>(base) + o;
-      if ((reinterpret_cast<uintptr_t>(p16) & 15) == 0) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(p16);
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (dt == NGDN2_BF16) {
-            out[2 * i] = __uint_as_float(w[i] << 16);
-            out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-          } else {
-            out[2 * i] = __half2float(__ushort_as_half(uint16_t(w[i] & 0xffffu)));
-            out[2 * i + 1] = __half2float(__ushort_as_half(uint16_t(w[i] >> 16)));
-          }
-        }
-        return;
-      }
-    } else {
-      const float* p32 = reinterpret_cast<const float*>(base) + o;
-      if ((reinterpret_cast<uintptr_t>(p32) & 15) == 0) {
-        const float4 a = *reinterpret_cast<const float4*>(p32);
-        const float4 c = *reinterpret_cast<const float4*>(p32 + 4);
-        out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
-        out[4] = c.x; out[5] = c.y; out[6] = c.z; out[7] = c.w;
-        return;
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) out[i] = load_elem(base, o + i * sd, dt);
-}
-
 __device__ __forceinline__ const float* ck_level(const FwdParams& f, int64_t bh, int level, int j) {
   const int64_t kv = int64_t(f.K) * f.V;
   return level == 0 ? f.ck0 + (bh * (f.NT + 1) + j) * kv

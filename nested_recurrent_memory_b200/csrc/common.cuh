@@ -24,6 +24,15 @@ __device__ __forceinline__ float load_elem(const void* p, int64_t i, int dtype) 
   }
 }
 
+// load_elem with the dtype known at compile time (for loops whose loads
+// should all be in flight at once).
+template <int DT>
+__device__ __forceinline__ float load_typed(const void* p, int64_t i) {
+  if constexpr (DT == NGDN2_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  else if constexpr (DT == NGDN2_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  else return reinterpret_cast<const float*>(p)[i];
+}
+
 __device__ __forceinline__ void store_elem(void* p, int64_t i, float x, int dtype) {
   switch (dtype) {
     case NGDN2_BF16: reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x); break;

@@ -24,6 +24,8 @@
 // which doubles as the running state; per-(b, h) temporaries live in the
 // workspace.
 
+#include <type_traits>
+
 #include "fwd_params.cuh"
 #include "promote_simt.cuh"
 
@@ -57,23 +59,36 @@ __global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
   float* BKs = Ks + kC * KP;   // [64][K+1] b * k
   float* Akk = BKs + kC * KP;  // [64][65]
   float* Aqk = Akk + kC * 65;  // [64][65]
-  const int tid = threadIdx.x;
+  float* mixs = Aqk + kC * 65 + kGemmSmemFloats;  // [64][L] mix of the rows
+  const int tid = threadIdx.x, L = p.L;
   const int t0 = n * kC;
 
-  // Load the chunk; tokens past T are zero (naive.py:302-312).
-  for (int e = tid; e < kC * K; e += blockDim.x) {
-    const int i = e / K, d = e % K, t = t0 + i;
-    float vq = 0.f, vk = 0.f, vg = 0.f, vb = 0.f;
+  // Load the chunk, 8 channels per load and all four inputs before any
+  // store; tokens past T are zero (naive.py:302-312).
+  for (int e = tid; e < kC * K / 8; e += blockDim.x) {
+    const int i = e / (K / 8), d0 = 8 * (e % (K / 8)), t = t0 + i;
+    float q8[8], k8[8], g8[8], b8[8];
     if (t < p.T) {
-      vq = p.q.at(b, t, h, 0, d);
-      vk = p.k.at(b, t, h, d);
-      vg = p.g.at(b, t, h, d);
-      vb = p.b.at(b, t, h, d);
+      load8_any(p.q.p, p.q.dt, p.q.off(b, t, h, 0, d0), p.q.sd, q8);
+      load8_any(p.k.p, p.k.dt, p.k.off(b, t, h, d0), p.k.sd, k8);
+      load8_any(p.g.p, p.g.dt, p.g.off(b, t, h, d0), p.g.sd, g8);
+      load8_any(p.b.p, p.b.dt, p.b.off(b, t, h, d0), p.b.sd, b8);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) q8[u] = k8[u] = g8[u] = b8[u] = 0.f;
     }
-    Qs[i * KP + d] = vq;
-    Ks[i * KP + d] = vk;
-    Gs[i * KP + d] = vg;
-    BKs[i * KP + d] = vb * vk;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int x = i * KP + d0 + u;
+      Qs[x] = q8[u];
+      Ks[x] = k8[u];
+      Gs[x] = g8[u];
+      BKs[x] = b8[u] * k8[u];
+    }
+  }
+  for (int e = tid; e < kC * L; e += blockDim.x) {
+    const int i = e / L, l = e % L, t = t0 + i;
+    mixs[e] = t < p.T ? p.mix.at(b, t, h, l) : 0.f;
   }
   __syncthreads();
   // G = cumsum of g along the chunk (naive.py:329).
@@ -164,19 +179,41 @@ __global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
   // one column per thread (naive.py:346-351).
   const int c = tid;
   if (c < V + K) {
+    // Right-hand sides first (their global loads all in flight), then the
+    // dependent substitution chain.
     float x[kC];
+    if (c < V) {
+      auto rhs = [&](auto dt) {
+        constexpr int DT = decltype(dt)::value;
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+          const int t = t0 + i;
+          x[i] = (t < p.T) ? load_typed<DT>(p.w.p, p.w.off(b, t, h, c)) *
+                                 load_typed<DT>(p.v.p, p.v.off(b, t, h, c))
+                           : 0.f;
+        }
+      };
+      if (p.w.dt == p.v.dt && p.w.dt == NGDN2_BF16) {
+        rhs(std::integral_constant<int, NGDN2_BF16>());
+      } else if (p.w.dt == p.v.dt && p.w.dt == NGDN2_F16) {
+        rhs(std::integral_constant<int, NGDN2_F16>());
+      } else if (p.w.dt == p.v.dt && p.w.dt == NGDN2_F32) {
+        rhs(std::integral_constant<int, NGDN2_F32>());
+      } else {
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+          const int t = t0 + i;
+          x[i] = (t < p.T) ? p.w.at(b, t, h, c) * p.v.at(b, t, h, c) : 0.f;
+        }
+      }
+    } else {
+      const int d = c - V;
+#pragma unroll
+      for (int i = 0; i < kC; ++i) x[i] = BKs[i * KP + d] * expf(Gs[i * KP + d]);
+    }
 #pragma unroll
     for (int i = 0; i < kC; ++i) {
-      const int t = t0 + i;
-      float r;
-      if (c < V) {
-        r = (t < p.T) ? p.w.at(b, t, h, c) *
-                            p.v.at(b, t, h, c)
-                      : 0.f;
-      } else {
-        const int d = c - V;
-        r = BKs[i * KP + d] * expf(Gs[i * KP + d]);
-      }
+      float r = x[i];
 #pragma unroll
       for (int j = 0; j < i; ++j) r = fmaf(-Akk[i * 65 + j], x[j], r);
       x[i] = r;
@@ -190,25 +227,31 @@ __global__ void __launch_bounds__(256) prep_simt_kernel(FwdParams p) {
 
   // Output-side operands.
   for (int e = tid; e < kC * kC; e += blockDim.x) {
-    const int i = e / kC, j = e % kC, t = t0 + i;
-    const float m0 = t < p.T ? p.mix.at(b, t, h, 0) : 0.f;
+    const int i = e / kC, j = e % kC;
+    const float m0 = mixs[i * L];
     rec[p.rec.A + e] = (j <= i) ? Aqk[i * 65 + j] * p.scale * m0 : 0.f;
   }
   for (int e = tid; e < kC * K; e += blockDim.x) {
-    const int i = e / K, d = e % K, t = t0 + i;
-    const float m0 = t < p.T ? p.mix.at(b, t, h, 0) : 0.f;
+    const int i = e / K, d = e % K;
+    const float m0 = mixs[i * L];
     const float gi = Gs[i * KP + d];
     rec[p.rec.Q + e] = m0 * p.scale * Qs[i * KP + d] * expf(gi);
     rec[p.rec.Kt + e] = Ks[i * KP + d] * expf(Gs[(kC - 1) * KP + d] - gi);
   }
-  for (int l = 1; l < p.L; ++l) {
-    for (int e = tid; e < kC * K; e += blockDim.x) {
-      const int i = e / K, d = e % K, t = t0 + i;
-      float val = 0.f;
-      if (t < p.T)
-        val = p.mix.at(b, t, h, l) * p.scale *
-              p.q.at(b, t, h, l, d);
-      rec[p.rec.Q + int64_t(l) * kC * K + e] = val;
+  for (int l = 1; l < L; ++l) {
+    float* dst = rec + p.rec.Q + int64_t(l) * kC * K;
+    for (int e = tid; e < kC * K / 8; e += blockDim.x) {
+      const int i = e / (K / 8), d0 = 8 * (e % (K / 8)), t = t0 + i;
+      float q8[8];
+      if (t < p.T) {
+        load8_any(p.q.p, p.q.dt, p.q.off(b, t, h, l, d0), p.q.sd, q8);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) q8[u] = 0.f;
+      }
+      const float sc = mixs[i * L + l] * p.scale;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) dst[i * K + d0 + u] = sc * q8[u];
     }
   }
   if (tid < K) rec[p.rec.eg + tid] = expf(Gs[(kC - 1) * KP + tid]);
@@ -350,8 +393,8 @@ __global__ void __launch_bounds__(256) update_simt_kernel(UpdParams u) {
 // Host launchers
 // ---------------------------------------------------------------------------
 
-size_t prep_simt_smem(int K) {
-  return sizeof(float) * (4 * kC * (K + 1) + 2 * kC * 65 + kGemmSmemFloats);
+size_t prep_simt_smem(int K, int L) {
+  return sizeof(float) * (4 * kC * (K + 1) + 2 * kC * 65 + kGemmSmemFloats + kC * L);
 }
 
 cudaError_t launch_convert_params(const FwdParams& p, cudaStream_t stream) {
@@ -373,7 +416,7 @@ cudaError_t launch_fwd_simt(const FwdParams& p, int stage, cudaStream_t stream) 
   if (stage == 0 || stage == 1) {
     if ((err = launch_convert_params(p, stream)) != cudaSuccess) return err;
     if (p.NT > 0) {
-      const size_t smem = prep_simt_smem(p.K);
+      const size_t smem = prep_simt_smem(p.K, p.L);
       err = cudaFuncSetAttribute(prep_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  int(smem));
       if (err != cudaSuccess) return err;

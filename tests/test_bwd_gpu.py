@@ -112,6 +112,19 @@ def test_initial_state_gradient(promotion):
     _compare(got, ref, BWD_REL)
 
 
+@pytest.mark.parametrize("lift", [0.02, 0.1])
+def test_positive_log_decays(lift):
+    """Log-decays above zero on 8 channels of the second chunk: the local
+    pass takes the clamped per-term sums on those channels and the running
+    products everywhere else (and the checkpointing prep its per-element
+    decay loop for that chunk). All against the float64 oracle."""
+    d, L = _case(1, 256, 2, 64, 64, 2, 16, (1, 2), seed=12)
+    d["g"] = d["g"].copy()
+    d["g"][:, 64:128, :, :8] = lift
+    _, _, ref = oracle_grads(d, L, "learned")
+    _compare(_cuda_grads(d, L, "learned"), ref, BWD_REL)
+
+
 def test_l1_reduces_to_level_zero():
     d, L = _case(1, 192, 2, 64, 32, 1, 16, (1,), seed=6, with_init=True)
     _, _, ref = oracle_grads(d, L, "learned")
