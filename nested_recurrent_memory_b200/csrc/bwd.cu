@@ -180,11 +180,12 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
              [&](int r, int k, float a) { Zg[r * K + k] = a + kGLogitInit; });
   for (int k = tid; k < K; k += nth) {
     float s = 0.f;
+#pragma unroll 8
     for (int r = 0; r < m; ++r) s += -softplusf_(Zg[r * K + k]);
     gv[k] = s / float(m);
   }
   __syncthreads();
-  for (int e = tid; e < K * V; e += nth) Sd[e] = Sold[e] * expf(gv[e / V]);
+  block_map<2>(Sd, Sold, K * V, [&](int e, float x) { return x * expf(gv[e / V]); });
   __syncthreads();
 
   // --- backward of S' = S_d - K^T (K*b) S_d + K^T (V' * w), S_d = e^g S ---
@@ -233,7 +234,7 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
     if (lane == 0) dgv[k] = s;
   }
   __syncthreads();
-  for (int e = tid; e < K * V; e += nth) dSl[e] = expf(gv[e / V]) * dSd[e];
+  block_map<2>(dSl, dSd, K * V, [&](int e, float x) { return expf(gv[e / V]) * x; });
   // Gates: dV' = Z * w; dw -> d(w logit) = Z * V' * w (1 - w) (into Wg);
   // db = d(K*b) * K -> d(b logit) = db * b (1 - b) (into Bg);
   // dK += d(K*b) * b; d(g logit) = -(dg / m) sigmoid(z) (into Zg).
@@ -367,7 +368,7 @@ __global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
                [&](int k, int c) { return dS[k * V + c]; }, gsm,
                [&](int i, int c, float a) { dv[i * V + c] += a; });
     float* dsn = p.dsn + (bh * f.NT + n) * K * V;
-    for (int e = tid; e < K * V; e += blockDim.x) dsn[e] = dS[e];
+    block_map<2>(dsn, dS, K * V, [](int, float x) { return x; });
     __syncthreads();
     // dS0 <- e^(G_last) dS0 + (mix0 scale q e^G)^T dO - W^T dv_new
     block_gemm<true, false>(K, V, 2 * kC,
@@ -481,9 +482,33 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   // 377-378, clamped decays).
   {
     const float* ta = f.ck_ta + (bh * f.NT + n) * 2 * kC * kC;
-    for (int e = tid; e < kC * kC; e += nth) {
-      Ts[(e / kC) * 65 + e % kC] = ta[e];
-      As[(e / kC) * 65 + e % kC] = ta[kC * kC + e];
+    if ((reinterpret_cast<uintptr_t>(ta) & 15) == 0) {
+      // 16-byte loads, four of each block in flight per thread
+      const float4* t4 = reinterpret_cast<const float4*>(ta);
+      constexpr int n4 = kC * kC / 4;
+      for (int base = tid; base < n4; base += 4 * nth) {
+        float4 a[4], c[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int x = base + u * nth;
+          a[u] = x < n4 ? t4[x] : make_float4(0.f, 0.f, 0.f, 0.f);
+          c[u] = x < n4 ? t4[n4 + x] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int x = base + u * nth;
+          if (x < n4) {
+            const int o = (4 * x / kC) * 65 + (4 * x) % kC;
+            Ts[o] = a[u].x; Ts[o + 1] = a[u].y; Ts[o + 2] = a[u].z; Ts[o + 3] = a[u].w;
+            As[o] = c[u].x; As[o + 1] = c[u].y; As[o + 2] = c[u].z; As[o + 3] = c[u].w;
+          }
+        }
+      }
+    } else {
+      for (int e = tid; e < kC * kC; e += nth) {
+        Ts[(e / kC) * 65 + e % kC] = ta[e];
+        As[(e / kC) * 65 + e % kC] = ta[kC * kC + e];
+      }
     }
   }
   __syncthreads();
@@ -496,11 +521,9 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
              },
              [&](int j, int c) { return j < kC ? vn[j * V + c] : S0[(j - kC) * V + c]; }, gsm,
              [&](int i, int c, float a) { dRU[i * V + c] = a * dO(i, c); });
-  for (int i = tid; i < kC; i += nth) {
-    float s = 0.f;
-    for (int c = 0; c < V; ++c) s += dRU[i * V + c];
+  row_sums(dRU, kC, V, [&](int i, float s) {
     if (t0 + i < f.T) p.dmix[(int64_t(b) * f.T + t0 + i) * f.H * f.L + h * f.L] = s;
-  }
+  });
   __syncthreads();
   // dA_qk = (mix_0 dO) v_new^T on the causal triangle; d(q~ e^G) = (mix_0 dO) S0^T
   block_gemm<false, true>(kC, kC + K, V, [&](int i, int c) { return mx[i] * dO(i, c); },
@@ -516,7 +539,7 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
   block_gemm<false, true>(kC, K, V, [&](int i, int c) { return dvn[i * V + c]; },
              [&](int c, int k) { return S0[k * V + c]; }, gsm,
              [&](int i, int k, float a) { dRW[i * K + k] = -a; });
-  for (int e = tid; e < kC * V; e += nth) dRU[e] = dvn[e];
+  block_map(dRU, dvn, kC * V, [](int, float x) { return x; });
   // dG_last from S' = e^(G_last) S0: sum_v S0 dS' e^(G_last); a warp per
   // row, its lanes along the row (coalesced), then a shuffle reduction.
   {
@@ -552,12 +575,19 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
              [&](int c, int j) { return c < V ? Um[j * V + c] : Wm[j * K + c - V]; }, gsm,
              [&](int i, int j, float a) { Dt[i * 65 + j] = j < i ? -a : 0.f; });
   // dv = dR_U w, dw = dR_U v (R_V = w * v, naive.py:346)
-  for (int e = tid; e < kC * V; e += nth) {
-    const int i = e / V, c = e % V, t = t0 + i;
+  for (int e = tid; e < kC * V / 8; e += nth) {
+    const int i = e / (V / 8), c0 = 8 * (e % (V / 8)), t = t0 + i;
     if (t < f.T) {
-      const float d = dRU[e];
-      p.dv[orow(i, V) + c] = d * f.w.at(b, t, h, c);
-      p.dw[orow(i, V) + c] = d * f.v.at(b, t, h, c);
+      float w8[8], v8[8], d8[8];
+      load8_any(f.w.p, f.w.dt, f.w.off(b, t, h, c0), f.w.sd, w8);
+      load8_any(f.v.p, f.v.dt, f.v.off(b, t, h, c0), f.v.sd, v8);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d8[u] = dRU[i * V + c0 + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        p.dv[orow(i, V) + c0 + u] = d8[u] * w8[u];
+        p.dw[orow(i, V) + c0 + u] = d8[u] * v8[u];
+      }
     }
   }
   // Column pass over the decayed blocks: for key j, sums over the rows i.
@@ -682,11 +712,9 @@ __global__ void __launch_bounds__(256) bwd_local_kernel(BwdParams p) {
                [&](int i, int k) { return dRW[i * K + k]; },
                [&](int k, int c) { return Sl[k * V + c]; }, gsm,
                [&](int i, int c, float a) { dRU[i * V + c] = a * dO(i, c); });
-    for (int i = tid; i < kC; i += nth) {
-      float s2 = 0.f;
-      for (int c = 0; c < V; ++c) s2 += dRU[i * V + c];
+    row_sums(dRU, kC, V, [&](int i, float s2) {
       if (t0 + i < f.T) p.dmix[(int64_t(b) * f.T + t0 + i) * f.H * f.L + h * f.L + l] = f.scale * s2;
-    }
+    });
   }
 }
 

@@ -76,6 +76,60 @@ __device__ __forceinline__ float softplusf_(float x) {
 // must be a multiple of 16. ``smem`` holds kGemmSmemFloats floats.
 // ---------------------------------------------------------------------------
 
+// dst[e] = op(e, src[e]) for e < n over the whole block (dst may be src):
+// float4 accesses with U loads in flight per thread when both pointers are
+// 16-byte aligned and n is a multiple of 4, else one element at a time.
+// For global-memory loops, where one dependent load per iteration would
+// cost a full L2 round trip each.
+template <int U = 4, class Op>
+__device__ __forceinline__ void block_map(float* dst, const float* src, int n, Op op) {
+  const int tid = threadIdx.x, nth = blockDim.x;
+  if ((((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0) &&
+      (n & 3) == 0) {
+    const int n4 = n >> 2;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int base = tid; base < n4; base += U * nth) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * nth;
+        v[u] = i < n4 ? s4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * nth;
+        if (i < n4) {
+          float4 r = v[u];
+          r.x = op(4 * i, r.x);
+          r.y = op(4 * i + 1, r.y);
+          r.z = op(4 * i + 2, r.z);
+          r.w = op(4 * i + 3, r.w);
+          d4[i] = r;
+        }
+      }
+    }
+  } else {
+    for (int e = tid; e < n; e += nth) dst[e] = op(e, src[e]);
+  }
+}
+
+// out(r, sum_c X[r * cols + c]) for r < rows: a warp per row, lanes along
+// the row (coalesced), then a shuffle reduction (a fixed order, so the sums
+// are reproducible). Lane 0 calls out.
+template <class Out>
+__device__ __forceinline__ void row_sums(const float* X, int rows, int cols, Out out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+  for (int r = warp; r < rows; r += nwarp) {
+    float s = 0.f;
+#pragma unroll 4
+    for (int c = lane; c < cols; c += 32) s += X[int64_t(r) * cols + c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out(r, s);
+  }
+}
+
 constexpr int kGemmThreads = 256;
 constexpr int kGemmLd = 65;
 constexpr int kGemmSmemFloats = 2 * 16 * kGemmLd;

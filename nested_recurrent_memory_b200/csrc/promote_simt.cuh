@@ -76,6 +76,7 @@ static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, flo
   // g = mean over pairs of -softplus(logit - 4) (probe.py:65)
   for (int k = tid; k < K; k += blockDim.x) {
     float s = 0.f;
+#pragma unroll 8
     for (int r = 0; r < m; ++r) s += -softplusf_(Gl[r * K + k] + kGLogitInit);
     gv[k] = s / float(m);
   }
@@ -92,7 +93,7 @@ static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, flo
     return;
   }
   // S <- e^g S; vn = v*w - (k*b) S; S <- S + k^T vn  (update_fwd.py:120-123)
-  for (int e = tid; e < K * V; e += blockDim.x) Sl[e] *= expf(gv[e / V]);
+  block_map(Sl, Sl, K * V, [&](int e, float x) { return x * expf(gv[e / V]); });
   __syncthreads();
   block_gemm<false, false, PF>(m, V, K, [&](int r, int k) { return Bl[r * K + k]; },
              [&](int k, int c) { return Sl[k * V + c]; }, gsm,

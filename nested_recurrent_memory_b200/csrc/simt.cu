@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(256) scan_simt_kernel(FwdParams p) {
     const float* src = S + int64_t(level) * K * V;
     float* dst = level == 0 ? p.ck0 + (bh * (p.NT + 1) + j) * K * V
                             : p.ck_up + p.ck_up_off[level] + (bh * p.ck_up_n[level] + j) * K * V;
-    for (int e = tid; e < K * V; e += blockDim.x) dst[e] = src[e];
+    block_map(dst, src, K * V, [](int, float x) { return x; });
   };
   for (int n = 0; n < p.NT; ++n) {
     const float* rec = p.chunks + (bh * p.NT + n) * p.rec.size;
