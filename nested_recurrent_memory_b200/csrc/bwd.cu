@@ -106,7 +106,8 @@ __device__ __forceinline__ const float* ck_level(const FwdParams& f, int64_t bh,
 // checkpoints. In: dS_l after the firing. Out: dS_l before it, dS_{l-1}
 // (the source, level l-1 after chunk n) increased by the probe's gradient,
 // and the parameter gradients added into p.dparams.
-__device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, float* gsm) {
+__device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n,
+                                            float* gsm) {
   const FwdParams& f = p.f;
   const int K = f.K, V = f.V, tid = threadIdx.x, nth = blockDim.x;
   const int64_t bh = int64_t(b) * f.H + h;
@@ -152,13 +153,10 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
   // --- the probe, recomputed (as promote_simt) ---
   const float* vals = X;  // merge: the values are the level below (probe.py:133-136)
   if (!merge) {
-    block_gemm(m, V, K, [&](int r, int k) { return qb[r * K + k]; },
-               [&](int k, int c) { return X[k * V + c]; }, gsm,
-               [&](int r, int c, float a) { Vp[r * V + c] = a; });
+    block_gemm_cp(m, V, K, qb, K, X, V, gsm, [&](int r, int c, float a) { Vp[r * V + c] = a; });
     vals = Vp;
-    block_gemm<false, true>(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
-               [&](int v, int k) { return kp[k * V + v]; }, gsm,
-               [&](int r, int k, float a) { Kk[r * K + k] = a; });
+    block_gemm_cp<false, true>(m, K, V, vals, V, kp, V, gsm,
+                               [&](int r, int k, float a) { Kk[r * K + k] = a; });
     for (int r = warp; r < m; r += nwarp) {
       float s = 0.f;
       for (int k = lane; k < K; k += 32) s = fmaf(Kk[r * K + k], Kk[r * K + k], s);
@@ -169,15 +167,16 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
       if (lane == 0) Nr[r] = nrm;
     }
   }
-  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
-             [&](int v, int k) { return bp[v * K + k]; }, gsm,
-             [&](int r, int k, float a) { Bg[r * K + k] = sigmoidf_(a + kBLogitInit); });
-  block_gemm(m, V, V, [&](int r, int v) { return vals[r * V + v]; },
-             [&](int v, int u) { return wp[v * V + u]; }, gsm,
-             [&](int r, int u, float a) { Wg[r * V + u] = sigmoidf_(a + kWLogitInit); });
-  block_gemm(m, K, V, [&](int r, int v) { return vals[r * V + v]; },
-             [&](int v, int k) { return gp[v * K + k]; }, gsm,
-             [&](int r, int k, float a) { Zg[r * K + k] = a + kGLogitInit; });
+  // (learned: k * b goes to the d(K*b) buffer, free until its own product)
+  block_gemm_cp(m, K, V, vals, V, bp, K, gsm, [&](int r, int k, float a) {
+    const float bg = sigmoidf_(a + kBLogitInit);
+    Bg[r * K + k] = bg;
+    if (!merge) dKB[r * K + k] = Kk[r * K + k] * bg;
+  });
+  block_gemm_cp(m, V, V, vals, V, wp, V, gsm,
+                [&](int r, int u, float a) { Wg[r * V + u] = sigmoidf_(a + kWLogitInit); });
+  block_gemm_cp(m, K, V, vals, V, gp, K, gsm,
+                [&](int r, int k, float a) { Zg[r * K + k] = a + kGLogitInit; });
   for (int k = tid; k < K; k += nth) {
     float s = 0.f;
 #pragma unroll 8
@@ -191,23 +190,21 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
   // --- backward of S' = S_d - K^T (K*b) S_d + K^T (V' * w), S_d = e^g S ---
   // Z = K dS', Y = (K*b) S_d  (merge: K = I)
   if (!merge) {
-    block_gemm(m, V, K, [&](int r, int k) { return Kk[r * K + k]; },
-               [&](int k, int c) { return dSl[k * V + c]; }, gsm,
-               [&](int r, int c, float a) { Z[r * V + c] = a; });
-    block_gemm(m, V, K, [&](int r, int k) { return Kk[r * K + k] * Bg[r * K + k]; },
-               [&](int k, int c) { return Sd[k * V + c]; }, gsm,
-               [&](int r, int c, float a) { Y[r * V + c] = a; });
+    const float* KB = dKB;  // K * b, written with the gates above
+    block_gemm_cp(m, V, K, Kk, K, dSl, V, gsm, [&](int r, int c, float a) { Z[r * V + c] = a; });
+    // Y holds V' * w - (K*b) S_d, the left operand of dK
+    block_gemm_cp(m, V, K, KB, K, Sd, V, gsm, [&](int r, int c, float a) {
+      Y[r * V + c] = vals[r * V + c] * Wg[r * V + c] - a;
+    });
+    // dS_d = dS' - (K*b)^T Z  (before d(K*b) overwrites K * b)
+    block_gemm_cp<true, false>(K, V, m, KB, K, Z, V, gsm, [&](int k, int c, float a) {
+      dSd[k * V + c] = dSl[k * V + c] - a;
+    });
     // dK = (V' * w - Y) dS'^T;  d(K*b) = -Z S_d^T
-    block_gemm<false, true>(m, K, V, [&](int r, int c) { return vals[r * V + c] * Wg[r * V + c] - Y[r * V + c]; },
-               [&](int c, int k) { return dSl[k * V + c]; }, gsm,
-               [&](int r, int k, float a) { dKk[r * K + k] = a; });
-    block_gemm<false, true>(m, K, V, [&](int r, int c) { return Z[r * V + c]; },
-               [&](int c, int k) { return Sd[k * V + c]; }, gsm,
-               [&](int r, int k, float a) { dKB[r * K + k] = -a; });
-    // dS_d = dS' - (K*b)^T Z
-    block_gemm<true, false>(K, V, m, [&](int k, int r) { return Kk[r * K + k] * Bg[r * K + k]; },
-               [&](int r, int c) { return Z[r * V + c]; }, gsm,
-               [&](int k, int c, float a) { dSd[k * V + c] = dSl[k * V + c] - a; });
+    block_gemm_cp<false, true>(m, K, V, Y, V, dSl, V, gsm,
+                               [&](int r, int k, float a) { dKk[r * K + k] = a; });
+    block_gemm_cp<false, true>(m, K, V, Z, V, Sd, V, gsm,
+                               [&](int r, int k, float a) { dKB[r * K + k] = -a; });
   } else {
     for (int e = tid; e < K * V; e += nth) {
       const int k = e / V;
@@ -257,25 +254,18 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
     Zg[e] = -(dgv[k] / float(m)) * sigmoidf_(Zg[e]);
   }
   __syncthreads();
-  // dV' += d(g logit) W_g^T + d(w logit) W_w^T + d(b logit) W_b^T
-  block_gemm<false, true>(m, V, 2 * K + V,
-             [&](int r, int j) {
-               return j < K ? Zg[r * K + j] : j < 2 * K ? Bg[r * K + j - K] : Wg[r * V + j - 2 * K];
-             },
-             [&](int j, int v) {
-               return j < K ? gp[v * K + j] : j < 2 * K ? bp[v * K + j - K] : wp[v * V + j - 2 * K];
-             },
-             gsm, [&](int r, int v, float a) { dVp[r * V + v] += a; });
+  // dV' += d(g logit) W_g^T + d(b logit) W_b^T + d(w logit) W_w^T
+  auto add_dvp = [&](int r, int v, float a) { dVp[r * V + v] += a; };
+  block_gemm_cp<false, true>(m, V, K, Zg, K, gp, K, gsm, add_dvp);
+  block_gemm_cp<false, true>(m, V, K, Bg, K, bp, K, gsm, add_dvp);
+  block_gemm_cp<false, true>(m, V, V, Wg, V, wp, V, gsm, add_dvp);
   // parameter gradients of the gates: V'^T d(logit)
-  block_gemm<true, false>(V, 2 * K + V, m, [&](int v, int r) { return vals[r * V + v]; },
-             [&](int r, int j) {
-               return j < K ? Zg[r * K + j] : j < 2 * K ? Bg[r * K + j - K] : Wg[r * V + j - 2 * K];
-             },
-             gsm, [&](int v, int j, float a) {
-               if (j < K) dgp[v * K + j] += a;
-               else if (j < 2 * K) dbp[v * K + j - K] += a;
-               else dwp[v * V + j - 2 * K] += a;
-             });
+  block_gemm_cp<true, false>(V, K, m, vals, V, Zg, K, gsm,
+                             [&](int v, int j, float a) { dgp[v * K + j] += a; });
+  block_gemm_cp<true, false>(V, K, m, vals, V, Bg, K, gsm,
+                             [&](int v, int j, float a) { dbp[v * K + j] += a; });
+  block_gemm_cp<true, false>(V, V, m, vals, V, Wg, V, gsm,
+                             [&](int v, int j, float a) { dwp[v * V + j] += a; });
   if (merge) {
     for (int e = tid; e < K * V; e += nth) dSb[e] += dVp[e];
     __syncthreads();
@@ -295,27 +285,22 @@ __device__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n, floa
   }
   __syncthreads();
   // dV' += du W_k; dW_k += du^T V'
-  block_gemm(m, V, K, [&](int r, int k) { return dKk[r * K + k]; },
-             [&](int k, int v) { return kp[k * V + v]; }, gsm,
-             [&](int r, int v, float a) { dVp[r * V + v] += a; });
-  block_gemm<true, false>(K, V, m, [&](int k, int r) { return dKk[r * K + k]; },
-             [&](int r, int v) { return vals[r * V + v]; }, gsm,
-             [&](int k, int v, float a) { dkp[k * V + v] += a; });
+  block_gemm_cp(m, V, K, dKk, K, kp, V, gsm, add_dvp);
+  block_gemm_cp<true, false>(K, V, m, dKk, K, vals, V, gsm,
+                             [&](int k, int v, float a) { dkp[k * V + v] += a; });
   // V' = Q_bank X: dQ_bank += dV' X^T; dX = Q_bank^T dV'
-  block_gemm<false, true>(m, K, V, [&](int r, int v) { return dVp[r * V + v]; },
-             [&](int v, int k) { return X[k * V + v]; }, gsm,
-             [&](int r, int k, float a) { dqb[r * K + k] += a; });
-  block_gemm<true, false>(K, V, m, [&](int k, int r) { return qb[r * K + k]; },
-             [&](int r, int v) { return dVp[r * V + v]; }, gsm,
-             [&](int k, int v, float a) { dSb[k * V + v] += a; });
+  block_gemm_cp<false, true>(m, K, V, dVp, V, X, V, gsm,
+                             [&](int r, int k, float a) { dqb[r * K + k] += a; });
+  block_gemm_cp<true, false>(K, V, m, qb, K, dVp, V, gsm,
+                             [&](int k, int v, float a) { dSb[k * V + v] += a; });
 }
 
 // ---------------------------------------------------------------------------
 // bwd_scan: grid (H, B), 256 threads; chunks in reverse.
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
-  __shared__ float gsm[kGemmSmemFloats];
+__global__ void __launch_bounds__(256, 1) bwd_scan_kernel(BwdParams p) {
+  __shared__ float gsm[kGemmCpSmemFloats];
   const FwdParams& f = p.f;
   const int h = blockIdx.x, b = blockIdx.y, K = f.K, V = f.V, L = f.L, tid = threadIdx.x;
   const int64_t bh = int64_t(b) * f.H + h;
@@ -354,27 +339,24 @@ __global__ void __launch_bounds__(256) bwd_scan_kernel(BwdParams p) {
     for (int l = 1; l < L; ++l) {
       const float* Ql = rec + f.rec.Q + int64_t(l) * kC * K;
       float* dSl = dS + int64_t(l) * K * V;
-      block_gemm<true, false>(K, V, kC, [&](int k, int i) { return Ql[i * K + k]; },
-                 [&](int i, int c) { return dOs[i * V + c]; }, gsm,
-                 [&](int k, int c, float a) { dSl[k * V + c] += a; });
+      block_gemm_cp<true, false>(K, V, kC, Ql, K, dOs, V, gsm,
+                                 [&](int k, int c, float a) { dSl[k * V + c] += a; });
     }
     // Level 0: dv_new = (mix0 scale A_qk)^T dO + Kt dS0 (the S0 entering the
     // next chunk, naive.py:392), kept for the local pass with dS0 itself.
     float* dv = p.dvn + (bh * f.NT + n) * kC * V;
-    block_gemm<true, false>(kC, V, kC, [&](int i, int j) { return Am[j * kC + i]; },
-                            [&](int j, int c) { return dOs[j * V + c]; }, gsm,
-                            [&](int i, int c, float a) { dv[i * V + c] = a; });
-    block_gemm(kC, V, K, [&](int i, int k) { return Kt[i * K + k]; },
-               [&](int k, int c) { return dS[k * V + c]; }, gsm,
-               [&](int i, int c, float a) { dv[i * V + c] += a; });
+    block_gemm_cp<true, false>(kC, V, kC, Am, kC, dOs, V, gsm,
+                               [&](int i, int c, float a) { dv[i * V + c] = a; });
+    block_gemm_cp(kC, V, K, Kt, K, dS, V, gsm, [&](int i, int c, float a) { dv[i * V + c] += a; });
     float* dsn = p.dsn + (bh * f.NT + n) * K * V;
     block_map<2>(dsn, dS, K * V, [](int, float x) { return x; });
     __syncthreads();
     // dS0 <- e^(G_last) dS0 + (mix0 scale q e^G)^T dO - W^T dv_new
-    block_gemm<true, false>(K, V, 2 * kC,
-               [&](int k, int i) { return i < kC ? Q0[i * K + k] : -Wm[(i - kC) * K + k]; },
-               [&](int i, int c) { return i < kC ? dOs[i * V + c] : dv[(i - kC) * V + c]; },
-               gsm, [&](int k, int c, float a) { dS[k * V + c] = eg[k] * dS[k * V + c] + a; });
+    block_gemm_cp<true, false>(K, V, kC, Q0, K, dOs, V, gsm, [&](int k, int c, float a) {
+      dS[k * V + c] = eg[k] * dS[k * V + c] + a;
+    });
+    block_gemm_cp<true, false>(K, V, kC, Wm, K, dv, V, gsm,
+                               [&](int k, int c, float a) { dS[k * V + c] -= a; });
   }
   if (p.dinit)
     for (int64_t e = tid; e < int64_t(L) * K * V; e += blockDim.x) p.dinit[bh * L * K * V + e] = dS[e];
