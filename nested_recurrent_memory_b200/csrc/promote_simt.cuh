@@ -1,5 +1,5 @@
 // Promotion of one level into the next on CUDA cores, fp32 (shared by the
-// CUDA-core scan and the tensor-core scan, which runs its promotions here).
+// CUDA-core scan and the decode step's promotion kernel).
 #pragma once
 
 #include "fwd_params.cuh"
@@ -7,8 +7,7 @@
 namespace ngdn2 {
 
 // Promote level l-1 into level l for one (b, h): probe then update. PF is
-// block_gemm's prefetch switch (off inside the register-capped tensor-core
-// scan).
+// block_gemm's prefetch switch (for a caller at its register cap).
 template <bool PF = true>
 static __device__ void promote_simt(const FwdParams& p, int b, int h, int l, float* S, float* sc,
                              float* gsm) {
