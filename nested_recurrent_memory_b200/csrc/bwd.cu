@@ -30,6 +30,7 @@
 
 #include "fwd_params.cuh"
 #include "promote_simt.cuh"
+#include "tc_gemm3.cuh"
 
 namespace ngdn2 {
 
@@ -301,13 +302,29 @@ __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, in
 
 __global__ void __launch_bounds__(256, 1) bwd_scan_kernel(BwdParams p) {
   __shared__ float gsm[kGemmCpSmemFloats];
+  __shared__ uint64_t tc_bar;
+  __shared__ uint32_t tc_base;
+  __shared__ int tc_abort;
+  extern __shared__ uint8_t dyn_smem[];
   const FwdParams& f = p.f;
   const int h = blockIdx.x, b = blockIdx.y, K = f.K, V = f.V, L = f.L, tid = threadIdx.x;
   const int64_t bh = int64_t(b) * f.H + h;
+  // Tensor-core products (tc::tc_gemm3): TMEM accumulator, MMA barrier, staging.
+  if ((tid >> 5) == 0) tc::tmem_alloc(&tc_base, tc::kTc3TmemCols);
+  if (tid == 0) {
+    tc::mbar_init(&tc_bar, 1);
+    tc::fence_mbar_init();
+    tc_abort = 0;
+  }
   float* dS = p.dS + bh * L * K * V;
   for (int64_t e = tid; e < int64_t(L) * K * V; e += blockDim.x)
     dS[e] = p.d_final ? p.d_final[bh * L * K * V + e] : 0.f;
+  tc::fence_before_sync();
   __syncthreads();
+  tc::fence_after_sync();
+  tc::Tc3Ctx tcx{tc_base, &tc_bar, 0u,
+            reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023)),
+            &tc_abort};
   for (int n = f.NT - 1; n >= 0; --n) {
     const float* rec = f.chunks + (bh * f.NT + n) * f.rec.size;
     const float* Am = rec + f.rec.A;   // mix0 scale A_qk
@@ -339,27 +356,36 @@ __global__ void __launch_bounds__(256, 1) bwd_scan_kernel(BwdParams p) {
     for (int l = 1; l < L; ++l) {
       const float* Ql = rec + f.rec.Q + int64_t(l) * kC * K;
       float* dSl = dS + int64_t(l) * K * V;
-      block_gemm_cp<true, false>(K, V, kC, Ql, K, dOs, V, gsm,
-                                 [&](int k, int c, float a) { dSl[k * V + c] += a; });
+      tc::tc_gemm3<true, false>(
+          tcx, K, V, kC, Ql, K, dOs, V, [&](int k, int c) { return dSl[k * V + c]; },
+          [&](int k, int c, float a, float old) { dSl[k * V + c] = old + a; });
     }
     // Level 0: dv_new = (mix0 scale A_qk)^T dO + Kt dS0 (the S0 entering the
     // next chunk, naive.py:392), kept for the local pass with dS0 itself.
     float* dv = p.dvn + (bh * f.NT + n) * kC * V;
-    block_gemm_cp<true, false>(kC, V, kC, Am, kC, dOs, V, gsm,
-                               [&](int i, int c, float a) { dv[i * V + c] = a; });
-    block_gemm_cp(kC, V, K, Kt, K, dS, V, gsm, [&](int i, int c, float a) { dv[i * V + c] += a; });
+    tc::tc_gemm3<true, false>(
+        tcx, kC, V, kC, Am, kC, dOs, V, [](int, int) { return 0.f; },
+        [&](int i, int c, float a, float) { dv[i * V + c] = a; });
+    tc::tc_gemm3(
+        tcx, kC, V, K, Kt, K, dS, V, [&](int i, int c) { return dv[i * V + c]; },
+        [&](int i, int c, float a, float old) { dv[i * V + c] = old + a; });
     float* dsn = p.dsn + (bh * f.NT + n) * K * V;
     block_map<2>(dsn, dS, K * V, [](int, float x) { return x; });
     __syncthreads();
     // dS0 <- e^(G_last) dS0 + (mix0 scale q e^G)^T dO - W^T dv_new
-    block_gemm_cp<true, false>(K, V, kC, Q0, K, dOs, V, gsm, [&](int k, int c, float a) {
-      dS[k * V + c] = eg[k] * dS[k * V + c] + a;
-    });
-    block_gemm_cp<true, false>(K, V, kC, Wm, K, dv, V, gsm,
-                               [&](int k, int c, float a) { dS[k * V + c] -= a; });
+    tc::tc_gemm3<true, false>(
+        tcx, K, V, kC, Q0, K, dOs, V, [&](int k, int c) { return dS[k * V + c]; },
+        [&](int k, int c, float a, float old) { dS[k * V + c] = eg[k] * old + a; });
+    tc::tc_gemm3<true, false>(
+        tcx, K, V, kC, Wm, K, dv, V, [&](int k, int c) { return dS[k * V + c]; },
+        [&](int k, int c, float a, float old) { dS[k * V + c] = old - a; });
   }
   if (p.dinit)
     for (int64_t e = tid; e < int64_t(L) * K * V; e += blockDim.x) p.dinit[bh * L * K * V + e] = dS[e];
+  if (tid == 0 && tc_abort && f.status) atomicOr(f.status, NGDN2_STATUS_WAIT_TIMEOUT);
+  tc::fence_before_sync();
+  __syncthreads();
+  if ((tid >> 5) == 0) tc::tmem_dealloc(tc_base, tc::kTc3TmemCols);
 }
 
 // ---------------------------------------------------------------------------
@@ -797,7 +823,12 @@ cudaError_t launch_bwd(BwdParams bp, float* ws, float* const dparam_out[5], cuda
     err = cudaMemsetAsync(bp.dparams, 0, sizeof(float) * f.B * f.pl.size, stream);
     if (err != cudaSuccess) return err;
   }
-  bwd_scan_kernel<<<dim3(f.H, f.B), 256, 0, stream>>>(bp);
+  {
+    const int dyn = tc::kTc3StageBytes + 1024;  // staging of the tensor-core products, 1 KB aligned
+    err = cudaFuncSetAttribute(bwd_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+    if (err != cudaSuccess) return err;
+    bwd_scan_kernel<<<dim3(f.H, f.B), 256, dyn, stream>>>(bp);
+  }
   if ((err = cudaGetLastError()) != cudaSuccess) return err;
   if (f.NT > 0) {
     const size_t smem = bwd_local_smem(f.K);
