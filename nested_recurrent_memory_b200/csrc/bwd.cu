@@ -108,7 +108,7 @@ __device__ __forceinline__ const float* ck_level(const FwdParams& f, int64_t bh,
 // (the source, level l-1 after chunk n) increased by the probe's gradient,
 // and the parameter gradients added into p.dparams.
 __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, int l, int n,
-                                            float* gsm) {
+                                            tc::Tc3Ctx& tcx) {
   const FwdParams& f = p.f;
   const int K = f.K, V = f.V, tid = threadIdx.x, nth = blockDim.x;
   const int64_t bh = int64_t(b) * f.H + h;
@@ -154,10 +154,11 @@ __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, in
   // --- the probe, recomputed (as promote_simt) ---
   const float* vals = X;  // merge: the values are the level below (probe.py:133-136)
   if (!merge) {
-    block_gemm_cp(m, V, K, qb, K, X, V, gsm, [&](int r, int c, float a) { Vp[r * V + c] = a; });
+    tc::tc_gemm3(tcx, m, V, K, qb, K, X, V, [](int, int) { return 0.f; },
+                 [&](int r, int c, float a, float) { Vp[r * V + c] = a; });
     vals = Vp;
-    block_gemm_cp<false, true>(m, K, V, vals, V, kp, V, gsm,
-                               [&](int r, int k, float a) { Kk[r * K + k] = a; });
+    tc::tc_gemm3<false, true>(tcx, m, K, V, vals, V, kp, V, [](int, int) { return 0.f; },
+                              [&](int r, int k, float a, float) { Kk[r * K + k] = a; });
     for (int r = warp; r < m; r += nwarp) {
       float s = 0.f;
       for (int k = lane; k < K; k += 32) s = fmaf(Kk[r * K + k], Kk[r * K + k], s);
@@ -169,15 +170,15 @@ __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, in
     }
   }
   // (learned: k * b goes to the d(K*b) buffer, free until its own product)
-  block_gemm_cp(m, K, V, vals, V, bp, K, gsm, [&](int r, int k, float a) {
+  tc::tc_gemm3(tcx, m, K, V, vals, V, bp, K, [](int, int) { return 0.f; }, [&](int r, int k, float a, float) {
     const float bg = sigmoidf_(a + kBLogitInit);
     Bg[r * K + k] = bg;
     if (!merge) dKB[r * K + k] = Kk[r * K + k] * bg;
   });
-  block_gemm_cp(m, V, V, vals, V, wp, V, gsm,
-                [&](int r, int u, float a) { Wg[r * V + u] = sigmoidf_(a + kWLogitInit); });
-  block_gemm_cp(m, K, V, vals, V, gp, K, gsm,
-                [&](int r, int k, float a) { Zg[r * K + k] = a + kGLogitInit; });
+  tc::tc_gemm3(tcx, m, V, V, vals, V, wp, V, [](int, int) { return 0.f; },
+               [&](int r, int u, float a, float) { Wg[r * V + u] = sigmoidf_(a + kWLogitInit); });
+  tc::tc_gemm3(tcx, m, K, V, vals, V, gp, K, [](int, int) { return 0.f; },
+               [&](int r, int k, float a, float) { Zg[r * K + k] = a + kGLogitInit; });
   for (int k = tid; k < K; k += nth) {
     float s = 0.f;
 #pragma unroll 8
@@ -192,20 +193,21 @@ __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, in
   // Z = K dS', Y = (K*b) S_d  (merge: K = I)
   if (!merge) {
     const float* KB = dKB;  // K * b, written with the gates above
-    block_gemm_cp(m, V, K, Kk, K, dSl, V, gsm, [&](int r, int c, float a) { Z[r * V + c] = a; });
+    tc::tc_gemm3(tcx, m, V, K, Kk, K, dSl, V, [](int, int) { return 0.f; },
+                 [&](int r, int c, float a, float) { Z[r * V + c] = a; });
     // Y holds V' * w - (K*b) S_d, the left operand of dK
-    block_gemm_cp(m, V, K, KB, K, Sd, V, gsm, [&](int r, int c, float a) {
+    tc::tc_gemm3(tcx, m, V, K, KB, K, Sd, V, [](int, int) { return 0.f; }, [&](int r, int c, float a, float) {
       Y[r * V + c] = vals[r * V + c] * Wg[r * V + c] - a;
     });
     // dS_d = dS' - (K*b)^T Z  (before d(K*b) overwrites K * b)
-    block_gemm_cp<true, false>(K, V, m, KB, K, Z, V, gsm, [&](int k, int c, float a) {
-      dSd[k * V + c] = dSl[k * V + c] - a;
-    });
+    tc::tc_gemm3<true, false>(
+        tcx, K, V, m, KB, K, Z, V, [&](int k, int c) { return dSl[k * V + c]; },
+        [&](int k, int c, float a, float old) { dSd[k * V + c] = old - a; });
     // dK = (V' * w - Y) dS'^T;  d(K*b) = -Z S_d^T
-    block_gemm_cp<false, true>(m, K, V, Y, V, dSl, V, gsm,
-                               [&](int r, int k, float a) { dKk[r * K + k] = a; });
-    block_gemm_cp<false, true>(m, K, V, Z, V, Sd, V, gsm,
-                               [&](int r, int k, float a) { dKB[r * K + k] = -a; });
+    tc::tc_gemm3<false, true>(tcx, m, K, V, Y, V, dSl, V, [](int, int) { return 0.f; },
+                              [&](int r, int k, float a, float) { dKk[r * K + k] = a; });
+    tc::tc_gemm3<false, true>(tcx, m, K, V, Z, V, Sd, V, [](int, int) { return 0.f; },
+                              [&](int r, int k, float a, float) { dKB[r * K + k] = -a; });
   } else {
     for (int e = tid; e < K * V; e += nth) {
       const int k = e / V;
@@ -256,17 +258,21 @@ __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, in
   }
   __syncthreads();
   // dV' += d(g logit) W_g^T + d(b logit) W_b^T + d(w logit) W_w^T
-  auto add_dvp = [&](int r, int v, float a) { dVp[r * V + v] += a; };
-  block_gemm_cp<false, true>(m, V, K, Zg, K, gp, K, gsm, add_dvp);
-  block_gemm_cp<false, true>(m, V, K, Bg, K, bp, K, gsm, add_dvp);
-  block_gemm_cp<false, true>(m, V, V, Wg, V, wp, V, gsm, add_dvp);
+  auto ld_dvp = [&](int r, int v) { return dVp[r * V + v]; };
+  auto add_dvp = [&](int r, int v, float a, float old) { dVp[r * V + v] = old + a; };
+  tc::tc_gemm3<false, true>(tcx, m, V, K, Zg, K, gp, K, ld_dvp, add_dvp);
+  tc::tc_gemm3<false, true>(tcx, m, V, K, Bg, K, bp, K, ld_dvp, add_dvp);
+  tc::tc_gemm3<false, true>(tcx, m, V, V, Wg, V, wp, V, ld_dvp, add_dvp);
   // parameter gradients of the gates: V'^T d(logit)
-  block_gemm_cp<true, false>(V, K, m, vals, V, Zg, K, gsm,
-                             [&](int v, int j, float a) { dgp[v * K + j] += a; });
-  block_gemm_cp<true, false>(V, K, m, vals, V, Bg, K, gsm,
-                             [&](int v, int j, float a) { dbp[v * K + j] += a; });
-  block_gemm_cp<true, false>(V, V, m, vals, V, Wg, V, gsm,
-                             [&](int v, int j, float a) { dwp[v * V + j] += a; });
+  tc::tc_gemm3<true, false>(
+      tcx, V, K, m, vals, V, Zg, K, [&](int v, int j) { return dgp[v * K + j]; },
+      [&](int v, int j, float a, float old) { dgp[v * K + j] = old + a; });
+  tc::tc_gemm3<true, false>(
+      tcx, V, K, m, vals, V, Bg, K, [&](int v, int j) { return dbp[v * K + j]; },
+      [&](int v, int j, float a, float old) { dbp[v * K + j] = old + a; });
+  tc::tc_gemm3<true, false>(
+      tcx, V, V, m, vals, V, Wg, V, [&](int v, int j) { return dwp[v * V + j]; },
+      [&](int v, int j, float a, float old) { dwp[v * V + j] = old + a; });
   if (merge) {
     for (int e = tid; e < K * V; e += nth) dSb[e] += dVp[e];
     __syncthreads();
@@ -286,14 +292,17 @@ __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, in
   }
   __syncthreads();
   // dV' += du W_k; dW_k += du^T V'
-  block_gemm_cp(m, V, K, dKk, K, kp, V, gsm, add_dvp);
-  block_gemm_cp<true, false>(K, V, m, dKk, K, vals, V, gsm,
-                             [&](int k, int v, float a) { dkp[k * V + v] += a; });
+  tc::tc_gemm3(tcx, m, V, K, dKk, K, kp, V, ld_dvp, add_dvp);
+  tc::tc_gemm3<true, false>(
+      tcx, K, V, m, dKk, K, vals, V, [&](int k, int v) { return dkp[k * V + v]; },
+      [&](int k, int v, float a, float old) { dkp[k * V + v] = old + a; });
   // V' = Q_bank X: dQ_bank += dV' X^T; dX = Q_bank^T dV'
-  block_gemm_cp<false, true>(m, K, V, dVp, V, X, V, gsm,
-                             [&](int r, int k, float a) { dqb[r * K + k] += a; });
-  block_gemm_cp<true, false>(K, V, m, qb, K, dVp, V, gsm,
-                             [&](int k, int v, float a) { dSb[k * V + v] += a; });
+  tc::tc_gemm3<false, true>(
+      tcx, m, K, V, dVp, V, X, V, [&](int r, int k) { return dqb[r * K + k]; },
+      [&](int r, int k, float a, float old) { dqb[r * K + k] = old + a; });
+  tc::tc_gemm3<true, false>(
+      tcx, K, V, m, qb, K, dVp, V, [&](int k, int v) { return dSb[k * V + v]; },
+      [&](int k, int v, float a, float old) { dSb[k * V + v] = old + a; });
 }
 
 // ---------------------------------------------------------------------------
@@ -301,7 +310,6 @@ __device__ __forceinline__ void promote_bwd(const BwdParams& p, int b, int h, in
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(256, 1) bwd_scan_kernel(BwdParams p) {
-  __shared__ float gsm[kGemmCpSmemFloats];
   __shared__ uint64_t tc_bar;
   __shared__ uint32_t tc_base;
   __shared__ int tc_abort;
@@ -351,7 +359,7 @@ __global__ void __launch_bounds__(256, 1) bwd_scan_kernel(BwdParams p) {
     __syncthreads();
     // The firings after this chunk, top level first (naive.py:394-415 reversed).
     for (int l = L - 1; l >= 1; --l)
-      if ((n + 1) % f.firing[l] == 0) promote_bwd(p, b, h, l, n, gsm);
+      if ((n + 1) % f.firing[l] == 0) promote_bwd(p, b, h, l, n, tcx);
     // Upper-level reads (naive.py:382-385): dS_l += (mix_l scale q_l)^T dO.
     for (int l = 1; l < L; ++l) {
       const float* Ql = rec + f.rec.Q + int64_t(l) * kC * K;
