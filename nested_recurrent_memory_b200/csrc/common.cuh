@@ -238,143 +238,4 @@ __device__ void block_gemm(int M, int N, int Kd, LA la, LB lb, float* smem, Epi 
   }
 }
 
-// ---------------------------------------------------------------------------
-// block_gemm_cp: the same product as block_gemm for operands that are plain
-// strided arrays in global memory, staged into shared memory by cp.async
-// (4-byte copies, zero-filled past M / N) through 3-4 buffers. The copies
-// for the next k-steps are in flight while a step is multiplied, across
-// output-tile boundaries, and need no registers. Output tiles are 64 x 128
-// (4 x 8 outputs a thread at a stride of 16) when N > 64, else 64 x 64.
-// A(m, k) is A[m * lda + k] (AT: A[k * lda + m]); B(k, n) is B[k * ldb + n]
-// (BT: B[n * ldb + k]). The epilogue runs as each output tile completes,
-// while later copies are in flight, so it must not write what A or B read.
-// smem holds kGemmCpSmemFloats floats; Kd must be a multiple of 16; every
-// thread of the block must call it.
-// ---------------------------------------------------------------------------
-
-constexpr int kCpStages = 4;
-// The 64 x 128 variant (4 x 8 outputs a thread) keeps three stages.
-constexpr int kCpStagesWide = 3;
-constexpr int kGemmLdWide = 129;
-constexpr int kGemmCpSmemFloats =
-    kCpStages * 2 * 16 * kGemmLd > kCpStagesWide * 16 * (kGemmLd + kGemmLdWide)
-        ? kCpStages * 2 * 16 * kGemmLd
-        : kCpStagesWide * 16 * (kGemmLd + kGemmLdWide);
-
-__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gsrc, bool valid) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(gsrc),
-               "r"(valid ? 4 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
-// Stage g of block_gemm_cp (TN columns a thread: 64 x 16 TN tiles): the
-// cp.async copies of its A and B tiles, then a commit (by every thread,
-// every call, so the group counts stay uniform).
-template <bool AT, bool BT, int TN>
-__device__ __forceinline__ void gemm_cp_issue(int g, int total, int nk, int ntn, int M, int N,
-                                              const float* A, int64_t lda, const float* B,
-                                              int64_t ldb, float* smem) {
-  constexpr int NW = 16 * TN, LDB = NW + 1, ST = TN == 4 ? kCpStages : kCpStagesWide;
-  const int tid = threadIdx.x;
-  if (g < total && tid < kGemmThreads) {
-    const int tile = g / nk, k0 = (g % nk) * 16;
-    const int m0 = (tile / ntn) * 64, n0 = (tile % ntn) * NW;
-    float* As = smem + (g % ST) * (16 * (kGemmLd + LDB));
-    float* Bs = As + 16 * kGemmLd;
-#pragma unroll
-    for (int q = 0; q < 64 * 16 / kGemmThreads; ++q) {
-      const int e = tid + q * kGemmThreads;
-      const int mm = AT ? e % 64 : e / 16, ka = AT ? e / 64 : e % 16;
-      const bool va = m0 + mm < M;
-      const float* sa = AT ? A + int64_t(k0 + ka) * lda + (m0 + mm)
-                           : A + int64_t(m0 + mm) * lda + (k0 + ka);
-      cp_async4(As + ka * kGemmLd + mm, va ? sa : A, va);
-    }
-#pragma unroll
-    for (int q = 0; q < NW * 16 / kGemmThreads; ++q) {
-      const int e = tid + q * kGemmThreads;
-      const int kb = BT ? e % 16 : e / NW, nn = BT ? e / 16 : e % NW;
-      const bool vb = n0 + nn < N;
-      const float* sb = BT ? B + int64_t(n0 + nn) * ldb + (k0 + kb)
-                           : B + int64_t(k0 + kb) * ldb + (n0 + nn);
-      cp_async4(Bs + kb * LDB + nn, vb ? sb : B, vb);
-    }
-  }
-  cp_async_commit();
-}
-
-template <bool AT, bool BT, int TN, class Epi>
-__device__ __forceinline__ void block_gemm_cp_t(int M, int N, int Kd, const float* A, int64_t lda,
-                                                const float* B, int64_t ldb, float* smem, Epi epi) {
-  constexpr int NW = 16 * TN, LDB = NW + 1, ST = TN == 4 ? kCpStages : kCpStagesWide;
-  constexpr int kStage = 16 * (kGemmLd + LDB);
-  const int tid = threadIdx.x;
-  const bool act = tid < kGemmThreads;
-  const int tm = tid / 16, tn = tid % 16;
-  const int ntn = (N + NW - 1) / NW, nk = Kd / 16;
-  const int total = ((M + 63) / 64) * ntn * nk;
-#pragma unroll
-  for (int st = 0; st < ST - 1; ++st)
-    gemm_cp_issue<AT, BT, TN>(st, total, nk, ntn, M, N, A, lda, B, ldb, smem);
-  const int ntiles = total / nk;
-  int g = 0;
-  for (int tile = 0; tile < ntiles; ++tile) {
-    float acc[4][TN];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
-    for (int kt = 0; kt < nk; ++kt, ++g) {
-      cp_async_wait<ST - 2>();
-      __syncthreads();  // stage g landed for every thread; stage g - 1 is consumed
-      gemm_cp_issue<AT, BT, TN>(g + ST - 1, total, nk, ntn, M, N, A, lda, B, ldb, smem);
-      if (act) {
-        const float* As = smem + (g % ST) * kStage;
-        const float* Bs = As + 16 * kGemmLd;
-#pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
-          float a[4], bb[TN];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) a[i] = As[kk * kGemmLd + tm + 16 * i];
-#pragma unroll
-          for (int j = 0; j < TN; ++j) bb[j] = Bs[kk * LDB + tn + 16 * j];
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
-        }
-      }
-    }
-    if (act) {
-      const int m0 = (tile / ntn) * 64, n0 = (tile % ntn) * NW;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < TN; ++j) {
-          const int gm = m0 + tm + 16 * i, gn = n0 + tn + 16 * j;
-          if (gm < M && gn < N) epi(gm, gn, acc[i][j]);
-        }
-    }
-  }
-  cp_async_wait<0>();
-  __syncthreads();
-}
-
-// Products with N > 64 take 64 x 128 tiles (4 x 8 outputs a thread, twice
-// the multiply-adds per shared-memory read), others 64 x 64.
-template <bool AT = false, bool BT = false, class Epi>
-__device__ __forceinline__ void block_gemm_cp(int M, int N, int Kd, const float* A, int64_t lda,
-                                              const float* B, int64_t ldb, float* smem, Epi epi) {
-  if (N > 64) block_gemm_cp_t<AT, BT, 8>(M, N, Kd, A, lda, B, ldb, smem, epi);
-  else block_gemm_cp_t<AT, BT, 4>(M, N, Kd, A, lda, B, ldb, smem, epi);
-}
-
 }  // namespace ngdn2
